@@ -1,0 +1,381 @@
+"""Benchmark of the B200 DC-attention forward (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload config1|config2|config3|config4] [--G g] [--window w]
+
+A step is one fused DC-attention forward over one batch of the workload (the
+metric of the reference: µs/call and effective TFLOP/s).  ``value`` is the
+whole-job TFLOP/s (algorithmic FLOPs of every rank / max-over-ranks device
+time), inputs resident in HBM (2.2 GB at the default workload: larger than
+L2, so no flush is needed).  ``e2e`` is the same metric through the public
+API with pinned host buffers copied in and the output copied back inside the
+timed region.  ``--impl reference`` times the CPU restatement of the
+reference algorithm (oracle/dc_oracle_torch.py, fp32, all host threads) on a
+bounded sample of the same workload; under torchrun only rank 0 runs it.
+
+Workloads (synthetic, seeded, BASELINE distributions):
+  config1  B16 T4096 H32 D128 window 128, R1 (G sweep via --G, default 1)
+  config2  B16 T4096 H32 D128 window 256, R2 (--G in {1,4,32})
+  config3  B4  T4096 H32 D128 full causal, G4, R2
+  config4  B64 T8192 H32 D128 window 256, G1, R2, batch split over the ranks
+Multi-GPU: configs 1-3 give every rank the full workload (weak scaling);
+config4 splits its batch (strong scaling).  No collective touches the data
+path: the op has no cross-batch dependency.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+WORKLOADS = {
+    "config1": dict(B=16, T=4096, H=32, D=128, window=128, G=1, R=1),
+    "config2": dict(B=16, T=4096, H=32, D=128, window=256, G=1, R=2),
+    "config3": dict(B=4, T=4096, H=32, D=128, window=None, G=4, R=2),
+    "config4": dict(B=64, T=8192, H=32, D=128, window=256, G=1, R=2),
+}
+FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
+
+
+def pairs(T, W):
+    if W is None or W >= T:
+        return T * (T + 1) // 2
+    return T * W - W * (W - 1) // 2
+
+
+def pairs_range(t0, t1, W):
+    return sum(t + 1 if (W is None or t + 1 < W) else W for t in range(t0, t1))
+
+
+def flops(B, H, D, G, R, npairs):
+    """Algorithmic FLOPs: QK^T + PV, plus pre+post composition (static mix 2*HPG,
+    query- and key-wise rank-R aggregate+apply 8R, qdd/kdd 4) per (b,h,t,s)."""
+    hpg = H // G
+    return 4 * D * H * B * npairs + 2 * (2 * hpg + 8 * R + 4) * H * B * npairs
+
+
+def algo_bytes(B, T, H, D, R, esize=2):
+    """q,k,v read once + out written once, plus the two sets of per-token
+    weights (qw1, qw2, kw1, kw2: R each; qdd, kdd)."""
+    return 4 * B * T * H * D * esize + 2 * (4 * R + 2) * B * T * H * esize
+
+
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            m = json.load(f)
+        return float(m["hbm_gbs"]), float(m["bf16_tflops"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def make_inputs(cfg, device, dtype=torch.bfloat16, seed=0):
+    from dc_triton_opt_b200 import DCTerms
+    B, T, H, D, G, R = (cfg[k] for k in ("B", "T", "H", "D", "G", "R"))
+    hpg = H // G
+    g = torch.Generator(device=device).manual_seed(seed)
+    rn = lambda *s: torch.randn(*s, generator=g, device=device, dtype=torch.float32)
+    q, k, v = (rn(B, T, H, D).to(dtype) for _ in range(3))
+    sets = []
+    for _ in range(2):
+        sets.append(DCTerms(
+            identity=False, w=torch.eye(hpg, device=device)[None] + 0.02 * rn(G, hpg, hpg),
+            qw1=(0.1 * rn(B, T, H, R)).to(dtype), qw2=(0.1 * rn(B, T, R, H)).to(dtype),
+            kw1=(0.1 * rn(B, T, H, R)).to(dtype), kw2=(0.1 * rn(B, T, R, H)).to(dtype),
+            qdd=(0.1 * rn(B, T, H)).to(dtype), kdd=(0.1 * rn(B, T, H)).to(dtype)))
+    return q, k, v, sets[0], sets[1]
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "200"],
+                                      stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.p = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *a):
+        if self.p is not None:
+            self.p.terminate()
+            try:
+                self.p.wait(timeout=5)
+            except Exception:
+                self.p.kill()
+
+    def summary(self):
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, val in zip(names, r[5:9]) if "Active" in val
+                          and "Not" not in val})
+        load = [s for s in sm if s > 0.5 * (max(mx) if mx else 1)] or sm
+        return {"sm_mhz": statistics.median(load) if load else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons, "samples": len(rows)}
+
+
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+    else:
+        torch.cuda.set_device(0)
+    return world, rank, local
+
+
+def shard_batch(B, world, rank):
+    """Contiguous batch slice [b0, b1) of this rank (even split, remainder to the first ranks)."""
+    base, rem = divmod(B, world)
+    b0 = rank * base + min(rank, rem)
+    return b0, b0 + base + (1 if rank < rem else 0)
+
+
+_CPU_INPUTS = {}
+
+
+def cpu_port_sample(cfg, target_s=12.0, threads=None):
+    """Time the torch-CPU restatement on batch 0, a bounded query range, repeated
+    until ~target_s seconds; returns (TFLOP/s, cores, sample description)."""
+    from oracle.dc_oracle import make_inputs as np_inputs
+    from oracle.dc_oracle_torch import dc_attn_torch_cpu
+    threads = threads or os.cpu_count()
+    torch.set_num_threads(threads)
+    T, H, D, G, R, W = cfg["T"], cfg["H"], cfg["D"], cfg["G"], cfg["R"], cfg["window"]
+    t0, t1 = (T - 512, T) if W is not None else (T - 256, T)
+    key = (T, H, D, G, R)
+    if key not in _CPU_INPUTS:
+        _CPU_INPUTS[key] = np_inputs(1, T, H, D, G, R, seed=0)
+        q, k, v, pre, post = _CPU_INPUTS[key]
+        dc_attn_torch_cpu(q, k, v, pre, post, D ** -0.5, W, G, None, t_range=(t1 - 64, t1))  # warm
+    q, k, v, pre, post = _CPU_INPUTS[key]
+    scale = D ** -0.5
+    n, start = 0, time.perf_counter()
+    while True:
+        dc_attn_torch_cpu(q, k, v, pre, post, scale, W, G, None, t_range=(t0, t1))
+        n += 1
+        el = time.perf_counter() - start
+        if el >= target_s:
+            break
+    fl = flops(1, H, D, G, R, pairs_range(t0, t1, W)) * n
+    sample = (f"batch 1 of {cfg['B']}, queries [{t0},{t1}) of T={T}, all {H} heads; "
+              f"{n} calls in {el:.1f} s (fp32 torch CPU, oracle/dc_oracle_torch.py)")
+    return fl / el / 1e12, threads, sample
+
+
+def run_reference(args, cfg, world, rank):
+    if world > 1 and rank != 0:
+        return
+    vals = []
+    for _ in range(args.warmup + args.steps):
+        v, cores, sample = cpu_port_sample(cfg, target_s=max(2.0, 30.0 / max(1, args.steps + args.warmup)))
+        vals.append(v)
+    val = statistics.median(vals[args.warmup:]) if len(vals) > args.warmup else vals[-1]
+    line = {
+        "impl": "reference", "metric": "DC-attn fwd effective TFLOP/s", "value": val, "unit": "TFLOP/s",
+        "n_gpus": 0, "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+        "dtype": "f32", "data": "synthetic", "config": config_desc(args, cfg, world),
+        "cpu_baseline": {"value": val, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": val, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "vs_baseline": None,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def config_desc(args, cfg, world):
+    d = {"workload": args.workload, "B": cfg["B"], "T": cfg["T"], "H": cfg["H"], "D": cfg["D"],
+         "window": cfg["window"] if cfg["window"] is not None else "full_causal", "G": cfg["G"],
+         "HPG": cfg["H"] // cfg["G"], "R": cfg["R"],
+         "terms": "static W + query- and key-wise rank R + qdd + kdd (pre and post)",
+         "l2": "inputs larger than L2 (no flush)", "parallelism": f"batch-sharded x{world}, no collectives"}
+    return d
+
+
+def load_traffic(workload_key):
+    path = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(workload_key)
+    except Exception:
+        return None
+
+
+def run_ours(args, cfg, world, rank, local):
+    import dc_triton_opt_b200 as dc
+    from dc_triton_opt_b200 import _lib
+    _lib.load()
+    device = torch.device("cuda", local)
+    rcfg = dict(cfg)
+    if args.workload == "config4":
+        b0, b1 = shard_batch(cfg["B"], world, rank)
+        rcfg["B"] = b1 - b0
+    q, k, v, pre, post = make_inputs(rcfg, device, seed=1234 + rank)
+    B, T, H, D, G, R, W = (rcfg[k] for k in ("B", "T", "H", "D", "G", "R", "window"))
+    stream = torch.cuda.current_stream(device)
+    out = torch.empty_like(q)
+    call = lambda: dc.dc_attn_fwd(q, k, v, pre, post, D ** -0.5, W, G, out=out, kernel=args.kernel)
+    kernel_used = dc.select_kernel(q, k, v, pre, post, W, G) if args.kernel == "auto" else args.kernel
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier()
+        torch.cuda.synchronize()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        ev0.record(stream)
+        for _ in range(args.steps):
+            call()
+        ev1.record(stream)
+        barrier()
+    ms = ev0.elapsed_time(ev1)
+    ms_max = ms
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms_max = float(t.item())
+    ms_step = ms_max / args.steps
+
+    # end to end: pinned host inputs -> device, forward, output -> host, every step
+    host = {}
+    dev_in = []
+    for name, t in (("q", q), ("k", k), ("v", v)):
+        host[name] = t.cpu().pin_memory()
+        dev_in.append((host[name], t))
+    for side, tm in (("pre", pre), ("post", post)):
+        for f in ("qw1", "qw2", "kw1", "kw2", "qdd", "kdd"):
+            t = getattr(tm, f)
+            h = t.cpu().pin_memory()
+            dev_in.append((h, t))
+    out_host = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+    h2d = sum(h.numel() * h.element_size() for h, _ in dev_in)
+    d2h = out_host.numel() * out_host.element_size()
+    e2e_steps = max(1, min(args.steps, 10))
+
+    def e2e_step():
+        for h, d in dev_in:
+            d.copy_(h, non_blocking=True)
+        call()
+        out_host.copy_(out, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    barrier()
+    ev0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    ev1.record(stream)
+    barrier()
+    e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    fl_rank = flops(B, H, D, G, R, pairs(T, W))
+    total_fl = fl_rank * world
+    value = total_fl / (ms_step * 1e-3) / 1e12
+    e2e_val = total_fl / (e2e_ms * 1e-3) / 1e12
+    hbm, tc_peak, peak_src = peaks()
+    by = algo_bytes(B, T, H, D, R)
+    achieved = by / (ms_step * 1e-3) / 1e9
+    tflops_rank = fl_rank / (ms_step * 1e-3) / 1e12
+    if rank != 0:
+        return
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        v_cpu, cores, sample = cpu_port_sample(cfg, target_s=12.0)
+        cpu = {"value": v_cpu, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
+    wl_key = f"{args.workload}_G{G}_W{W}"
+    line = {
+        "metric": "DC-attn fwd effective TFLOP/s", "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step, "us_per_call": ms_step * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong" if args.workload == "config4" else "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded; BASELINE distributions)",
+        "config": config_desc(args, cfg, world), "kernel": kernel_used,
+        "gpu_launches": args.steps,
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                     "frac": achieved / hbm, "peak_source": peak_src,
+                     "traffic": load_traffic(wl_key), "algo_bytes_per_launch": by,
+                     "tensor_tflops": tflops_rank, "tensor_peak": tc_peak,
+                     "tensor_frac": tflops_rank / tc_peak},
+        "e2e": {"value": e2e_val, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "ms_per_step": e2e_ms},
+        "clocks": clk.summary(),
+        "cpu_baseline": cpu,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="config1", choices=sorted(WORKLOADS))
+    ap.add_argument("--G", type=int, default=None)
+    ap.add_argument("--window", type=int, default=None)
+    ap.add_argument("--B", type=int, default=None)
+    ap.add_argument("--T", type=int, default=None)
+    ap.add_argument("--kernel", default="auto", choices=["auto", "simt", "tc"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    cfg = dict(WORKLOADS[args.workload])
+    for k in ("G", "window", "B", "T"):
+        if getattr(args, k) is not None:
+            cfg[k] = getattr(args, k)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.impl == "reference":
+        run_reference(args, cfg, world, int(os.environ.get("RANK", "0")))
+        return
+    world, rank, local = dist_setup()
+    try:
+        run_ours(args, cfg, world, rank, local)
+    finally:
+        if world > 1:
+            torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,14 @@
+"""B200-native (sm_100a) DC-attention forward.
+
+Drop-in replacements for the reference project's torch-callable DC-attention
+entry points, backed by hand-written CUDA kernels behind a C ABI
+(``include/dc_attn.h``).  See :mod:`dc_triton_opt_b200.api`.
+"""
+
+from .api import (DCTerms, dc_attn_fwd, dc_attention_decomposed_window_chunked,
+                  dc_attention_window_chunked_residual,
+                  dc_attention_window_chunked_residual_grouped, select_kernel)
+
+__all__ = ["DCTerms", "dc_attn_fwd", "dc_attention_window_chunked_residual_grouped",
+           "dc_attention_window_chunked_residual", "dc_attention_decomposed_window_chunked",
+           "select_kernel"]

@@ -1,0 +1,225 @@
+"""Torch-callable DC-attention forward on B200, backed by ``libdcattn.so``.
+
+Entry points (each a drop-in for the reference call it names):
+
+* :func:`dc_attn_fwd` — general form: static head mix W, query- and key-wise
+  rank-R weights, qdd/kdd gates, per-query matrices; window or full causal.
+* :func:`dc_attention_window_chunked_residual_grouped` —
+  ``dc_attention_torch.py:159`` (same signature, defaults, output [B,N,T,D]).
+* :func:`dc_attention_window_chunked_residual` — ``dc_attention_torch.py:88``.
+* :func:`dc_attention_decomposed_window_chunked` — ``dc_attention_torch.py:22``
+  (per-query N x N mixing matrices, output [B,T,N,D]).
+
+All of them run the CUDA kernels on the tensors' device and current stream,
+asynchronously, and raise ``RuntimeError`` for bad arguments (the reference
+raises through ``TORCH_CHECK``, which surfaces as ``RuntimeError`` too).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass, fields
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+
+_DTYPES = {torch.bfloat16: _lib.DC_DTYPE_BF16, torch.float16: _lib.DC_DTYPE_FP16}
+
+
+@dataclass
+class DCTerms:
+    """One composition term set (pre on logits, post on probabilities).
+
+    Shapes (B,T,H heads, G groups, HPG=H/G, rank R):
+      w [G,HPG,HPG] (any float dtype, used as fp32): a'[h] += sum_h' a[h'] w[g,h',h]
+      qw1/kw1 [B,T,H,R]; qw2/kw2 [B,T,R,H]; qdd/kdd [B,T,H]; qmat [B,T,H,HPG].
+    ``identity`` adds a[h] itself (the reference's residual term).
+    """
+
+    identity: bool = False
+    w: Optional[torch.Tensor] = None
+    qw1: Optional[torch.Tensor] = None
+    qw2: Optional[torch.Tensor] = None
+    kw1: Optional[torch.Tensor] = None
+    kw2: Optional[torch.Tensor] = None
+    qdd: Optional[torch.Tensor] = None
+    kdd: Optional[torch.Tensor] = None
+    qmat: Optional[torch.Tensor] = None
+
+    @staticmethod
+    def residual(w1, w2, dd) -> "DCTerms":
+        """The reference's residual rank-1 set from three [B,T,N] tensors
+        (``dc_attention_torch.py:217-225``): a + dd*a + w2 * sum(w1*a)."""
+        return DCTerms(identity=True, qw1=w1.unsqueeze(-1), qw2=w2.unsqueeze(-2), qdd=dd)
+
+
+def _check(cond, msg):
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _prep(t: Optional[torch.Tensor], name: str, shape, dtype, device, keep):
+    if t is None:
+        return None
+    _check(isinstance(t, torch.Tensor), f"{name} must be a torch.Tensor")
+    _check(t.device == device, f"{name} must be on {device} (got {t.device})")
+    _check(tuple(t.shape) == tuple(shape), f"{name} must have shape {list(shape)} (got {list(t.shape)})")
+    t = t.to(dtype).contiguous()
+    keep.append(t)
+    return t
+
+
+def _terms_struct(tm: Optional[DCTerms], name, B, T, H, G, R, dtype, device, keep) -> _lib.DcTerms:
+    s = _lib.DcTerms()
+    if tm is None:
+        s.identity = 1
+        return s
+    hpg = H // G
+    s.identity = 1 if tm.identity else 0
+    shapes = {"w": (G, hpg, hpg), "qw1": (B, T, H, R), "qw2": (B, T, R, H), "kw1": (B, T, H, R),
+              "kw2": (B, T, R, H), "qdd": (B, T, H), "kdd": (B, T, H), "qmat": (B, T, H, hpg)}
+    for f in fields(DCTerms):
+        if f.name == "identity":
+            continue
+        t = getattr(tm, f.name)
+        dt = torch.float32 if f.name == "w" else dtype
+        t = _prep(t, f"{name}.{f.name}", shapes[f.name], dt, device, keep)
+        setattr(s, f.name, None if t is None else t.data_ptr())
+    return s
+
+
+def _infer_rank(*sets: Optional[DCTerms]) -> int:
+    R = 0
+    for tm in sets:
+        if tm is None:
+            continue
+        for a in (tm.qw1, tm.kw1):
+            if a is not None:
+                R = max(R, a.shape[-1])
+    return R
+
+
+def dc_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                pre: Optional[DCTerms] = None, post: Optional[DCTerms] = None,
+                scaling: Optional[float] = None, window: Optional[int] = None, G: int = 1,
+                seq_lens: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                kernel: str = "auto") -> torch.Tensor:
+    """General DC-attention forward.  q,k,v [B,T,H,D] (bf16 or fp16) -> [B,T,H,D].
+
+    ``window=None`` is full causal; otherwise key s is visible from query t iff
+    t - window < s <= t.  ``pre``/``post`` default to the identity (plain
+    attention).  ``out`` may be any tensor whose last dim is contiguous and whose
+    [b,t,h] strides are positive (e.g. a [B,N,T,D] tensor permuted to
+    [B,T,N,D]); it is written in place and returned.
+    """
+    _check(q.dim() == 4, f"q must be [B,T,H,D] (got {list(q.shape)})")
+    _check(k.shape == q.shape and v.shape == q.shape, "k and v must match q's shape")
+    _check(q.dtype in _DTYPES, f"q must be bfloat16 or float16 (got {q.dtype})")
+    _check(k.dtype == q.dtype and v.dtype == q.dtype, "q, k, v must share one dtype")
+    _check(q.is_cuda and k.device == q.device and v.device == q.device,
+           "q, k, v must be CUDA tensors on one device")
+    B, T, H, D = q.shape
+    _check(G >= 1 and H % G == 0, f"H={H} must be divisible by G={G}")
+    R = _infer_rank(pre, post)
+    device, dtype = q.device, q.dtype
+    keep = []
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    if out is None:
+        out = torch.empty((B, T, H, D), device=device, dtype=dtype)
+    _check(out.shape == (B, T, H, D) and out.dtype == dtype and out.device == device,
+           "out must be a [B,T,H,D] tensor of q's dtype and device")
+    _check(out.stride(3) == 1, "out must be contiguous in its last dim")
+    p = _lib.DcAttnParams()
+    p.abi_version = _lib.ABI_VERSION
+    p.B, p.T, p.H, p.D, p.G, p.R = B, T, H, D, G, R
+    p.window = 0 if window is None else int(window)
+    _check(window is None or int(window) >= 1, f"window must be >= 1 or None (got {window})")
+    p.scale = float(D ** -0.5 if scaling is None else scaling)
+    p.dtype = _DTYPES[dtype]
+    _check(kernel in _lib.KERNELS, f"kernel must be one of {sorted(_lib.KERNELS)}")
+    p.kernel = _lib.KERNELS[kernel]
+    p.q, p.k, p.v, p.out = q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr()
+    p.out_sb, p.out_st, p.out_sh = out.stride(0), out.stride(1), out.stride(2)
+    if seq_lens is not None:
+        _check(seq_lens.shape == (B,), f"seq_lens must be [B]={B} (got {list(seq_lens.shape)})")
+        seq_lens = seq_lens.to(device=device, dtype=torch.int32).contiguous()
+        keep.append(seq_lens)
+        p.seq_lens = seq_lens.data_ptr()
+    p.pre = _terms_struct(pre, "pre", B, T, H, G, R, dtype, device, keep)
+    p.post = _terms_struct(post, "post", B, T, H, G, R, dtype, device, keep)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        _lib.check(lib.dc_attn_fwd(ctypes.byref(p), ctypes.c_void_p(stream)))
+    # Converted temporaries in `keep` may be freed on return: the caching
+    # allocator only hands their blocks to later work on this same stream.
+    return out
+
+
+def select_kernel(q, k, v, pre=None, post=None, window=None, G=1) -> str:
+    """Which kernel ``kernel='auto'`` runs for these arguments ('tc' or 'simt')."""
+    B, T, H, D = q.shape
+    p = _lib.DcAttnParams()
+    p.abi_version = _lib.ABI_VERSION
+    p.B, p.T, p.H, p.D, p.G, p.R = B, T, H, D, G, _infer_rank(pre, post)
+    p.window = 0 if window is None else int(window)
+    p.scale = 1.0
+    p.dtype = _DTYPES.get(q.dtype, -1)
+    p.q = p.k = p.v = p.out = 16  # placeholders: selection reads only sizes and term presence
+    p.out_sb, p.out_st, p.out_sh = T * H * D, H * D, D
+    for side, tm in (("pre", pre), ("post", post)):
+        st = getattr(p, side)
+        st.identity = 1 if (tm is None or tm.identity) else 0
+        if tm is not None:
+            for f in fields(DCTerms):
+                if f.name != "identity" and getattr(tm, f.name) is not None:
+                    setattr(st, f.name, 16)
+    rc = _lib.load().dc_attn_select_kernel(ctypes.byref(p))
+    _lib.check(rc if rc < 0 else 0, "dc_attn_select_kernel")
+    return {1: "simt", 2: "tc"}[rc]
+
+
+def _residual_call(q, k, v, dc_weights, scaling, window, seq_lens, G, out):
+    _check(len(dc_weights) == 6, "dc_weights must be (pre_w1, pre_w2, pre_dd, post_w1, post_w2, post_dd)")
+    pw1, pw2, pdd, qw1, qw2, qdd = dc_weights
+    B, T, N, D = q.shape
+    for name, w in zip(("pre_w1", "pre_w2", "pre_dd", "post_w1", "post_w2", "post_dd"), dc_weights):
+        _check(tuple(w.shape) == (B, T, N), f"{name} must be [B,T,N]")
+    return dc_attn_fwd(q, k, v, DCTerms.residual(pw1, pw2, pdd), DCTerms.residual(qw1, qw2, qdd),
+                       scaling, window, G, seq_lens, out)
+
+
+def dc_attention_window_chunked_residual_grouped(
+        q, k, v, dc_weights: Sequence[torch.Tensor], scaling: float, window: Optional[int] = None,
+        seq_lens: Optional[torch.Tensor] = None, chunk_size: Optional[int] = None, G: int = 1):
+    """Drop-in for ``dc_attention_torch.dc_attention_window_chunked_residual_grouped``
+    (``dc_attention_torch.py:159-258``): q,k,v [B,T,N,D], six [B,T,N] weights,
+    window default 256, returns a contiguous [B,N,T,D] tensor of q's dtype.
+    ``chunk_size`` is accepted and ignored (the reference's mask is exact)."""
+    B, T, N, D = q.shape
+    if window is None:
+        window = 256
+    out = torch.empty((B, N, T, D), device=q.device, dtype=q.dtype)
+    _residual_call(q, k, v, dc_weights, scaling, window, seq_lens, G, out.permute(0, 2, 1, 3))
+    return out
+
+
+def dc_attention_window_chunked_residual(q, k, v, dc_weights, scaling, window=None, seq_lens=None,
+                                         chunk_size=None):
+    """Drop-in for ``dc_attention_torch.dc_attention_window_chunked_residual``
+    (``dc_attention_torch.py:88-156``): the G=1 case, output [B,N,T,D]."""
+    return dc_attention_window_chunked_residual_grouped(q, k, v, dc_weights, scaling, window,
+                                                        seq_lens, chunk_size, G=1)
+
+
+def dc_attention_decomposed_window_chunked(q, k, v, pre_w, post_w, scaling, window, seq_lens,
+                                           chunk_size):
+    """Drop-in for ``dc_attention_torch.dc_attention_decomposed_window_chunked``
+    (``dc_attention_torch.py:22-84``): per-query N x N matrices
+    (``mixed[i] = sum_j pre_w[b,t,i,j] L[j]``), no residual, output [B,T,N,D].
+    ``window`` is clamped to [1, T] as in the reference (``:38``)."""
+    B, T, N, D = q.shape
+    window = max(1, min(int(window), T))
+    return dc_attn_fwd(q, k, v, DCTerms(qmat=pre_w), DCTerms(qmat=post_w), scaling, window, 1, seq_lens)

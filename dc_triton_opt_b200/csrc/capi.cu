@@ -1,0 +1,154 @@
+// C ABI of the DC-attention forward: argument validation, kernel selection,
+// launch.  Mirrors the checks of the reference bindings
+// (dc_hopper_cuda/dc_hopper_kernel.cu:579-635 check_fixed_inputs, and the
+// shape gates of cuda_dc_onekernel_v4.py:27-40) as error codes instead of
+// TORCH_CHECK, so any FFI can bind it.
+
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+
+#include "common.cuh"
+
+namespace dcattn {
+cudaError_t launch_simt(const ParamsDev &p, int dtype, cudaStream_t st);
+size_t simt_smem_bytes(int HPG, int D, int R, int dtype);
+bool tc_supports(const dc_attn_params &p, std::string *why);
+cudaError_t launch_tc(const dc_attn_params &p, cudaStream_t st);
+}  // namespace dcattn
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
+int fail(int code, const char *fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int check_terms(const dc_attn_params &p, const dc_terms &t, const char *side) {
+  if ((t.qw1 == nullptr) != (t.qw2 == nullptr))
+    return fail(DC_ERR_NULL, "%s: qw1 and qw2 must both be given or both be NULL", side);
+  if ((t.kw1 == nullptr) != (t.kw2 == nullptr))
+    return fail(DC_ERR_NULL, "%s: kw1 and kw2 must both be given or both be NULL", side);
+  if ((t.qw1 || t.kw1) && p.R < 1)
+    return fail(DC_ERR_SHAPE, "%s: rank-R weights given but R=%d", side, p.R);
+  return DC_OK;
+}
+
+int validate(const dc_attn_params *pp) {
+  if (!pp) return fail(DC_ERR_NULL, "params is NULL");
+  const dc_attn_params &p = *pp;
+  if (p.abi_version != DC_ATTN_ABI_VERSION)
+    return fail(DC_ERR_SHAPE, "abi_version %d != library %d", p.abi_version, DC_ATTN_ABI_VERSION);
+  if (!p.q || !p.k || !p.v || !p.out) return fail(DC_ERR_NULL, "q, k, v and out must be non-NULL");
+  if (p.dtype != DC_DTYPE_BF16 && p.dtype != DC_DTYPE_FP16)
+    return fail(DC_ERR_DTYPE, "dtype must be DC_DTYPE_BF16 or DC_DTYPE_FP16 (got %d)", p.dtype);
+  if (p.B < 1 || p.T < 1 || p.H < 1 || p.D < 1 || p.G < 1)
+    return fail(DC_ERR_SHAPE, "B, T, H, D, G must be >= 1 (B=%d T=%d H=%d D=%d G=%d)", p.B, p.T, p.H, p.D,
+                p.G);
+  if (p.H % p.G != 0) return fail(DC_ERR_SHAPE, "H=%d must be divisible by G=%d", p.H, p.G);
+  if (p.H / p.G > 128) return fail(DC_ERR_SHAPE, "heads per group H/G=%d exceeds 128", p.H / p.G);
+  if (p.D > 128 || p.D % 8 != 0) return fail(DC_ERR_SHAPE, "D=%d must be a multiple of 8 and <= 128", p.D);
+  if (p.R < 0 || p.R > 8) return fail(DC_ERR_SHAPE, "R=%d must be in [0, 8]", p.R);
+  if ((int64_t)p.B * p.G > 65535) return fail(DC_ERR_SHAPE, "B*G=%lld exceeds 65535", (long long)p.B * p.G);
+  if (!(p.scale == p.scale)) return fail(DC_ERR_SHAPE, "scale is NaN");
+  if (p.out_sh < p.D || p.out_sb < 1 || p.out_st < 1)
+    return fail(DC_ERR_SHAPE, "output strides (b=%lld t=%lld h=%lld) must be positive with h-stride >= D",
+                (long long)p.out_sb, (long long)p.out_st, (long long)p.out_sh);
+  int rc;
+  if ((rc = check_terms(p, p.pre, "pre")) != DC_OK) return rc;
+  if ((rc = check_terms(p, p.post, "post")) != DC_OK) return rc;
+  return DC_OK;
+}
+
+int select_kernel(const dc_attn_params &p) {
+  if (p.kernel == DC_KERNEL_SIMT) return DC_KERNEL_SIMT;
+  std::string why;
+  const bool tc_ok = dcattn::tc_supports(p, &why);
+  if (p.kernel == DC_KERNEL_TC) {
+    if (!tc_ok) return fail(DC_ERR_UNSUPPORTED, "tensor-core kernel does not support this call: %s", why.c_str());
+    return DC_KERNEL_TC;
+  }
+  if (p.kernel != DC_KERNEL_AUTO) return fail(DC_ERR_SHAPE, "unknown kernel selector %d", p.kernel);
+  return tc_ok ? DC_KERNEL_TC : DC_KERNEL_SIMT;
+}
+
+int check_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(DC_ERR_DEVICE, "cudaGetDevice failed");
+  int major = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess)
+    return fail(DC_ERR_DEVICE, "device query failed");
+  if (major != 10) return fail(DC_ERR_DEVICE, "this library is built for sm_100a; device %d is sm_%d.x", dev, major);
+  return DC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int dc_attn_abi_version(void) { return DC_ATTN_ABI_VERSION; }
+
+int dc_attn_params_size(void) { return (int)sizeof(dc_attn_params); }
+
+const char *dc_attn_last_error(void) { return g_last_error.c_str(); }
+
+int dc_attn_select_kernel(const dc_attn_params *p) {
+  int rc = validate(p);
+  if (rc != DC_OK) return rc;
+  return select_kernel(*p);
+}
+
+int dc_attn_fwd(const dc_attn_params *pp, void *stream) {
+  int rc = validate(pp);
+  if (rc != DC_OK) return rc;
+  const dc_attn_params &p = *pp;
+  const int which = select_kernel(p);
+  if (which < 0) return which;
+  if ((rc = check_device()) != DC_OK) return rc;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  if (which == DC_KERNEL_TC) {
+    e = dcattn::launch_tc(p, st);
+  } else {
+    e = dcattn::launch_simt(dcattn::to_dev(p), p.dtype, st);
+  }
+  if (e != cudaSuccess)
+    return fail(DC_ERR_LAUNCH, "kernel launch failed: %s", cudaGetErrorString(e));
+  g_last_error.clear();
+  return DC_OK;
+}
+
+int dc_attn_fwd_residual(const void *q, const void *k, const void *v, const void *pre_w1, const void *pre_w2,
+                         const void *pre_dd, const void *post_w1, const void *post_w2, const void *post_dd,
+                         void *out, int64_t out_sb, int64_t out_st, int64_t out_sh, const int32_t *seq_lens,
+                         int32_t B, int32_t T, int32_t N, int32_t D, int32_t G, float scaling, int32_t window,
+                         int32_t chunk_size, int32_t dtype, void *stream) {
+  (void)chunk_size;  // tiling hint only in the reference; the mask is exact
+  if (!pre_w1 || !pre_w2 || !pre_dd || !post_w1 || !post_w2 || !post_dd)
+    return fail(DC_ERR_NULL, "all six DC weights must be non-NULL");
+  dc_attn_params p;
+  std::memset(&p, 0, sizeof(p));
+  p.abi_version = DC_ATTN_ABI_VERSION;
+  p.B = B; p.T = T; p.H = N; p.D = D; p.G = G; p.R = 1;
+  p.window = window; p.scale = scaling; p.dtype = dtype; p.kernel = DC_KERNEL_AUTO;
+  p.q = q; p.k = k; p.v = v; p.out = out;
+  p.out_sb = out_sb; p.out_st = out_st; p.out_sh = out_sh;
+  p.seq_lens = seq_lens;
+  // [B,T,N] weights are [B,T,N,1] / [B,T,1,N] rank-1 factors with identical memory layout
+  p.pre.identity = 1; p.pre.qw1 = pre_w1; p.pre.qw2 = pre_w2; p.pre.qdd = pre_dd;
+  p.post.identity = 1; p.post.qw1 = post_w1; p.post.qw2 = post_w2; p.post.qdd = post_dd;
+  return dc_attn_fwd(&p, stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,139 @@
+/*
+ * dc_attn.h — C ABI of the B200 (sm_100a) DC-attention forward.
+ *
+ * DC ("dynamically composable multi-head") attention forward for one layer:
+ *   L_h   = scale * Q_h K_h^T                         (per head)
+ *   S     = compose_pre(L)                            (across the HPG heads of a group)
+ *   P_h   = softmax_s(mask(S_h))                      (causal, sliding window, seq_lens)
+ *   P'    = compose_post(P)
+ *   out_h = P'_h V_h
+ * compose(a)[h] = [identity] a[h] + sum_h' a[h'] w[g,h',h]
+ *               + sum_r qw2[b,t,r,h] sum_h' qw1[b,t,h',r] a[h']
+ *               + sum_r kw2[b,s,r,h] sum_h' kw1[b,s,h',r] a[h']
+ *               + (qdd[b,t,h] + kdd[b,s,h]) a[h]
+ *               + sum_j qmat[b,t,h,j] a[g*HPG + j]
+ *
+ * The reference project (Lisennlp/dc_triton_opt) exposes this path through
+ * pybind11/torch bindings only; the entry points below are the plain-pointer
+ * equivalents those bindings would call:
+ *   - dc_attn_fwd           replaces the general forward named by the project
+ *                           (superset of dc_attention_torch.py:22-258)
+ *   - dc_attn_fwd_residual  replaces dc_hopper_cuda/dc_hopper_api.cpp:17-28
+ *                           (forward_hpg4_wide_ref / _opt / _cluster, kernel
+ *                           dc_hopper_kernel.cu:639-687) and
+ *                           dc_fused_cuda/kernel.cu:1350-1431
+ *                           (dc_onekernel_v4_fwd_cuda), i.e. the residual
+ *                           rank-1 form with six [B,T,N] weight tensors.
+ *
+ * Conventions (mirroring the reference bindings):
+ *   - all pointers are device pointers owned by the caller; the library
+ *     allocates nothing and never synchronises;
+ *   - work is enqueued on `stream` (a cudaStream_t passed as void*; NULL =
+ *     legacy default stream) and is asynchronous;
+ *   - the return value is 0 on success or a negative DC_ERR_* code; the
+ *     message of the last error on the calling thread is returned by
+ *     dc_attn_last_error().
+ */
+#ifndef DC_ATTN_H_
+#define DC_ATTN_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define DC_ATTN_ABI_VERSION 1
+
+#if defined(_WIN32)
+#define DC_API __declspec(dllexport)
+#else
+#define DC_API __attribute__((visibility("default")))
+#endif
+
+/* element type of q, k, v, out and the per-token composition weights */
+enum dc_dtype { DC_DTYPE_BF16 = 0, DC_DTYPE_FP16 = 1 };
+
+enum dc_status {
+  DC_OK = 0,
+  DC_ERR_NULL = -1,        /* a required pointer is NULL                       */
+  DC_ERR_SHAPE = -2,       /* inconsistent or out-of-range sizes               */
+  DC_ERR_DTYPE = -3,       /* unknown dtype                                    */
+  DC_ERR_UNSUPPORTED = -4, /* valid request the selected kernel cannot handle  */
+  DC_ERR_ALIGN = -5,       /* a pointer or stride breaks the 16-byte rule      */
+  DC_ERR_LAUNCH = -6,      /* CUDA launch / attribute error                    */
+  DC_ERR_DEVICE = -7       /* no sm_100 device / device query failed           */
+};
+
+/* kernel selection (dc_attn_params.kernel) */
+enum dc_kernel {
+  DC_KERNEL_AUTO = 0, /* fastest kernel that supports the request            */
+  DC_KERNEL_SIMT = 1, /* general CUDA-core kernel: every term, any window    */
+  DC_KERNEL_TC = 2    /* tcgen05/TMEM/TMA kernel (windowed layers)           */
+};
+
+/* One composition term set (pre: on logits, post: on probabilities).
+ * Every pointer may be NULL (term absent).  Per-token tensors are contiguous
+ * in the params' dtype; w is fp32.  Shapes use B,T,H,G,R,HPG=H/G of the call. */
+typedef struct dc_terms {
+  int32_t identity;    /* non-zero: add a[h] (the reference's residual "+ L")   */
+  const float *w;      /* [G, HPG, HPG]  static head mix, a'[h] += a[h'] w[g,h',h] */
+  const void *qw1;     /* [B, T, H, R]   query-wise rank-R, first factor        */
+  const void *qw2;     /* [B, T, R, H]   query-wise rank-R, second factor       */
+  const void *kw1;     /* [B, T, H, R]   key-wise rank-R (indexed by the key)   */
+  const void *kw2;     /* [B, T, R, H]                                          */
+  const void *qdd;     /* [B, T, H]      query-wise diagonal gate               */
+  const void *kdd;     /* [B, T, H]      key-wise diagonal gate                 */
+  const void *qmat;    /* [B, T, H, HPG] per-query full mix inside the group    */
+} dc_terms;
+
+typedef struct dc_attn_params {
+  int32_t abi_version;     /* must be DC_ATTN_ABI_VERSION                        */
+  int32_t B, T, H, D, G, R;
+  int32_t window;          /* > 0: key s visible iff t-window < s <= t; <= 0: full causal */
+  float scale;             /* softmax scale applied to q.k                        */
+  int32_t dtype;           /* enum dc_dtype                                       */
+  int32_t kernel;          /* enum dc_kernel                                      */
+  const void *q, *k, *v;   /* [B, T, H, D] contiguous                             */
+  void *out;               /* out[b*out_sb + t*out_st + h*out_sh + d]             */
+  int64_t out_sb, out_st, out_sh; /* element strides; d is contiguous             */
+  const int32_t *seq_lens; /* [B] keys s >= seq_lens[b] are masked; NULL = T      */
+  int32_t *err_flag;       /* optional device int; kernels that wait on barriers
+                              write a non-zero code here instead of hanging       */
+  dc_terms pre, post;
+} dc_attn_params;
+
+/* General forward.  Returns DC_OK or a DC_ERR_* code. */
+DC_API int dc_attn_fwd(const dc_attn_params *p, void *stream);
+
+/* Residual rank-1 form of the reference (six [B,T,N] weights, identity
+ * residual), output [B,T,N,D] written with the given element strides.
+ * window <= 0 means full causal.  chunk_size is accepted for signature parity
+ * with the reference and does not change the result. */
+DC_API int dc_attn_fwd_residual(const void *q, const void *k, const void *v,
+                         const void *pre_w1, const void *pre_w2, const void *pre_dd,
+                         const void *post_w1, const void *post_w2, const void *post_dd,
+                         void *out, int64_t out_sb, int64_t out_st, int64_t out_sh,
+                         const int32_t *seq_lens, int32_t B, int32_t T, int32_t N,
+                         int32_t D, int32_t G, float scaling, int32_t window,
+                         int32_t chunk_size, int32_t dtype, void *stream);
+
+/* Which kernel DC_KERNEL_AUTO would pick for *p (enum dc_kernel), or a
+ * negative DC_ERR_* code if no kernel supports the request. */
+DC_API int dc_attn_select_kernel(const dc_attn_params *p);
+
+/* Message of the last error on the calling thread ("" if none). */
+DC_API const char *dc_attn_last_error(void);
+
+/* Library ABI version (DC_ATTN_ABI_VERSION of the build). */
+DC_API int dc_attn_abi_version(void);
+
+/* sizeof(dc_attn_params) in this build, so FFI bindings can check their
+ * struct mirror. */
+DC_API int dc_attn_params_size(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DC_ATTN_H_ */

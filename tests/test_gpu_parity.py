@@ -1,0 +1,220 @@
+"""Parity of the CUDA kernels with the oracle and the reference's golden vectors.
+
+Every call goes through the library's C ABI (ctypes -> libdcattn.so); the
+oracle in oracle/dc_oracle.py is only the checker.  Tolerances: tests/tolerances.py.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import dc_triton_opt_b200 as dc
+from dc_triton_opt_b200 import dc_hopper_cuda, onekernel
+from oracle import dc_oracle as O
+from tests.golden_cases import load_cases
+from tests.tolerances import assert_close
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda:0"
+TORCH_DT = {"bf16": torch.bfloat16, "fp16": torch.float16}
+KERNELS = ["simt", "auto"]
+
+
+def T_(x, dt):
+    return None if x is None else torch.from_numpy(np.ascontiguousarray(x)).to(DEV).to(dt)
+
+
+def to_dcterms(t: O.Terms, dt) -> dc.DCTerms:
+    return dc.DCTerms(identity=t.identity, w=T_(t.w, torch.float32), qw1=T_(t.qw1, dt), qw2=T_(t.qw2, dt),
+                      kw1=T_(t.kw1, dt), kw2=T_(t.kw2, dt), qdd=T_(t.qdd, dt), kdd=T_(t.kdd, dt),
+                      qmat=T_(t.qmat, dt))
+
+
+def round_terms(t: O.Terms, dt) -> O.Terms:
+    """Round a term set's per-token tensors to the kernel dtype (w stays fp32)."""
+    r = O.Terms(identity=t.identity, w=t.w)
+    for n in ("qw1", "qw2", "kw1", "kw2", "qdd", "kdd", "qmat"):
+        a = getattr(t, n)
+        if a is not None:
+            setattr(r, n, torch.from_numpy(np.ascontiguousarray(a)).to(dt).float().numpy())
+    return r
+
+
+def rnd(x, dt):
+    return torch.from_numpy(np.ascontiguousarray(x)).to(dt).float().numpy()
+
+
+def run_general(q, k, v, pre, post, scale, window, G, seq_lens=None, dtype="bf16", kernel="auto"):
+    dt = TORCH_DT[dtype]
+    out = dc.dc_attn_fwd(T_(q, dt), T_(k, dt), T_(v, dt), to_dcterms(pre, dt), to_dcterms(post, dt), scale,
+                         window, G, None if seq_lens is None else torch.tensor(seq_lens, device=DEV),
+                         kernel=kernel)
+    torch.cuda.synchronize()
+    return out.float().cpu().numpy()
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _cuda():
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    torch.cuda.init()
+
+
+# ---------------------------------------------------------------- golden vectors
+
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("case", load_cases(), ids=lambda c: c.name)
+def test_golden(case, kernel):
+    dt = TORCH_DT[case.dtype]
+    q, k, v = (T_(x, dt) for x in (case.q, case.k, case.v))
+    sl = None if case.seq_lens is None else torch.tensor(case.seq_lens, device=DEV)
+    if case.kind in ("grouped", "residual"):
+        ws = tuple(T_(w, dt) for w in case.ws)
+        if kernel == "auto" and case.kind == "grouped":
+            got = dc.dc_attention_window_chunked_residual_grouped(q, k, v, ws, case.scale, case.window, sl,
+                                                                  case.chunk, G=case.G)
+        elif kernel == "auto":
+            got = dc.dc_attention_window_chunked_residual(q, k, v, ws, case.scale, case.window, sl, case.chunk)
+        else:
+            got = dc.dc_attn_fwd(q, k, v, dc.DCTerms.residual(*ws[:3]), dc.DCTerms.residual(*ws[3:]),
+                                 case.scale, case.eff_window, case.G, sl, kernel=kernel).permute(0, 2, 1, 3)
+    elif case.kind == "decomposed":
+        pw, qw = T_(case.pre_w, dt), T_(case.post_w, dt)
+        if kernel == "auto":
+            got = dc.dc_attention_decomposed_window_chunked(q, k, v, pw, qw, case.scale, case.window, sl,
+                                                            case.chunk)
+        else:
+            got = dc.dc_attn_fwd(q, k, v, dc.DCTerms(qmat=pw), dc.DCTerms(qmat=qw), case.scale,
+                                 min(case.window, case.T), 1, sl, kernel=kernel)
+    else:
+        got = dc.dc_attn_fwd(q, k, v, to_dcterms(case.pre, dt), to_dcterms(case.post, dt), case.scale,
+                             case.window, case.G, sl, kernel=kernel)
+    torch.cuda.synchronize()
+    assert_close(got.float().cpu().numpy(), case.out, case.name)
+
+
+# ---------------------------------------------------------------- general terms
+
+GENERAL = [
+    # B, T, H, G, R, window, terms, seq_lens
+    (1, 96, 8, 2, 1, 32, ("w", "qw", "kw", "qdd", "kdd"), None),
+    (2, 80, 8, 1, 2, 24, ("w", "qw", "kw", "qdd", "kdd"), [80, 41]),
+    (1, 64, 8, 8, 2, 16, ("w", "qw", "kw", "qdd", "kdd"), None),   # HPG=1
+    (1, 130, 8, 2, 1, None, ("w", "qw", "kw", "qdd", "kdd"), None),  # full causal, ragged T
+    (1, 64, 16, 1, 1, 1, ("w", "qw", "kw", "qdd", "kdd"), None),   # window 1 (self only)
+    (1, 72, 8, 2, 2, 40, ("qw", "kw"), None),                      # identity + rank terms only
+]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "fp16"])
+@pytest.mark.parametrize("kernel", KERNELS)
+@pytest.mark.parametrize("B,T,H,G,R,window,terms,seq_lens", GENERAL)
+def test_general_terms(B, T, H, G, R, window, terms, seq_lens, kernel, dtype):
+    dt = TORCH_DT[dtype]
+    q, k, v, pre, post = O.make_inputs(B, T, H, 128, G, R, seed=B * 1000 + T + G, terms=terms)
+    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens)
+    got = run_general(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens, dtype, kernel)
+    assert_close(got, ref, f"B{B} T{T} H{H} G{G} R{R} W{window} {kernel} {dtype}")
+
+
+@pytest.mark.parametrize("kernel", KERNELS)
+def test_config0_shape(kernel):
+    """BASELINE config 0 shape (B2 T512 H32 D128 G1 W128 R1, every term), bf16 inputs."""
+    dt = torch.bfloat16
+    q, k, v, pre, post = O.make_inputs(2, 512, 32, 128, 1, 1, seed=0)
+    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, 128, 1, None, chunk=128)
+    got = run_general(q, k, v, pre, post, 128 ** -0.5, 128, 1, None, "bf16", kernel)
+    assert_close(got, ref, f"config0 {kernel}")
+
+
+@pytest.mark.parametrize("G", [1, 2, 4, 8, 16, 32])
+def test_group_sweep_small(G):
+    """Every G of the BASELINE sweep (HPG = 32/G) at a small T, auto kernel."""
+    dt = torch.bfloat16
+    q, k, v, pre, post = O.make_inputs(1, 160, 32, 128, G, 1, seed=G)
+    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, 64, G, None)
+    got = run_general(q, k, v, pre, post, 128 ** -0.5, 64, G)
+    assert_close(got, ref, f"G{G}")
+
+
+# ---------------------------------------------------------------- API surfaces
+
+def _residual_inputs(B, T, N, std, dt, seed):
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = (torch.randn(B, T, N, 128, generator=g).to(dt).to(DEV) for _ in range(3))
+    ws = tuple((std * torch.randn(B, T, N, generator=g)).to(dt).to(DEV) for _ in range(6))
+    return q, k, v, ws
+
+
+def _oracle_residual(q, k, v, ws, scale, window, G):
+    f = lambda x: x.float().cpu().numpy()
+    return O.grouped_residual(f(q), f(k), f(v), [f(w) for w in ws], scale, window, None, None, G)
+
+
+def test_hopper_api_matches_oracle():
+    """dc_hopper_cuda.forward_hpg4_wide_* with the reference test's own cases
+    (test_dc_hopper_cuda.py:171-175 shapes at B=1, std-1 weights, fp16)."""
+    for T, BM, W in ((256, 32, 224), (256, 16, 240)):
+        q, k, v, ws = _residual_inputs(1, T, 32, 1.0, torch.float16, T + BM)
+        ref = _oracle_residual(q, k, v, ws, 128 ** -0.5, W, 8).transpose(0, 2, 1, 3)
+        for fn in (dc_hopper_cuda.forward_hpg4_wide_ref, dc_hopper_cuda.forward_hpg4_wide_opt,
+                   dc_hopper_cuda.forward_hpg4_wide_cluster):
+            got = fn(q, k, v, *ws, 128 ** -0.5, W, BM)
+            torch.cuda.synchronize()
+            assert got.shape == (1, T, 32, 128)
+            assert_close(got.float().cpu().numpy(), ref, f"{fn.__name__} T{T} BM{BM} W{W}")
+
+
+def test_onekernel_class_matches_grouped():
+    q, k, v, ws = _residual_inputs(2, 192, 32, 0.1, torch.bfloat16, 11)
+    a = onekernel.TritonDCOneKernelMixedProbs.forward(q, k, v, ws, 128 ** -0.5, 112, None, G=8, chunk_size=16)
+    b = dc.dc_attention_window_chunked_residual_grouped(q, k, v, ws, 128 ** -0.5, 112, G=8)
+    torch.cuda.synchronize()
+    assert torch.equal(a, b.permute(0, 2, 1, 3))
+
+
+def test_output_layout_strided():
+    q, k, v, ws = _residual_inputs(1, 64, 8, 0.1, torch.bfloat16, 12)
+    out = dc.dc_attention_window_chunked_residual_grouped(q, k, v, ws, 0.1, 16, G=2)
+    assert out.shape == (1, 8, 64, 128) and out.is_contiguous()
+    flat = dc.dc_attn_fwd(q, k, v, dc.DCTerms.residual(*ws[:3]), dc.DCTerms.residual(*ws[3:]), 0.1, 16, 2)
+    torch.cuda.synchronize()
+    assert torch.equal(out.permute(0, 2, 1, 3), flat)
+
+
+def test_all_masked_rows_zero():
+    """seq_len 3 with window 4: queries t >= 6 see no key -> exact zeros (NaN-free)."""
+    q, k, v, ws = _residual_inputs(1, 32, 8, 0.1, torch.bfloat16, 13)
+    out = dc.dc_attn_fwd(q, k, v, dc.DCTerms.residual(*ws[:3]), dc.DCTerms.residual(*ws[3:]), 0.1, 4, 2,
+                         torch.tensor([3], device=DEV))
+    torch.cuda.synchronize()
+    assert torch.isfinite(out).all()
+    assert (out[0, 6:] == 0).all()
+
+
+def test_bad_arguments_raise():
+    q, k, v, ws = _residual_inputs(1, 32, 8, 0.1, torch.bfloat16, 14)
+    with pytest.raises(RuntimeError, match="divisible"):
+        dc.dc_attn_fwd(q, k, v, G=3)
+    with pytest.raises(RuntimeError, match="shape"):
+        dc.dc_attn_fwd(q, k, v, dc.DCTerms(qdd=ws[0][:, :16]))
+    with pytest.raises(RuntimeError, match="only N=32"):
+        dc_hopper_cuda.forward_hpg4_wide_ref(q, k, v, *ws, 0.1, 224, 32)
+
+
+def test_stream_semantics():
+    """The launch goes on the caller's current stream."""
+    q, k, v, ws = _residual_inputs(1, 128, 32, 0.1, torch.bfloat16, 15)
+    ref = dc.dc_attention_window_chunked_residual_grouped(q, k, v, ws, 0.1, 64, G=8)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        got = dc.dc_attention_window_chunked_residual_grouped(q, k, v, ws, 0.1, 64, G=8)
+    s.synchronize()
+    assert torch.equal(ref, got)
