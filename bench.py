@@ -14,7 +14,7 @@ reference algorithm (oracle/dc_oracle_torch.py, fp32, all host threads) on a
 bounded sample of the same workload; under torchrun only rank 0 runs it.
 
 Workloads (synthetic, seeded, BASELINE distributions):
-  config1  B16 T4096 H32 D128 window 128, R1 (G sweep via --G, default 1)
+  config1  B16 T4096 H32 D128 window 128, R1, G8 (HPG 4; G sweep via --G)
   config2  B16 T4096 H32 D128 window 256, R2 (--G in {1,4,32})
   config3  B4  T4096 H32 D128 full causal, G4, R2
   config4  B64 T8192 H32 D128 window 256, G1, R2, batch split over the ranks
@@ -42,7 +42,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 WORKLOADS = {
-    "config1": dict(B=16, T=4096, H=32, D=128, window=128, G=1, R=1),
+    "config1": dict(B=16, T=4096, H=32, D=128, window=128, G=8, R=1),
     "config2": dict(B=16, T=4096, H=32, D=128, window=256, G=1, R=2),
     "config3": dict(B=4, T=4096, H=32, D=128, window=None, G=4, R=2),
     "config4": dict(B=64, T=8192, H=32, D=128, window=256, G=1, R=2),

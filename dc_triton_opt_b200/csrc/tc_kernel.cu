@@ -1,22 +1,658 @@
-// Tensor-core (tcgen05/TMEM/TMA) DC-attention forward — placeholder until the
-// kernel lands; AUTO dispatch uses the SIMT kernel meanwhile.
+// Tensor-core DC-attention forward for windowed layers (sm_100a: TMA, tcgen05, TMEM).
+//
+// One CTA owns (query block of BM queries, batch b, head group g) for all
+// HPG heads of the group, BM * HPG = 128.  The block's key span
+// [q0 + BM - 128*NKT, q0 + BM) is cut into NKT key tiles of 128 keys.
+//
+// Layout choice: keys on TMEM lanes, (head, query) pairs on TMEM columns.
+//   S^T_h = K_h Q_h^T     A = K tile [128 keys x D]  (K-major, TMA 128B swizzle)
+//                         B = Q_h    [BM x D]        (K-major, TMA 128B swizzle)
+//                         D = TMEM lanes = keys, columns kt*128 + h*BM + i
+//   O^T_h = V_h^T P'^T_h  A = V tile [128 keys x D]  (MN-major: d contiguous)
+//                         B = P'_h   [keys x BM]     (MN-major, written by threads)
+//                         D = TMEM lanes = d, columns 128*NKT + h*BM + i
+// so one thread (= one key) holds the logits of every head and query of the
+// block at its key: the cross-head composition of DC attention
+// (dc_attention_torch.py:217-225 and :240-248) is thread-local, and the
+// softmax over keys is a cross-lane reduction (redux.sync.max for the max,
+// a shuffle transpose-reduce for the sum) plus a cross-warp pass in SMEM.
+//
+// Warp roles: warps 0 .. 4*NKT-1 compose (warp w: key tile w/4, TMEM lane
+// quarter w%4); the last warp's lane 0 issues TMA loads and tcgen05.mma.
+// Phases: QK (all heads, all key tiles) -> pre-compose + mask + max ->
+// exp + sum -> normalise + post-compose -> P' to SMEM -> PV -> epilogue.
+// Every mbarrier wait is bounded; on timeout the kernel records an error code
+// in err_flag and skips the remaining work instead of hanging.
+
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <string>
 
 #include "common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace dcattn {
+namespace tc {
+
+constexpr int NQ = 128;          // (head, query) columns per CTA
+constexpr int KT_ROWS = 128;     // keys per key tile (TMEM lanes)
+constexpr int TILE_BYTES = KT_ROWS * 128 * 2;  // one K or V tile: 128 rows x 128 d x 2 B
+constexpr int D = 128;
+
+enum Err { ERR_TIMEOUT_Q = 1, ERR_TIMEOUT_FULL = 2, ERR_TIMEOUT_FREE = 3, ERR_TIMEOUT_S = 4,
+           ERR_TIMEOUT_P = 5, ERR_TIMEOUT_O = 6 };
+
+struct Geo {
+  int nkt, nslot;
+  int q_off, ring_off, p_off, misc_off;
+  int wz_off, rec_off, red_off, mrow_off, linv_off, bar_off, tmem_off;
+  int rec_floats;  // per (set, query) record: dq[HPG] | qa[HPG*R] | qb[R*HPG], padded to 4
+  int total;
+};
+
+__host__ __device__ constexpr int round_up(int x, int a) { return (x + a - 1) / a * a; }
+
+__host__ __device__ inline Geo make_geo(int HPG, int R, int nkt) {
+  Geo g{};
+  const int BM = NQ / HPG;
+  g.nkt = nkt;
+  g.nslot = nkt == 3 ? 2 : 3;
+  g.q_off = 0;
+  g.ring_off = g.q_off + NQ * 256;
+  g.p_off = g.ring_off + g.nslot * TILE_BYTES;
+  g.misc_off = g.p_off + nkt * NQ * KT_ROWS * 2;
+  g.rec_floats = round_up(HPG * (2 * R + 1), 4);
+  int o = g.misc_off;
+  g.wz_off = o;   o += 2 * HPG * HPG * 4;
+  g.rec_off = round_up(o, 16); o = g.rec_off + 2 * BM * g.rec_floats * 4;
+  g.red_off = o;  o += 4 * nkt * NQ * 4;
+  g.mrow_off = o; o += NQ * 4;
+  g.linv_off = o; o += NQ * 4;
+  g.bar_off = round_up(o, 8); o = g.bar_off + 16 * 8;
+  g.tmem_off = o; o += 16;
+  g.total = o;
+  return g;
+}
+
+struct TermPtrs {
+  int identity;
+  const float *w;
+  const void *qw1, *qw2, *kw1, *kw2, *qdd, *kdd;
+};
+
+struct TcParams {
+  int B, T, H, G, window, slen_default;
+  float scale;
+  const int32_t *seq_lens;
+  void *out;
+  int64_t out_sb, out_st, out_sh;
+  int32_t *err_flag;
+  float *dbg;  // development hook: raw QK tile of CTA (0,0); NULL in the library
+  TermPtrs pre, post;
+};
+
+float *g_debug_dump = nullptr;  // set only by development harnesses
+
+__device__ int g_default_err;  // error sink when the caller passes no err_flag
+
+__device__ __forceinline__ void record_err(const TcParams &p, int code) {
+  int *dst = p.err_flag ? p.err_flag : &g_default_err;
+  atomicCAS(dst, 0, code);
+}
+
+// Composition of one (query, key) pair across the HPG heads of a group.
+// a: per-head inputs; Wz: static mix with zero diagonal; rec: per-query record
+// (dq = w[h,h] + identity + qdd[t,h]; qa = qw1[t,:,r]; qb = qw2[t,r,:]);
+// kw1/kw2/kdd: per-key weights of this thread's key.
+template <int HPG, int R>
+__device__ __forceinline__ void compose(const float (&a)[HPG], float (&o)[HPG], const float (&Wz)[HPG * HPG],
+                                        const float *rec, const float (&kw1)[HPG * R],
+                                        const float (&kw2)[R * HPG], const float (&kdd)[HPG]) {
+  float r4[round_up(HPG * (2 * R + 1), 4)];
+#pragma unroll
+  for (int j = 0; j < round_up(HPG * (2 * R + 1), 4); j += 4) {
+    const float4 x = *reinterpret_cast<const float4 *>(rec + j);
+    r4[j] = x.x; r4[j + 1] = x.y; r4[j + 2] = x.z; r4[j + 3] = x.w;
+  }
+  const float *dq = r4, *qa = r4 + HPG, *qb = r4 + HPG + HPG * R;
+  float aq[R], ak[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) { aq[r] = 0.f; ak[r] = 0.f; }
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      aq[r] = fmaf(qa[h * R + r], a[h], aq[r]);
+      ak[r] = fmaf(kw1[h * R + r], a[h], ak[r]);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) {
+    float x = (dq[h] + kdd[h]) * a[h];
+#pragma unroll
+    for (int hp = 0; hp < HPG; ++hp)
+      if (hp != h) x = fmaf(Wz[hp * HPG + h], a[hp], x);
+#pragma unroll
+    for (int r = 0; r < R; ++r) x = fmaf(qb[r * HPG + h], aq[r], fmaf(kw2[r * HPG + h], ak[r], x));
+    o[h] = x;
+  }
+}
+
+template <typename E>
+__device__ __forceinline__ float ld_w(const void *base, int64_t idx) {
+  return to_f<E>(reinterpret_cast<const E *>(base)[idx]);
+}
+
+template <typename E, int HPG, int R>
+__device__ __forceinline__ void load_key_weights(const TermPtrs &tm, int64_t tok, int H, int hbase, bool ok,
+                                                 float (&kw1)[HPG * R], float (&kw2)[R * HPG],
+                                                 float (&kdd)[HPG]) {
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      kw1[h * R + r] = (ok && tm.kw1) ? ld_w<E>(tm.kw1, (tok * H + hbase + h) * R + r) : 0.f;
+      kw2[r * HPG + h] = (ok && tm.kw2) ? ld_w<E>(tm.kw2, (tok * R + r) * H + hbase + h) : 0.f;
+    }
+    kdd[h] = (ok && tm.kdd) ? ld_w<E>(tm.kdd, tok * H + hbase + h) : 0.f;
+  }
+}
+
+template <typename E, int HPG, int R, int MAXT>
+__global__ void __launch_bounds__(MAXT, 1)
+    dc_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                 const __grid_constant__ CUtensorMap tm_v, const TcParams p, const int nkt) {
+  constexpr int BM = NQ / HPG;
+  constexpr int GI = 32 / HPG;  // queries per 32-value group
+  constexpr int NG = BM / GI;   // groups per pass (= 4)
+  static_assert(NG == 4, "group geometry");
+
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                          ~static_cast<uintptr_t>(1023));
+  const Geo geo = make_geo(HPG, R, nkt);
+  float *Wz = reinterpret_cast<float *>(smem + geo.wz_off);      // [2][HPG*HPG]
+  float *rec = reinterpret_cast<float *>(smem + geo.rec_off);    // [2][BM][rec_floats]
+  float *red = reinterpret_cast<float *>(smem + geo.red_off);    // [4*nkt][NQ]
+  float *mrow = reinterpret_cast<float *>(smem + geo.mrow_off);  // [NQ]
+  float *linv = reinterpret_cast<float *>(smem + geo.linv_off);  // [NQ]
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + geo.bar_off);
+  uint64_t *bar_q = bars + 0, *bar_full = bars + 1, *bar_free = bars + 4;
+  uint64_t *bar_S = bars + 7, *bar_P = bars + 8, *bar_O = bars + 9;
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + geo.tmem_off);
+
+  const int ncompose_warps = 4 * nkt;
+  const int ctrl_warp = ncompose_warps;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int b = blockIdx.y / p.G, g = blockIdx.y % p.G;
+  const int q0 = blockIdx.x * BM;
+  const int H = p.H, T = p.T, hbase = g * HPG;
+  const int kb = q0 + BM - KT_ROWS * nkt;  // first key of key tile 0
+  const int slen = p.seq_lens ? min(max(p.seq_lens[b], 0), T) : T;
+
+  // ---- stage the static mix and the per-query weights (fp32) in SMEM
+  for (int idx = threadIdx.x; idx < 2 * HPG * HPG; idx += blockDim.x) {
+    const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
+    const TermPtrs &tm = set ? p.post : p.pre;
+    const int hp = j / HPG, h = j % HPG;
+    Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
+  }
+  for (int idx = threadIdx.x; idx < 2 * BM * geo.rec_floats; idx += blockDim.x) {
+    const int set = idx / (BM * geo.rec_floats), rem = idx % (BM * geo.rec_floats);
+    const int i = rem / geo.rec_floats, j = rem % geo.rec_floats;
+    const TermPtrs &tm = set ? p.post : p.pre;
+    const int t = q0 + i;
+    float val = 0.f;
+    if (t < T) {
+      const int64_t tok = (int64_t)b * T + t;
+      if (j < HPG) {
+        const int h = j;
+        val = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)g * HPG + h) * HPG + h] : 0.f) +
+              (tm.qdd ? ld_w<E>(tm.qdd, tok * H + hbase + h) : 0.f);
+      } else if (j < HPG + HPG * R) {
+        const int h = (j - HPG) / R, r = (j - HPG) % R;
+        val = tm.qw1 ? ld_w<E>(tm.qw1, (tok * H + hbase + h) * R + r) : 0.f;
+      } else if (j < HPG + 2 * HPG * R) {
+        const int r = (j - HPG - HPG * R) / HPG, h = (j - HPG - HPG * R) % HPG;
+        val = tm.qw2 ? ld_w<E>(tm.qw2, (tok * R + r) * H + hbase + h) : 0.f;
+      }
+    }
+    rec[idx] = val;
+  }
+  if (threadIdx.x == 0) {
+    ptx::mbar_init(bar_q, 1);
+    for (int i = 0; i < 3; ++i) {
+      ptx::mbar_init(bar_full + i, 1);
+      ptx::mbar_init(bar_free + i, 1);
+    }
+    ptx::mbar_init(bar_S, 1);
+    ptx::mbar_init(bar_P, ncompose_warps);
+    ptx::mbar_init(bar_O, 1);
+    ptx::fence_mbar_init();
+  }
+  if (warp == ctrl_warp) ptx::tmem_alloc(tmem_slot, 512);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t o_col = KT_ROWS * nkt;
+
+  if (warp == ctrl_warp) {
+    // ================================================= TMA + MMA issue (one thread)
+    if (lane == 0) {
+      const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
+      const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 128, BM);
+      const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 128, BM);
+      const uint32_t q_addr = ptx::smem_u32(smem + geo.q_off);
+      const uint32_t ring_addr = ptx::smem_u32(smem + geo.ring_off);
+      const uint32_t p_addr = ptx::smem_u32(smem + geo.p_off);
+      const int nslot = geo.nslot;
+      const int nK = HPG * nkt, total = 2 * nK;
+      bool ok = true;
+      ptx::tma_prefetch_desc(&tm_q);
+      ptx::tma_prefetch_desc(&tm_k);
+      ptx::tma_prefetch_desc(&tm_v);
+      // Q for every head of the group: two 64-column halves of [BM x 64]
+      ptx::mbar_expect_tx(bar_q, NQ * 256);
+      for (int h = 0; h < HPG; ++h)
+        for (int c = 0; c < 2; ++c)
+          ptx::tma_load_4d(smem + geo.q_off + h * BM * 256 + c * BM * 128, &tm_q, bar_q, c * 64, hbase + h, q0, b);
+      auto issue = [&](int j) {
+        const int slot = j % nslot, use = j / nslot;
+        if (use > 0 && ok && !ptx::mbar_wait(bar_free + slot, (use - 1) & 1)) {
+          ok = false;
+          record_err(p, ERR_TIMEOUT_FREE);
+        }
+        if (!ok) return;
+        const CUtensorMap *m = j < nK ? &tm_k : &tm_v;
+        const int jj = j % nK, h = jj / nkt, kt = jj % nkt;
+        ptx::mbar_expect_tx(bar_full + slot, TILE_BYTES);
+        unsigned char *dst = smem + geo.ring_off + slot * TILE_BYTES;
+        ptx::tma_load_4d(dst, m, bar_full + slot, 0, hbase + h, kb + kt * KT_ROWS, b);
+        ptx::tma_load_4d(dst + TILE_BYTES / 2, m, bar_full + slot, 64, hbase + h, kb + kt * KT_ROWS, b);
+      };
+      int issued = 0;
+      for (; issued < nslot && issued < total; ++issued) issue(issued);
+      if (!ptx::mbar_wait(bar_q, 0)) { ok = false; record_err(p, ERR_TIMEOUT_Q); }
+      // ---- S^T_h = K_h Q_h^T for every (head, key tile)
+      for (int j = 0; j < nK && ok; ++j) {
+        const int slot = j % nslot;
+        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
+        ptx::tc_fence_after();
+        const int h = j / nkt, kt = j % nkt;
+        const uint32_t a0 = ring_addr + slot * TILE_BYTES;
+        const uint32_t b0 = q_addr + h * BM * 256;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks) {
+          const uint64_t ad = ptx::smem_desc(a0 + (ks >> 2) * (TILE_BYTES / 2) + (ks & 3) * 32, 16, 1024, 2);
+          const uint64_t bd = ptx::smem_desc(b0 + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 16, 1024, 2);
+          ptx::mma_f16_ss(tbase + kt * KT_ROWS + h * BM, ad, bd, idesc_qk, ks > 0);
+        }
+        ptx::mma_commit(bar_free + slot);
+        if (issued < total) issue(issued++);
+      }
+      ptx::mma_commit(bar_S);
+      // ---- O^T_h = V_h^T P'^T_h, accumulated over key tiles
+      if (ok && !ptx::mbar_wait(bar_P, 0, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_P); }
+      ptx::tc_fence_after();
+      for (int j = nK; j < total && ok; ++j) {
+        const int slot = j % nslot;
+        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
+        ptx::tc_fence_after();
+        const int jj = j - nK, h = jj / nkt, kt = jj % nkt;
+        const uint32_t a0 = ring_addr + slot * TILE_BYTES;
+        const uint32_t b0 = p_addr + (h * nkt + kt) * (KT_ROWS * BM * 2);
+#pragma unroll
+        for (int ks = 0; ks < KT_ROWS / 16; ++ks) {
+          // V tile, MN-major 128B swizzle: 8-key groups 1024 B apart, d halves 16 KB apart
+          const uint64_t ad = ptx::smem_desc(a0 + ks * 2048, TILE_BYTES / 2, 1024, 2);
+          // P' tile, MN-major no swizzle: 8x8 core matrices, query blocks 128 B apart,
+          // 8-key blocks BM*16 B apart
+          const uint64_t bd = ptx::smem_desc(b0 + ks * (2 * BM * 16), BM * 16, 128, 0);
+          ptx::mma_f16_ss(tbase + o_col + h * BM, ad, bd, idesc_pv, (kt > 0 || ks > 0));
+        }
+        ptx::mma_commit(bar_free + slot);
+        if (issued < total) issue(issued++);
+      }
+      ptx::mma_commit(bar_O);
+    }
+    __syncwarp();
+  } else {
+    // ================================================= compose warps
+    const int sub = warp & 3, kt = warp >> 2;
+    const int s_local = 32 * sub + lane;          // key row inside the key tile
+    const int s = kb + kt * KT_ROWS + s_local;    // absolute key index
+    const bool key_ok = s >= 0 && s < slen;
+    const uint32_t tl = tbase + (static_cast<uint32_t>(32 * sub) << 16) + kt * KT_ROWS;
+    // does any (query, key) pair of this warp survive the mask?
+    const int wk0 = kb + kt * KT_ROWS + 32 * sub, wk1 = wk0 + 31;
+    const int klo = max(0, p.window > 0 ? q0 - p.window + 1 : 0), khi = min(q0 + BM - 1, slen - 1);
+    const bool active = wk1 >= klo && wk0 <= khi;
+    const int64_t ktok = (int64_t)b * T + s;
+    // softmax scale folded into the exponent: composition is linear, so
+    // softmax(compose(scale*L)) = softmax(scale*compose(L)) for scale > 0
+    const float sl2e = p.scale * kLog2e;
+    bool ok = true;
+
+    float Wreg[HPG * HPG];
+    float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
+
+    auto valid = [&](int t) { return key_ok && s <= t && t - s < p.window && t < T; };
+
+    if (!ptx::mbar_wait(bar_S, 0)) { ok = false; record_err(p, ERR_TIMEOUT_S); }
+    ptx::tc_fence_after();
+    if (p.dbg && blockIdx.x == 0 && blockIdx.y == 0) {
+#pragma unroll 1
+      for (int c = 0; c < NQ; c += 8) {
+        float v[8];
+        ptx::tmem_ld<8>(tl + c, v);
+        ptx::tmem_wait_ld();
+        for (int j = 0; j < 8; ++j) p.dbg[(kt * KT_ROWS + s_local) * NQ + c + j] = v[j];
+      }
+    }
+
+    // ---- pass A: pre-composition, mask, column max
+    if (active && ok) {
+#pragma unroll
+      for (int j = 0; j < HPG * HPG; ++j) Wreg[j] = Wz[j];
+      load_key_weights<E, HPG, R>(p.pre, ktok, H, hbase, key_ok, kw1, kw2, kdd);
+    }
+#pragma unroll 1
+    for (int grp = 0; grp < NG; ++grp) {
+      const int i0 = grp * GI;
+      float mine = -INFINITY;
+      if (active && ok) {
+        float v[HPG][GI];
+#pragma unroll
+        for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int ii = 0; ii < GI; ++ii) {
+          float a[HPG], o[HPG];
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
+          compose<HPG, R>(a, o, Wreg, rec + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+          const bool vl = valid(q0 + i0 + ii);
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : -INFINITY;
+        }
+#pragma unroll
+        for (int h = 0; h < HPG; ++h) ptx::tmem_st<GI>(tl + h * BM + i0, v[h]);
+#pragma unroll
+        for (int h = 0; h < HPG; ++h)
+#pragma unroll
+          for (int ii = 0; ii < GI; ++ii) {
+            const float r = ptx::warp_max(v[h][ii]);
+            if (lane == h * GI + ii) mine = r;
+          }
+      }
+      red[warp * NQ + (lane / GI) * BM + i0 + (lane % GI)] = mine;
+    }
+    ptx::tmem_wait_st();
+    ptx::named_bar_sync(1, 32 * ncompose_warps);
+    if (threadIdx.x < NQ) {
+      float m = -INFINITY;
+      for (int w = 0; w < ncompose_warps; ++w) m = fmaxf(m, red[w * NQ + threadIdx.x]);
+      mrow[threadIdx.x] = m == -INFINITY ? 0.f : m * sl2e;
+    }
+    ptx::named_bar_sync(1, 32 * ncompose_warps);
+
+    // ---- pass B: e = exp(S - m), column sums
+#pragma unroll 1
+    for (int grp = 0; grp < NG; ++grp) {
+      const int i0 = grp * GI;
+      float mine = 0.f;
+      if (active && ok) {
+        float v[HPG][GI];
+#pragma unroll
+        for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
+        ptx::tmem_wait_ld();
+        float x[32];
+#pragma unroll
+        for (int h = 0; h < HPG; ++h)
+#pragma unroll
+          for (int ii = 0; ii < GI; ++ii) {
+            const float e = exp2f(fmaf(v[h][ii], sl2e, -mrow[h * BM + i0 + ii]));
+            v[h][ii] = e;
+            x[h * GI + ii] = e;
+          }
+#pragma unroll
+        for (int h = 0; h < HPG; ++h) ptx::tmem_st<GI>(tl + h * BM + i0, v[h]);
+        // transpose-reduce: afterwards lane L holds the column sum of value L
+#pragma unroll
+        for (int off = 16, cnt = 32; off >= 1; off >>= 1, cnt >>= 1) {
+          const bool upper = (lane & off) != 0;
+#pragma unroll
+          for (int j = 0; j < cnt / 2; ++j) {
+            const float send = upper ? x[j] : x[j + cnt / 2];
+            const float keep = upper ? x[j + cnt / 2] : x[j];
+            x[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+          }
+        }
+        mine = x[0];
+      }
+      red[warp * NQ + (lane / GI) * BM + i0 + (lane % GI)] = mine;
+    }
+    ptx::tmem_wait_st();
+    ptx::named_bar_sync(1, 32 * ncompose_warps);
+    if (threadIdx.x < NQ) {
+      float l = 0.f;
+      for (int w = 0; w < ncompose_warps; ++w) l += red[w * NQ + threadIdx.x];
+      linv[threadIdx.x] = l > 0.f ? 1.f / l : 0.f;
+    }
+    ptx::named_bar_sync(1, 32 * ncompose_warps);
+
+    // ---- pass C: normalise, post-composition, P' -> SMEM (PV B operand)
+    if (active && ok) {
+#pragma unroll
+      for (int j = 0; j < HPG * HPG; ++j) Wreg[j] = Wz[HPG * HPG + j];
+      load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
+    }
+    unsigned char *prow = smem + geo.p_off + (s_local & 7) * 16 + (s_local >> 3) * (BM * 16);
+#pragma unroll 1
+    for (int grp = 0; grp < NG; ++grp) {
+      const int i0 = grp * GI;
+      float v[HPG][GI];
+      if (active && ok) {
+#pragma unroll
+        for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int ii = 0; ii < GI; ++ii) {
+          float a[HPG], o[HPG];
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * linv[h * BM + i0 + ii];
+          compose<HPG, R>(a, o, Wreg, rec + (BM + i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < HPG; ++h)
+#pragma unroll
+          for (int ii = 0; ii < GI; ++ii) v[h][ii] = 0.f;
+      }
+#pragma unroll
+      for (int h = 0; h < HPG; ++h) {
+        unsigned char *tile = prow + (h * nkt + kt) * (KT_ROWS * BM * 2);
+#pragma unroll
+        for (int c = 0; c < GI; c += 8 < GI ? 8 : GI) {
+          // up to 8 queries -> one 16-byte row of an 8x8 core matrix
+          constexpr int W8 = GI < 8 ? GI : 8;
+          uint32_t pk[W8 / 2];
+#pragma unroll
+          for (int u = 0; u < W8 / 2; ++u) {
+            const E lo = from_f<E>(v[h][c + 2 * u]), hi = from_f<E>(v[h][c + 2 * u + 1]);
+            pk[u] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&lo)) |
+                    (static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&hi)) << 16);
+          }
+          const int i = i0 + c;
+          unsigned char *dst = tile + (i >> 3) * 128 + (i & 7) * 2;
+          if constexpr (W8 == 8) {
+            *reinterpret_cast<uint4 *>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+          } else if constexpr (W8 == 4) {
+            *reinterpret_cast<uint2 *>(dst) = make_uint2(pk[0], pk[1]);
+          } else {
+            *reinterpret_cast<uint32_t *>(dst) = pk[0];
+          }
+        }
+      }
+    }
+    if (p.dbg && blockIdx.x == 0 && blockIdx.y == 0) {
+      // P' as this thread wrote it: dbg[3*128*128 + ((h*nkt + kt)*128 + s_local)*BM + i]
+      for (int h = 0; h < HPG; ++h)
+        for (int i = 0; i < BM; ++i) {
+          const E *e = reinterpret_cast<const E *>(prow + (h * nkt + kt) * (KT_ROWS * BM * 2) + (i >> 3) * 128 +
+                                                   (i & 7) * 2);
+          p.dbg[3 * 128 * 128 + ((h * nkt + kt) * 128 + s_local) * BM + i] = to_f<E>(*e);
+        }
+    }
+    ptx::fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(bar_P);
+
+    // ---- epilogue: O^T (lanes = d) -> out[b, t, h, d]
+    if (!ptx::mbar_wait(bar_O, 0, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_O); }
+    ptx::tc_fence_after();
+    E *out = reinterpret_cast<E *>(p.out);
+    const int d = 32 * sub + lane;
+    if (ok) {
+#pragma unroll 1
+      for (int c = kt; c < NQ / 8; c += nkt) {
+        float v[8];
+        ptx::tmem_ld<8>(tbase + (static_cast<uint32_t>(32 * sub) << 16) + o_col + 8 * c, v);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const int col = 8 * c + jj, h = col / BM, i = col % BM, t = q0 + i;
+          if (t < T)
+            out[(int64_t)b * p.out_sb + (int64_t)t * p.out_st + (int64_t)(hbase + h) * p.out_sh + d] =
+                from_f<E>(v[jj]);
+        }
+      }
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == ctrl_warp) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tbase, 512);
+  }
+}
+
+// ------------------------------------------------------------------ host side
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// [B, T, H, D] tensor as a 4-D map (D, H, T, B); box = 64 d x 1 head x rows x 1.
+static bool make_map(CUtensorMap *m, const void *base, int dtype, int B, int T, int H, int rows) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)H * D * 2, (cuuint64_t)T * H * D * 2};
+  const cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == DC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(m, dt, 4, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+static int num_key_tiles(int HPG, int window) {
+  const int BM = NQ / HPG;
+  return (BM + window - 1 + KT_ROWS - 1) / KT_ROWS;
+}
+
+static TermPtrs to_ptrs(const dc_terms &t) {
+  TermPtrs r;
+  r.identity = t.identity;
+  r.w = t.w;
+  r.qw1 = t.qw1; r.qw2 = t.qw2; r.kw1 = t.kw1; r.kw2 = t.kw2; r.qdd = t.qdd; r.kdd = t.kdd;
+  return r;
+}
+
+template <typename E, int HPG, int R>
+static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
+  constexpr int BM = NQ / HPG;
+  const int nkt = num_key_tiles(HPG, p.window);
+  const Geo geo = make_geo(HPG, R, nkt);
+  const size_t smem = geo.total + 1024;
+  CUtensorMap mq, mk, mv;
+  if (!make_map(&mq, p.q, p.dtype, p.B, p.T, p.H, BM) || !make_map(&mk, p.k, p.dtype, p.B, p.T, p.H, KT_ROWS) ||
+      !make_map(&mv, p.v, p.dtype, p.B, p.T, p.H, KT_ROWS))
+    return cudaErrorInvalidValue;
+  TcParams tp;
+  tp.B = p.B; tp.T = p.T; tp.H = p.H; tp.G = p.G; tp.window = p.window; tp.slen_default = p.T;
+  tp.scale = p.scale;
+  tp.seq_lens = p.seq_lens;
+  tp.out = p.out;
+  tp.out_sb = p.out_sb; tp.out_st = p.out_st; tp.out_sh = p.out_sh;
+  tp.err_flag = p.err_flag;
+  tp.dbg = g_debug_dump;
+  tp.pre = to_ptrs(p.pre);
+  tp.post = to_ptrs(p.post);
+  auto kern = nkt <= 2 ? dc_tc_kernel<E, HPG, R, 288> : dc_tc_kernel<E, HPG, R, 416>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((p.T + BM - 1) / BM, p.B * p.G);
+  dim3 block(32 * (4 * nkt + 1));
+  kern<<<grid, block, smem, st>>>(mq, mk, mv, tp, nkt);
+  return cudaGetLastError();
+}
+
+template <typename E, int HPG>
+static cudaError_t launch_r(const dc_attn_params &p, cudaStream_t st) {
+  return p.R <= 1 ? launch_t<E, HPG, 1>(p, st) : launch_t<E, HPG, 2>(p, st);
+}
+
+template <typename E>
+static cudaError_t launch_e(const dc_attn_params &p, cudaStream_t st) {
+  switch (p.H / p.G) {
+    case 1: return launch_r<E, 1>(p, st);
+    case 2: return launch_r<E, 2>(p, st);
+    case 4: return launch_r<E, 4>(p, st);
+    case 8: return launch_r<E, 8>(p, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace tc
 
 bool tc_supports(const dc_attn_params &p, std::string *why) {
-  (void)p;
-  if (why) *why = "tensor-core kernel not built";
-  return false;
+  auto no = [&](const char *m) { if (why) *why = m; return false; };
+  const int HPG = p.H / p.G;
+  if (p.D != 128) return no("D must be 128");
+  if (HPG != 1 && HPG != 2 && HPG != 4 && HPG != 8) return no("heads per group must be 1, 2, 4 or 8");
+  if (p.window <= 0) return no("full-causal layers use the SIMT kernel");
+  if (tc::num_key_tiles(HPG, p.window) > 3) return no("window too large (BM + window - 1 > 384)");
+  if (p.R > 2) return no("rank R > 2");
+  if (!(p.scale > 0.f)) return no("non-positive softmax scale");
+  if (p.pre.qmat || p.post.qmat) return no("per-query mixing matrices use the SIMT kernel");
+  auto al = [](const void *x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
+  if (!al(p.q) || !al(p.k) || !al(p.v)) return no("q, k, v must be 16-byte aligned");
+  return true;
 }
 
 cudaError_t launch_tc(const dc_attn_params &p, cudaStream_t st) {
-  (void)p; (void)st;
-  return cudaErrorNotSupported;
+  if (p.dtype == DC_DTYPE_BF16) return tc::launch_e<__nv_bfloat16>(p, st);
+  return tc::launch_e<__half>(p, st);
 }
 
 }  // namespace dcattn

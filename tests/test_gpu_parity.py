@@ -218,3 +218,26 @@ def test_stream_semantics():
         got = dc.dc_attention_window_chunked_residual_grouped(q, k, v, ws, 0.1, 64, G=8)
     s.synchronize()
     assert torch.equal(ref, got)
+
+
+@pytest.mark.parametrize("G,window,expect", [(8, 128, "tc"), (4, 256, "tc"), (32, 128, "tc"), (16, 200, "tc"),
+                                              (1, 128, "simt"), (8, None, "simt")])
+def test_auto_dispatch(G, window, expect):
+    """AUTO runs the tensor-core kernel for windowed layers with <= 8 heads per group."""
+    q = torch.empty(1, 64, 32, 128, dtype=torch.bfloat16, device=DEV)
+    pre = dc.DCTerms(qw1=torch.empty(1, 64, 32, 1, dtype=torch.bfloat16, device=DEV),
+                     qw2=torch.empty(1, 64, 1, 32, dtype=torch.bfloat16, device=DEV))
+    assert dc.select_kernel(q, q, q, pre, pre, window, G) == expect
+
+
+@pytest.mark.parametrize("G,R,window,T", [(8, 1, 128, 320), (4, 2, 256, 300), (32, 1, 96, 200), (32, 2, 128, 260),
+                                          (16, 1, 240, 280), (8, 2, 1, 64)])
+def test_tc_kernel_vs_oracle(G, R, window, T):
+    """Tensor-core kernel, every term, ragged T, BASELINE distributions."""
+    dt = torch.bfloat16
+    q, k, v, pre, post = O.make_inputs(1, T, 32, 128, G, R, seed=G * 7 + R)
+    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, window, G, None)
+    got = run_general(q, k, v, pre, post, 128 ** -0.5, window, G, None, "bf16", "tc")
+    assert_close(got, ref, f"tc G{G} R{R} W{window} T{T}")
