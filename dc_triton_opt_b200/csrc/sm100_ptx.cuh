@@ -79,6 +79,19 @@ __device__ __forceinline__ void tma_load_4d(void *dst, const CUtensorMap *m, uin
       : "memory");
 }
 
+// 4-D tiled store from shared memory (bulk-group completion).  Rows outside
+// the tensor are clipped by the hardware; coordinates must be non-negative.
+__device__ __forceinline__ void tma_store_4d(const CUtensorMap *m, const void *src, int c0, int c1, int c2, int c3) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(m)),
+      "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Wait until the shared-memory sources of all committed bulk stores were read.
+__device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+
 // ---------------------------------------------------------------- TMEM
 // Warp-wide: allocate `ncols` TMEM columns, address written to *dst (smem).
 __device__ __forceinline__ void tmem_alloc(uint32_t *dst, uint32_t ncols) {

@@ -46,7 +46,7 @@ enum Err { ERR_TIMEOUT_Q = 1, ERR_TIMEOUT_FULL = 2, ERR_TIMEOUT_FREE = 3, ERR_TI
 struct Geo {
   int nkt, nslot;
   int q_off, ring_off, p_off, misc_off;
-  int wz_off, rec_off, red_off, mrow_off, linv_off, bar_off, tmem_off;
+  int wz_off, rec_off, red_off, bar_off, tmem_off;
   int rec_floats;  // per (set, query) record: dq[HPG] | qa[HPG*R] | qb[R*HPG], padded to 4
   int total;
 };
@@ -66,9 +66,7 @@ __host__ __device__ inline Geo make_geo(int HPG, int R, int nkt) {
   int o = g.misc_off;
   g.wz_off = o;   o += 2 * HPG * HPG * 4;
   g.rec_off = round_up(o, 16); o = g.rec_off + 2 * BM * g.rec_floats * 4;
-  g.red_off = o;  o += 4 * nkt * NQ * 4;
-  g.mrow_off = o; o += NQ * 4;
-  g.linv_off = o; o += NQ * 4;
+  g.red_off = o;  o += 2 * 4 * nkt * NQ * 4;
   g.bar_off = round_up(o, 8); o = g.bar_off + 16 * 8;
   g.tmem_off = o; o += 16;
   g.total = o;
@@ -88,13 +86,24 @@ struct TcParams {
   void *out;
   int64_t out_sb, out_st, out_sh;
   int32_t *err_flag;
-  float *dbg;  // development hook: raw QK tile of CTA (0,0); NULL in the library
   TermPtrs pre, post;
 };
 
-float *g_debug_dump = nullptr;  // set only by development harnesses
+__device__ int g_default_err;
 
-__device__ int g_default_err;  // error sink when the caller passes no err_flag
+#ifdef DC_TIMELINE
+// development builds only: per-CTA clock64 stamps of the phases
+__device__ unsigned long long g_timeline[8192][40];
+#define TL_STAMP(i)                                                                   \
+  do {                                                                                \
+    const int cta_ = blockIdx.y * gridDim.x + blockIdx.x;                             \
+    if (cta_ < 8192) g_timeline[cta_][i] = clock64();                                 \
+  } while (0)
+#else
+#define TL_STAMP(i) \
+  do {              \
+  } while (0)
+#endif  // error sink when the caller passes no err_flag
 
 __device__ __forceinline__ void record_err(const TcParams &p, int code) {
   int *dst = p.err_flag ? p.err_flag : &g_default_err;
@@ -159,14 +168,16 @@ __device__ __forceinline__ void load_key_weights(const TermPtrs &tm, int64_t tok
   }
 }
 
-template <typename E, int HPG, int R, int MAXT>
+template <typename E, int HPG, int R, int CS, int MAXT>
 __global__ void __launch_bounds__(MAXT, 1)
     dc_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                 const __grid_constant__ CUtensorMap tm_v, const TcParams p, const int nkt) {
+                 const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kl,
+                 const __grid_constant__ CUtensorMap tm_vl, const __grid_constant__ CUtensorMap tm_o,
+                 const TcParams p, const int nkt, const int rlast) {
   constexpr int BM = NQ / HPG;
   constexpr int GI = 32 / HPG;  // queries per 32-value group
-  constexpr int NG = BM / GI;   // groups per pass (= 4)
-  static_assert(NG == 4, "group geometry");
+  constexpr int NG = BM / GI;   // groups per key tile (= 4)
+  static_assert(NG == 4 && NG % CS == 0, "group geometry");
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -174,59 +185,32 @@ __global__ void __launch_bounds__(MAXT, 1)
   const Geo geo = make_geo(HPG, R, nkt);
   float *Wz = reinterpret_cast<float *>(smem + geo.wz_off);      // [2][HPG*HPG]
   float *rec = reinterpret_cast<float *>(smem + geo.rec_off);    // [2][BM][rec_floats]
-  float *red = reinterpret_cast<float *>(smem + geo.red_off);    // [4*nkt][NQ]
-  float *mrow = reinterpret_cast<float *>(smem + geo.mrow_off);  // [NQ]
-  float *linv = reinterpret_cast<float *>(smem + geo.linv_off);  // [NQ]
+  float *red = reinterpret_cast<float *>(smem + geo.red_off);    // [2][4*nkt][NQ]
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + geo.bar_off);
   uint64_t *bar_q = bars + 0, *bar_full = bars + 1, *bar_free = bars + 4;
-  uint64_t *bar_S = bars + 7, *bar_P = bars + 8, *bar_O = bars + 9;
+  uint64_t *bar_S = bars + 7 /* [3] */, *bar_P = bars + 10, *bar_O = bars + 11;
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + geo.tmem_off);
 
-  const int ncompose_warps = 4 * nkt;
+  const int ncompose_warps = 4 * nkt * CS;
+  const int ncompose = 32 * ncompose_warps;
   const int ctrl_warp = ncompose_warps;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int b = blockIdx.y / p.G, g = blockIdx.y % p.G;
   const int q0 = blockIdx.x * BM;
   const int H = p.H, T = p.T, hbase = g * HPG;
-  const int kb = q0 + BM - KT_ROWS * nkt;  // first key of key tile 0
+  // key span of the block: [q0 - window + 1, q0 + BM); tile kt covers
+  // [kb + 128 kt, kb + 128 kt + 128), the last tile only its first rlast rows
+  const int kb = q0 - p.window + 1;
   const int slen = p.seq_lens ? min(max(p.seq_lens[b], 0), T) : T;
+  if (threadIdx.x == 0) TL_STAMP(0);
 
-  // ---- stage the static mix and the per-query weights (fp32) in SMEM
-  for (int idx = threadIdx.x; idx < 2 * HPG * HPG; idx += blockDim.x) {
-    const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
-    const TermPtrs &tm = set ? p.post : p.pre;
-    const int hp = j / HPG, h = j % HPG;
-    Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
-  }
-  for (int idx = threadIdx.x; idx < 2 * BM * geo.rec_floats; idx += blockDim.x) {
-    const int set = idx / (BM * geo.rec_floats), rem = idx % (BM * geo.rec_floats);
-    const int i = rem / geo.rec_floats, j = rem % geo.rec_floats;
-    const TermPtrs &tm = set ? p.post : p.pre;
-    const int t = q0 + i;
-    float val = 0.f;
-    if (t < T) {
-      const int64_t tok = (int64_t)b * T + t;
-      if (j < HPG) {
-        const int h = j;
-        val = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)g * HPG + h) * HPG + h] : 0.f) +
-              (tm.qdd ? ld_w<E>(tm.qdd, tok * H + hbase + h) : 0.f);
-      } else if (j < HPG + HPG * R) {
-        const int h = (j - HPG) / R, r = (j - HPG) % R;
-        val = tm.qw1 ? ld_w<E>(tm.qw1, (tok * H + hbase + h) * R + r) : 0.f;
-      } else if (j < HPG + 2 * HPG * R) {
-        const int r = (j - HPG - HPG * R) / HPG, h = (j - HPG - HPG * R) % HPG;
-        val = tm.qw2 ? ld_w<E>(tm.qw2, (tok * R + r) * H + hbase + h) : 0.f;
-      }
-    }
-    rec[idx] = val;
-  }
   if (threadIdx.x == 0) {
     ptx::mbar_init(bar_q, 1);
     for (int i = 0; i < 3; ++i) {
       ptx::mbar_init(bar_full + i, 1);
       ptx::mbar_init(bar_free + i, 1);
+      ptx::mbar_init(bar_S + i, 1);
     }
-    ptx::mbar_init(bar_S, 1);
     ptx::mbar_init(bar_P, ncompose_warps);
     ptx::mbar_init(bar_O, 1);
     ptx::fence_mbar_init();
@@ -237,9 +221,42 @@ __global__ void __launch_bounds__(MAXT, 1)
   ptx::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   const uint32_t o_col = KT_ROWS * nkt;
+  if (threadIdx.x == 0) TL_STAMP(1);
 
   if (warp == ctrl_warp) {
-    // ================================================= TMA + MMA issue (one thread)
+    // ================================================= TMA producer (one thread)
+    if (lane == 0) {
+      const int nslot = geo.nslot;
+      const int nK = HPG * nkt, total = 2 * nK;
+      ptx::tma_prefetch_desc(&tm_q);
+      ptx::tma_prefetch_desc(&tm_k);
+      ptx::tma_prefetch_desc(&tm_v);
+      // Q for every head of the group: two 64-column halves of [BM x 64]
+      ptx::mbar_expect_tx(bar_q, NQ * 256);
+      for (int h = 0; h < HPG; ++h)
+        for (int c = 0; c < 2; ++c)
+          ptx::tma_load_4d(smem + geo.q_off + h * BM * 256 + c * BM * 128, &tm_q, bar_q, c * 64, hbase + h, q0, b);
+      // jobs are key-tile major: job j -> key tile j / HPG, head j % HPG; K jobs then V jobs
+      for (int j = 0; j < total; ++j) {
+        const int slot = j % nslot, use = j / nslot;
+        if (use > 0 && !ptx::mbar_wait(bar_free + slot, (use - 1) & 1, 1u << 26)) {
+          record_err(p, ERR_TIMEOUT_FREE);
+          break;
+        }
+        const bool isv = j >= nK;
+        const int jj = j % nK, kt = jj / HPG, h = jj % HPG;
+        const bool last = kt == nkt - 1;
+        const CUtensorMap *m = isv ? (last ? &tm_vl : &tm_v) : (last ? &tm_kl : &tm_k);
+        const int rows = last ? rlast : KT_ROWS;
+        ptx::mbar_expect_tx(bar_full + slot, rows * 256);
+        unsigned char *dst = smem + geo.ring_off + slot * TILE_BYTES;
+        ptx::tma_load_4d(dst, m, bar_full + slot, 0, hbase + h, kb + kt * KT_ROWS, b);
+        ptx::tma_load_4d(dst + TILE_BYTES / 2, m, bar_full + slot, 64, hbase + h, kb + kt * KT_ROWS, b);
+      }
+    }
+    __syncwarp();
+  } else if (warp == ctrl_warp + 1) {
+    // ================================================= MMA issuer (one thread)
     if (lane == 0) {
       const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
       const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 128, BM);
@@ -250,37 +267,15 @@ __global__ void __launch_bounds__(MAXT, 1)
       const int nslot = geo.nslot;
       const int nK = HPG * nkt, total = 2 * nK;
       bool ok = true;
-      ptx::tma_prefetch_desc(&tm_q);
-      ptx::tma_prefetch_desc(&tm_k);
-      ptx::tma_prefetch_desc(&tm_v);
-      // Q for every head of the group: two 64-column halves of [BM x 64]
-      ptx::mbar_expect_tx(bar_q, NQ * 256);
-      for (int h = 0; h < HPG; ++h)
-        for (int c = 0; c < 2; ++c)
-          ptx::tma_load_4d(smem + geo.q_off + h * BM * 256 + c * BM * 128, &tm_q, bar_q, c * 64, hbase + h, q0, b);
-      auto issue = [&](int j) {
-        const int slot = j % nslot, use = j / nslot;
-        if (use > 0 && ok && !ptx::mbar_wait(bar_free + slot, (use - 1) & 1)) {
-          ok = false;
-          record_err(p, ERR_TIMEOUT_FREE);
-        }
-        if (!ok) return;
-        const CUtensorMap *m = j < nK ? &tm_k : &tm_v;
-        const int jj = j % nK, h = jj / nkt, kt = jj % nkt;
-        ptx::mbar_expect_tx(bar_full + slot, TILE_BYTES);
-        unsigned char *dst = smem + geo.ring_off + slot * TILE_BYTES;
-        ptx::tma_load_4d(dst, m, bar_full + slot, 0, hbase + h, kb + kt * KT_ROWS, b);
-        ptx::tma_load_4d(dst + TILE_BYTES / 2, m, bar_full + slot, 64, hbase + h, kb + kt * KT_ROWS, b);
-      };
-      int issued = 0;
-      for (; issued < nslot && issued < total; ++issued) issue(issued);
-      if (!ptx::mbar_wait(bar_q, 0)) { ok = false; record_err(p, ERR_TIMEOUT_Q); }
-      // ---- S^T_h = K_h Q_h^T for every (head, key tile)
+      if (!ptx::mbar_wait(bar_q, 0, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_Q); }
+      TL_STAMP(2);
+      // ---- S^T_h = K_h Q_h^T; key tile kt is signalled as soon as its heads are issued
       for (int j = 0; j < nK && ok; ++j) {
         const int slot = j % nslot;
-        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
+        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
+        if (j < 12) TL_STAMP(12 + j);
         ptx::tc_fence_after();
-        const int h = j / nkt, kt = j % nkt;
+        const int kt = j / HPG, h = j % HPG;
         const uint32_t a0 = ring_addr + slot * TILE_BYTES;
         const uint32_t b0 = q_addr + h * BM * 256;
 #pragma unroll
@@ -290,21 +285,22 @@ __global__ void __launch_bounds__(MAXT, 1)
           ptx::mma_f16_ss(tbase + kt * KT_ROWS + h * BM, ad, bd, idesc_qk, ks > 0);
         }
         ptx::mma_commit(bar_free + slot);
-        if (issued < total) issue(issued++);
+        if (h == HPG - 1) ptx::mma_commit(bar_S + kt);
       }
-      ptx::mma_commit(bar_S);
+      TL_STAMP(3);
       // ---- O^T_h = V_h^T P'^T_h, accumulated over key tiles
       if (ok && !ptx::mbar_wait(bar_P, 0, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_P); }
+      TL_STAMP(7);
       ptx::tc_fence_after();
       for (int j = nK; j < total && ok; ++j) {
         const int slot = j % nslot;
-        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
+        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
         ptx::tc_fence_after();
-        const int jj = j - nK, h = jj / nkt, kt = jj % nkt;
+        const int jj = j - nK, kt = jj / HPG, h = jj % HPG;
+        const int ksteps = (kt == nkt - 1 ? rlast : KT_ROWS) / 16;
         const uint32_t a0 = ring_addr + slot * TILE_BYTES;
         const uint32_t b0 = p_addr + (h * nkt + kt) * (KT_ROWS * BM * 2);
-#pragma unroll
-        for (int ks = 0; ks < KT_ROWS / 16; ++ks) {
+        for (int ks = 0; ks < ksteps; ++ks) {
           // V tile, MN-major 128B swizzle: 8-key groups 1024 B apart, d halves 16 KB apart
           const uint64_t ad = ptx::smem_desc(a0 + ks * 2048, TILE_BYTES / 2, 1024, 2);
           // P' tile, MN-major no swizzle: 8x8 core matrices, query blocks 128 B apart,
@@ -313,21 +309,54 @@ __global__ void __launch_bounds__(MAXT, 1)
           ptx::mma_f16_ss(tbase + o_col + h * BM, ad, bd, idesc_pv, (kt > 0 || ks > 0));
         }
         ptx::mma_commit(bar_free + slot);
-        if (issued < total) issue(issued++);
       }
       ptx::mma_commit(bar_O);
+      TL_STAMP(10);
     }
     __syncwarp();
   } else {
     // ================================================= compose warps
-    const int sub = warp & 3, kt = warp >> 2;
+    // stage the static mix and the per-query weights (fp32) while the first loads fly
+    for (int idx = threadIdx.x; idx < 2 * HPG * HPG; idx += ncompose) {
+      const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
+      const TermPtrs &tm = set ? p.post : p.pre;
+      const int hp = j / HPG, h = j % HPG;
+      Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
+    }
+    for (int idx = threadIdx.x; idx < 2 * BM * geo.rec_floats; idx += ncompose) {
+      const int set = idx / (BM * geo.rec_floats), rem = idx % (BM * geo.rec_floats);
+      const int i = rem / geo.rec_floats, j = rem % geo.rec_floats;
+      const TermPtrs &tm = set ? p.post : p.pre;
+      const int t = q0 + i;
+      float val = 0.f;
+      if (t < T) {
+        const int64_t tok = (int64_t)b * T + t;
+        if (j < HPG) {
+          const int h = j;
+          val = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)g * HPG + h) * HPG + h] : 0.f) +
+                (tm.qdd ? ld_w<E>(tm.qdd, tok * H + hbase + h) : 0.f);
+        } else if (j < HPG + HPG * R) {
+          const int h = (j - HPG) / R, r = (j - HPG) % R;
+          val = tm.qw1 ? ld_w<E>(tm.qw1, (tok * H + hbase + h) * R + r) : 0.f;
+        } else if (j < HPG + 2 * HPG * R) {
+          const int r = (j - HPG - HPG * R) / HPG, h = (j - HPG - HPG * R) % HPG;
+          val = tm.qw2 ? ld_w<E>(tm.qw2, (tok * R + r) * H + hbase + h) : 0.f;
+        }
+      }
+      rec[idx] = val;
+    }
+    // warp -> (lane quarter sub, key tile kt, column half cs); warps sharing
+    // (sub, kt) split the NG column groups of the tile between them
+    const int sub = warp & 3, kt = (warp >> 2) % nkt, cs = warp / (4 * nkt);
+    const int rw = warp % (4 * nkt);  // reduction slot: one writer per (column, sub, kt)
+    const int g_begin = cs * (NG / CS), g_end = g_begin + NG / CS;
     const int s_local = 32 * sub + lane;          // key row inside the key tile
     const int s = kb + kt * KT_ROWS + s_local;    // absolute key index
     const bool key_ok = s >= 0 && s < slen;
     const uint32_t tl = tbase + (static_cast<uint32_t>(32 * sub) << 16) + kt * KT_ROWS;
     // does any (query, key) pair of this warp survive the mask?
     const int wk0 = kb + kt * KT_ROWS + 32 * sub, wk1 = wk0 + 31;
-    const int klo = max(0, p.window > 0 ? q0 - p.window + 1 : 0), khi = min(q0 + BM - 1, slen - 1);
+    const int klo = max(0, kb), khi = min(q0 + BM - 1, slen - 1);
     const bool active = wk1 >= klo && wk0 <= khi;
     const int64_t ktok = (int64_t)b * T + s;
     // softmax scale folded into the exponent: composition is linear, so
@@ -339,29 +368,26 @@ __global__ void __launch_bounds__(MAXT, 1)
     float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
 
     auto valid = [&](int t) { return key_ok && s <= t && t - s < p.window && t < T; };
+    auto col_of = [&](int L, int i0) { return (L / GI) * BM + i0 + (L % GI); };
+    float *redm = red;                  // [4*nkt][NQ] warp-local column max, later the scale factor
+    float *reds = red + 4 * nkt * NQ;   // [4*nkt][NQ] warp-local column sums
 
-    if (!ptx::mbar_wait(bar_S, 0)) { ok = false; record_err(p, ERR_TIMEOUT_S); }
-    ptx::tc_fence_after();
-    if (p.dbg && blockIdx.x == 0 && blockIdx.y == 0) {
-#pragma unroll 1
-      for (int c = 0; c < NQ; c += 8) {
-        float v[8];
-        ptx::tmem_ld<8>(tl + c, v);
-        ptx::tmem_wait_ld();
-        for (int j = 0; j < 8; ++j) p.dbg[(kt * KT_ROWS + s_local) * NQ + c + j] = v[j];
-      }
-    }
-
-    // ---- pass A: pre-composition, mask, column max
-    if (active && ok) {
+    if (active) load_key_weights<E, HPG, R>(p.pre, ktok, H, hbase, key_ok, kw1, kw2, kdd);
+    ptx::named_bar_sync(1, ncompose);  // staged weights visible
+    if (active) {
 #pragma unroll
       for (int j = 0; j < HPG * HPG; ++j) Wreg[j] = Wz[j];
-      load_key_weights<E, HPG, R>(p.pre, ktok, H, hbase, key_ok, kw1, kw2, kdd);
     }
+    if (!ptx::mbar_wait(bar_S + kt, 0)) { ok = false; record_err(p, ERR_TIMEOUT_S); }
+    ptx::tc_fence_after();
+    if (threadIdx.x == 0) TL_STAMP(4);
+
+    // ---- pass 1: pre-composition + mask, warp-local column max (redux), e = exp(S - m_w),
+    //      warp-local column sums (shuffle transpose-reduce); e written back to TMEM
 #pragma unroll 1
-    for (int grp = 0; grp < NG; ++grp) {
+    for (int grp = g_begin; grp < g_end; ++grp) {
       const int i0 = grp * GI;
-      float mine = -INFINITY;
+      float mine_m = -INFINITY, mine_s = 0.f;
       if (active && ok) {
         float v[HPG][GI];
 #pragma unroll
@@ -378,47 +404,20 @@ __global__ void __launch_bounds__(MAXT, 1)
           for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : -INFINITY;
         }
 #pragma unroll
-        for (int h = 0; h < HPG; ++h) ptx::tmem_st<GI>(tl + h * BM + i0, v[h]);
-#pragma unroll
         for (int h = 0; h < HPG; ++h)
 #pragma unroll
           for (int ii = 0; ii < GI; ++ii) {
-            const float r = ptx::warp_max(v[h][ii]);
-            if (lane == h * GI + ii) mine = r;
+            const float mw = ptx::warp_max(v[h][ii]);
+            if (lane == h * GI + ii) mine_m = mw;
+            v[h][ii] = exp2f((v[h][ii] - (mw == -INFINITY ? 0.f : mw)) * sl2e);
           }
-      }
-      red[warp * NQ + (lane / GI) * BM + i0 + (lane % GI)] = mine;
-    }
-    ptx::tmem_wait_st();
-    ptx::named_bar_sync(1, 32 * ncompose_warps);
-    if (threadIdx.x < NQ) {
-      float m = -INFINITY;
-      for (int w = 0; w < ncompose_warps; ++w) m = fmaxf(m, red[w * NQ + threadIdx.x]);
-      mrow[threadIdx.x] = m == -INFINITY ? 0.f : m * sl2e;
-    }
-    ptx::named_bar_sync(1, 32 * ncompose_warps);
-
-    // ---- pass B: e = exp(S - m), column sums
-#pragma unroll 1
-    for (int grp = 0; grp < NG; ++grp) {
-      const int i0 = grp * GI;
-      float mine = 0.f;
-      if (active && ok) {
-        float v[HPG][GI];
 #pragma unroll
-        for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
-        ptx::tmem_wait_ld();
+        for (int h = 0; h < HPG; ++h) ptx::tmem_st<GI>(tl + h * BM + i0, v[h]);
         float x[32];
 #pragma unroll
         for (int h = 0; h < HPG; ++h)
 #pragma unroll
-          for (int ii = 0; ii < GI; ++ii) {
-            const float e = exp2f(fmaf(v[h][ii], sl2e, -mrow[h * BM + i0 + ii]));
-            v[h][ii] = e;
-            x[h * GI + ii] = e;
-          }
-#pragma unroll
-        for (int h = 0; h < HPG; ++h) ptx::tmem_st<GI>(tl + h * BM + i0, v[h]);
+          for (int ii = 0; ii < GI; ++ii) x[h * GI + ii] = v[h][ii];
         // transpose-reduce: afterwards lane L holds the column sum of value L
 #pragma unroll
         for (int off = 16, cnt = 32; off >= 1; off >>= 1, cnt >>= 1) {
@@ -430,28 +429,42 @@ __global__ void __launch_bounds__(MAXT, 1)
             x[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
           }
         }
-        mine = x[0];
+        mine_s = x[0];
       }
-      red[warp * NQ + (lane / GI) * BM + i0 + (lane % GI)] = mine;
+      redm[rw * NQ + col_of(lane, i0)] = mine_m;
+      reds[rw * NQ + col_of(lane, i0)] = mine_s;
     }
     ptx::tmem_wait_st();
-    ptx::named_bar_sync(1, 32 * ncompose_warps);
+    ptx::named_bar_sync(1, ncompose);
+    // combine the warps of each column: m = max_w m_w, l = sum_w s_w 2^((m_w - m) sl2e);
+    // factor_w = 2^((m_w - m) sl2e) / l turns e_w into the normalised probability
     if (threadIdx.x < NQ) {
+      const int j = threadIdx.x;
+      float m = -INFINITY;
+      for (int w = 0; w < 4 * nkt; ++w) m = fmaxf(m, redm[w * NQ + j]);
       float l = 0.f;
-      for (int w = 0; w < ncompose_warps; ++w) l += red[w * NQ + threadIdx.x];
-      linv[threadIdx.x] = l > 0.f ? 1.f / l : 0.f;
+      for (int w = 0; w < 4 * nkt; ++w) {
+        const float mw = redm[w * NQ + j];
+        const float f = mw == -INFINITY ? 0.f : exp2f((mw - m) * sl2e);
+        redm[w * NQ + j] = f;
+        l += reds[w * NQ + j] * f;
+      }
+      const float il = l > 0.f ? 1.f / l : 0.f;
+      for (int w = 0; w < 4 * nkt; ++w) redm[w * NQ + j] *= il;
     }
-    ptx::named_bar_sync(1, 32 * ncompose_warps);
+    ptx::named_bar_sync(1, ncompose);
+    if (threadIdx.x == 0) TL_STAMP(5);
 
-    // ---- pass C: normalise, post-composition, P' -> SMEM (PV B operand)
+    // ---- pass 2: normalise, post-composition, P' -> SMEM (PV B operand)
     if (active && ok) {
 #pragma unroll
       for (int j = 0; j < HPG * HPG; ++j) Wreg[j] = Wz[HPG * HPG + j];
       load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
     }
+    const float *fac = redm + rw * NQ;
     unsigned char *prow = smem + geo.p_off + (s_local & 7) * 16 + (s_local >> 3) * (BM * 16);
 #pragma unroll 1
-    for (int grp = 0; grp < NG; ++grp) {
+    for (int grp = g_begin; grp < g_end; ++grp) {
       const int i0 = grp * GI;
       float v[HPG][GI];
       if (active && ok) {
@@ -462,7 +475,7 @@ __global__ void __launch_bounds__(MAXT, 1)
         for (int ii = 0; ii < GI; ++ii) {
           float a[HPG], o[HPG];
 #pragma unroll
-          for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * linv[h * BM + i0 + ii];
+          for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * fac[h * BM + i0 + ii];
           compose<HPG, R>(a, o, Wreg, rec + (BM + i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
 #pragma unroll
           for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
@@ -499,44 +512,521 @@ __global__ void __launch_bounds__(MAXT, 1)
         }
       }
     }
-    if (p.dbg && blockIdx.x == 0 && blockIdx.y == 0) {
-      // P' as this thread wrote it: dbg[3*128*128 + ((h*nkt + kt)*128 + s_local)*BM + i]
-      for (int h = 0; h < HPG; ++h)
-        for (int i = 0; i < BM; ++i) {
-          const E *e = reinterpret_cast<const E *>(prow + (h * nkt + kt) * (KT_ROWS * BM * 2) + (i >> 3) * 128 +
-                                                   (i & 7) * 2);
-          p.dbg[3 * 128 * 128 + ((h * nkt + kt) * 128 + s_local) * BM + i] = to_f<E>(*e);
-        }
-    }
     ptx::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(bar_P);
+    if (threadIdx.x == 0) TL_STAMP(6);
 
-    // ---- epilogue: O^T (lanes = d) -> out[b, t, h, d]
+    // ---- epilogue: O^T (lanes = d) -> SMEM [head][d half][query][64 d] -> TMA store
     if (!ptx::mbar_wait(bar_O, 0, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_O); }
     ptx::tc_fence_after();
-    E *out = reinterpret_cast<E *>(p.out);
+    if (threadIdx.x == 0) TL_STAMP(8);
+    unsigned char *stage = smem + geo.q_off;  // Q is dead once every MMA has completed
     const int d = 32 * sub + lane;
     if (ok) {
 #pragma unroll 1
-      for (int c = kt; c < NQ / 8; c += nkt) {
+      for (int c = warp >> 2; c < NQ / 8; c += nkt * CS) {
         float v[8];
         ptx::tmem_ld<8>(tbase + (static_cast<uint32_t>(32 * sub) << 16) + o_col + 8 * c, v);
         ptx::tmem_wait_ld();
 #pragma unroll
         for (int jj = 0; jj < 8; ++jj) {
-          const int col = 8 * c + jj, h = col / BM, i = col % BM, t = q0 + i;
-          if (t < T)
-            out[(int64_t)b * p.out_sb + (int64_t)t * p.out_st + (int64_t)(hbase + h) * p.out_sh + d] =
-                from_f<E>(v[jj]);
+          const int col = 8 * c + jj, h = col / BM, i = col % BM;
+          *reinterpret_cast<E *>(stage + (h * 2 + (d >> 6)) * (BM * 128) + i * 128 + (d & 63) * 2) =
+              from_f<E>(v[jj]);
         }
       }
+    }
+    ptx::fence_proxy_async_smem();
+    ptx::named_bar_sync(1, ncompose);
+    if (threadIdx.x == 0 && ok) {
+      for (int h = 0; h < HPG; ++h)
+        for (int c = 0; c < 2; ++c)
+          ptx::tma_store_4d(&tm_o, stage + (h * 2 + c) * (BM * 128), c * 64, hbase + h, q0, b);
+      ptx::bulk_commit();
+      ptx::bulk_wait_read0();
     }
   }
 
   ptx::tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) TL_STAMP(9);
   if (warp == ctrl_warp) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tbase, 512);
+  }
+}
+
+// ------------------------------------------------------------------ persistent kernel
+//
+// Windowed layers whose key span fits two key tiles (BM + window - 1 <= 256)
+// run persistently: one CTA per SM walks the (query block, batch, group)
+// tiles blockIdx.x, blockIdx.x + gridDim.x, ... and overlaps consecutive
+// tiles with double buffers:
+//   TMEM  two 256-column buffers; buffer = S of both key tiles, and after
+//         pass 2 the PV accumulator O aliases key tile 0's columns;
+//   SMEM  two Q buffers; a Q buffer becomes P' of key tile 0 once its QK
+//         products are done, then the output staging tile of the epilogue;
+//         two P' buffers for key tile 1; one K/V ring shared by all tiles.
+// Warps: compose warps (as in dc_tc_kernel), 4 epilogue warps (TMEM -> SMEM
+// -> TMA store), one TMA warp, one MMA warp.  Order of ring jobs and MMAs:
+// Q(n) K(n) V(n-1), i.e. QK(n) is issued before PV(n-1) so the compose warps
+// can start tile n while tile n-1 drains.
+
+// development switch: force the one-tile-per-CTA kernel
+bool g_disable_persistent = false;
+
+struct GeoP {
+  int nslot, q_off, p1_off, ring_off, wz_off, rec_off, red_off, bar_off, tmem_off, total, rec_floats, p1_bytes;
+};
+
+__host__ __device__ inline GeoP make_geo_p(int HPG, int R, int rlast, int nslot) {
+  GeoP g{};
+  const int BM = NQ / HPG;
+  g.nslot = nslot;
+  g.q_off = 0;                                   // 2 x (NQ * 256): Q / P'(tile 0) / staging
+  g.p1_bytes = round_up(HPG * rlast * BM * 2, 1024);
+  g.p1_off = 2 * NQ * 256;                       // 2 x P'(tile 1)
+  g.ring_off = g.p1_off + 2 * g.p1_bytes;
+  int o = g.ring_off + nslot * TILE_BYTES;
+  g.rec_floats = round_up(HPG * (2 * R + 1), 4);
+  g.wz_off = o;  o += 2 * HPG * HPG * 4;
+  g.rec_off = round_up(o, 16); o = g.rec_off + 2 * BM * g.rec_floats * 4;
+  g.red_off = o; o += 2 * 8 * NQ * 4;
+  g.bar_off = round_up(o, 8); o = g.bar_off + 32 * 8;
+  g.tmem_off = o; o += 16;
+  g.total = o;
+  return g;
+}
+
+template <typename E, int HPG, int R, int CS>
+__global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
+    dc_tcp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kl,
+                  const __grid_constant__ CUtensorMap tm_vl, const __grid_constant__ CUtensorMap tm_o,
+                  const TcParams p, const int nkt, const int rlast, const int nslot) {
+  constexpr int BM = NQ / HPG;
+  constexpr int GI = 32 / HPG;
+  constexpr int NG = BM / GI;
+  static_assert(NG == 4 && NG % CS == 0, "group geometry");
+
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                          ~static_cast<uintptr_t>(1023));
+  const GeoP geo = make_geo_p(HPG, R, rlast, nslot);
+  float *Wz = reinterpret_cast<float *>(smem + geo.wz_off);
+  float *rec = reinterpret_cast<float *>(smem + geo.rec_off);
+  float *red = reinterpret_cast<float *>(smem + geo.red_off);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + geo.bar_off);
+  uint64_t *bar_full = bars + 0, *bar_free = bars + 3;          // ring
+  uint64_t *bar_q = bars + 6;                                    // [2] Q landed
+  uint64_t *bar_S = bars + 8;                                    // [2][2] S of (buffer, key tile) ready
+  uint64_t *bar_P = bars + 12;                                   // [2] P' written (compose warps)
+  uint64_t *bar_O = bars + 14;                                   // [2] O complete (PV committed)
+  uint64_t *bar_Ofree = bars + 16;                               // [2] O read out of TMEM (epilogue)
+  uint64_t *bar_Qfree = bars + 18;                               // [2] staging tile stored (epilogue)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + geo.tmem_off);
+
+  const int ncw = 4 * nkt * CS;  // compose warps
+  const int ncompose = 32 * ncw;
+  const int epi_warp0 = ncw, tma_warp = ncw + 4, mma_warp = ncw + 5;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nqb = (p.T + BM - 1) / BM;
+  const int ntiles = nqb * p.B * p.G;
+  const int H = p.H, T = p.T;
+  const int rows_of[2] = {nkt == 1 ? rlast : KT_ROWS, rlast};
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < 3; ++i) {
+      ptx::mbar_init(bar_full + i, 1);
+      ptx::mbar_init(bar_free + i, 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(bar_q + i, 1);
+      ptx::mbar_init(bar_S + 2 * i, 1);
+      ptx::mbar_init(bar_S + 2 * i + 1, 1);
+      ptx::mbar_init(bar_P + i, ncw);
+      ptx::mbar_init(bar_O + i, 1);
+      ptx::mbar_init(bar_Ofree + i, 4);
+      ptx::mbar_init(bar_Qfree + i, 1);
+    }
+    ptx::fence_mbar_init();
+  }
+  if (warp == tma_warp) ptx::tmem_alloc(tmem_slot, 512);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+  const uint32_t WAIT = 1u << 26;
+
+  // tile -> (query block, batch, group)
+  auto tile_coords = [&](int tile, int &q0, int &b, int &g) {
+    const int qb = tile % nqb, bg = tile / nqb;
+    q0 = qb * BM; b = bg / p.G; g = bg % p.G;
+  };
+  // P' base of (buffer, key tile)
+  auto p_tile = [&](int buf, int kt) -> unsigned char * {
+    return kt == 0 ? smem + geo.q_off + buf * NQ * 256 : smem + geo.p1_off + buf * geo.p1_bytes;
+  };
+
+  if (warp == tma_warp) {
+    // ================================================= TMA producer
+    if (lane == 0) {
+      ptx::tma_prefetch_desc(&tm_q);
+      ptx::tma_prefetch_desc(&tm_k);
+      ptx::tma_prefetch_desc(&tm_v);
+      const int nK = HPG * nkt;
+      int job = 0;
+      bool ok = true;
+      auto load_kv = [&](bool isv, int q0, int b, int g, int jj) {
+        const int slot = job % nslot, use = job / nslot;
+        if (use > 0 && !ptx::mbar_wait(bar_free + slot, (use - 1) & 1, WAIT)) {
+          ok = false;
+          record_err(p, ERR_TIMEOUT_FREE);
+          return;
+        }
+        const int kt = jj / HPG, h = jj % HPG;
+        const bool last = kt == nkt - 1;
+        const CUtensorMap *m = isv ? (last ? &tm_vl : &tm_v) : (last ? &tm_kl : &tm_k);
+        const int kb = q0 - p.window + 1;
+        ptx::mbar_expect_tx(bar_full + slot, rows_of[kt] * 256);
+        unsigned char *dst = smem + geo.ring_off + slot * TILE_BYTES;
+        ptx::tma_load_4d(dst, m, bar_full + slot, 0, g * HPG + h, kb + kt * KT_ROWS, b);
+        ptx::tma_load_4d(dst + TILE_BYTES / 2, m, bar_full + slot, 64, g * HPG + h, kb + kt * KT_ROWS, b);
+        ++job;
+      };
+      int pq0 = 0, pb = 0, pg = 0;
+      int it = 0;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+        int q0, b, g;
+        tile_coords(tile, q0, b, g);
+        const int buf = it & 1;
+        if (it >= 2 && !ptx::mbar_wait(bar_Qfree + buf, ((it - 2) >> 1) & 1, WAIT)) {
+          record_err(p, ERR_TIMEOUT_Q);
+          break;
+        }
+        ptx::mbar_expect_tx(bar_q + buf, NQ * 256);
+        for (int h = 0; h < HPG; ++h)
+          for (int c = 0; c < 2; ++c)
+            ptx::tma_load_4d(smem + geo.q_off + buf * NQ * 256 + h * BM * 256 + c * BM * 128, &tm_q, bar_q + buf,
+                             c * 64, g * HPG + h, q0, b);
+        for (int jj = 0; jj < nK && ok; ++jj) load_kv(false, q0, b, g, jj);
+        if (it >= 1)
+          for (int jj = 0; jj < nK && ok; ++jj) load_kv(true, pq0, pb, pg, jj);
+        pq0 = q0; pb = b; pg = g;
+      }
+      if (it >= 1)
+        for (int jj = 0; jj < nK && ok; ++jj) load_kv(true, pq0, pb, pg, jj);
+    }
+    __syncwarp();
+  } else if (warp == mma_warp) {
+    // ================================================= MMA issuer
+    if (lane == 0) {
+      const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
+      const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 128, BM);
+      const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 128, BM);
+      const uint32_t ring_addr = ptx::smem_u32(smem + geo.ring_off);
+      const int nK = HPG * nkt;
+      int job = 0;
+      bool ok = true;
+      auto pv = [&](int pit) {
+        const int buf = pit & 1;
+        if (!ptx::mbar_wait(bar_P + buf, (pit >> 1) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_P); return; }
+        ptx::tc_fence_after();
+        for (int jj = 0; jj < nK && ok; ++jj, ++job) {
+          const int slot = job % nslot;
+          if (!ptx::mbar_wait(bar_full + slot, (job / nslot) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); return; }
+          ptx::tc_fence_after();
+          const int kt = jj / HPG, h = jj % HPG;
+          const int rows = rows_of[kt];
+          const uint32_t a0 = ring_addr + slot * TILE_BYTES;
+          const uint32_t b0 = ptx::smem_u32(p_tile(buf, kt)) + h * (rows * BM * 2);
+          for (int ks = 0; ks < rows / 16; ++ks) {
+            const uint64_t ad = ptx::smem_desc(a0 + ks * 2048, TILE_BYTES / 2, 1024, 2);
+            const uint64_t bd = ptx::smem_desc(b0 + ks * (2 * BM * 16), BM * 16, 128, 0);
+            ptx::mma_f16_ss(tbase + buf * 256 + h * BM, ad, bd, idesc_pv, (kt > 0 || ks > 0));
+          }
+          ptx::mma_commit(bar_free + slot);
+        }
+        ptx::mma_commit(bar_O + buf);
+      };
+      int it = 0;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+        const int buf = it & 1;
+        // TMEM buffer free once the epilogue of tile it-2 has read its O
+        if (it >= 2 && !ptx::mbar_wait(bar_Ofree + buf, ((it - 2) >> 1) & 1, WAIT)) {
+          ok = false; record_err(p, ERR_TIMEOUT_O); break;
+        }
+        if (!ptx::mbar_wait(bar_q + buf, (it >> 1) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_Q); break; }
+        ptx::tc_fence_after();
+        const uint32_t q_addr = ptx::smem_u32(smem + geo.q_off + buf * NQ * 256);
+        for (int jj = 0; jj < nK && ok; ++jj, ++job) {
+          const int slot = job % nslot;
+          if (!ptx::mbar_wait(bar_full + slot, (job / nslot) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
+          ptx::tc_fence_after();
+          const int kt = jj / HPG, h = jj % HPG;
+          const uint32_t a0 = ring_addr + slot * TILE_BYTES;
+          const uint32_t b0 = q_addr + h * BM * 256;
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint64_t ad = ptx::smem_desc(a0 + (ks >> 2) * (TILE_BYTES / 2) + (ks & 3) * 32, 16, 1024, 2);
+            const uint64_t bd = ptx::smem_desc(b0 + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 16, 1024, 2);
+            ptx::mma_f16_ss(tbase + buf * 256 + kt * KT_ROWS + h * BM, ad, bd, idesc_qk, ks > 0);
+          }
+          ptx::mma_commit(bar_free + slot);
+          if (h == HPG - 1) ptx::mma_commit(bar_S + 2 * buf + kt);
+        }
+        if (it >= 1 && ok) pv(it - 1);
+      }
+      if (it >= 1 && ok) pv(it - 1);
+    }
+    __syncwarp();
+  } else if (warp >= epi_warp0) {
+    // ================================================= epilogue: O^T (lanes = d) -> SMEM -> TMA store
+    const int quarter = warp & 3, d = 32 * quarter + lane;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      int q0, b, g;
+      tile_coords(tile, q0, b, g);
+      const int buf = it & 1;
+      if (!ptx::mbar_wait(bar_O + buf, (it >> 1) & 1, WAIT)) { record_err(p, ERR_TIMEOUT_O); break; }
+      ptx::tc_fence_after();
+      unsigned char *stage = smem + geo.q_off + buf * NQ * 256;
+#pragma unroll 1
+      for (int c = 0; c < NQ / 8; ++c) {
+        float v[8];
+        ptx::tmem_ld<8>(tbase + (static_cast<uint32_t>(32 * quarter) << 16) + buf * 256 + 8 * c, v);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int jj = 0; jj < 8; ++jj) {
+          const int col = 8 * c + jj, h = col / BM, i = col % BM;
+          *reinterpret_cast<E *>(stage + (h * 2 + (d >> 6)) * (BM * 128) + i * 128 + (d & 63) * 2) =
+              from_f<E>(v[jj]);
+        }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_Ofree + buf);
+      ptx::fence_proxy_async_smem();
+      ptx::named_bar_sync(2, 128);
+      if (warp == epi_warp0 && lane == 0) {
+        for (int h = 0; h < HPG; ++h)
+          for (int c = 0; c < 2; ++c)
+            ptx::tma_store_4d(&tm_o, stage + (h * 2 + c) * (BM * 128), c * 64, g * HPG + h, q0, b);
+        ptx::bulk_commit();
+        ptx::bulk_wait_read0();
+        ptx::mbar_arrive(bar_Qfree + buf);
+      }
+    }
+  } else {
+    // ================================================= compose warps
+    const int sub = warp & 3, kt = (warp >> 2) % nkt, cs = warp / (4 * nkt);
+    const int rw = warp % (4 * nkt);
+    const int g_begin = cs * (NG / CS), g_end = g_begin + NG / CS;
+    const int s_local = 32 * sub + lane;
+    const int rows_kt = rows_of[kt];
+    const float sl2e = p.scale * kLog2e;
+    float *redm = red, *reds = red + 4 * nkt * NQ;
+    auto col_of = [&](int L, int i0) { return (L / GI) * BM + i0 + (L % GI); };
+    float Wreg[HPG * HPG];
+    float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
+    int it = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+      int q0, b, g;
+      tile_coords(tile, q0, b, g);
+      const int buf = it & 1, hbase = g * HPG;
+      const int kb = q0 - p.window + 1;
+      const int slen = p.seq_lens ? min(max(p.seq_lens[b], 0), T) : T;
+      // previous tile's pass 2 is finished by every compose warp before rec / red are rewritten
+      ptx::named_bar_sync(1, ncompose);
+      if (it == 0)
+        for (int idx = threadIdx.x; idx < 2 * HPG * HPG; idx += ncompose) {
+          const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
+          const TermPtrs &tm = set ? p.post : p.pre;
+          const int hp = j / HPG, h = j % HPG;
+          Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
+        }
+      for (int idx = threadIdx.x; idx < 2 * BM * geo.rec_floats; idx += ncompose) {
+        const int set = idx / (BM * geo.rec_floats), rem = idx % (BM * geo.rec_floats);
+        const int i = rem / geo.rec_floats, j = rem % geo.rec_floats;
+        const TermPtrs &tm = set ? p.post : p.pre;
+        const int t = q0 + i;
+        float val = 0.f;
+        if (t < T) {
+          const int64_t tok = (int64_t)b * T + t;
+          if (j < HPG) {
+            const int h = j;
+            val = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)g * HPG + h) * HPG + h] : 0.f) +
+                  (tm.qdd ? ld_w<E>(tm.qdd, tok * H + hbase + h) : 0.f);
+          } else if (j < HPG + HPG * R) {
+            const int h = (j - HPG) / R, r = (j - HPG) % R;
+            val = tm.qw1 ? ld_w<E>(tm.qw1, (tok * H + hbase + h) * R + r) : 0.f;
+          } else if (j < HPG + 2 * HPG * R) {
+            const int r = (j - HPG - HPG * R) / HPG, h = (j - HPG - HPG * R) % HPG;
+            val = tm.qw2 ? ld_w<E>(tm.qw2, (tok * R + r) * H + hbase + h) : 0.f;
+          }
+        }
+        rec[idx] = val;
+      }
+      const int s = kb + kt * KT_ROWS + s_local;
+      const bool key_ok = s >= 0 && s < slen && s_local < rows_kt;
+      const int wk0 = kb + kt * KT_ROWS + 32 * sub, wk1 = wk0 + 31;
+      const int khi = min(q0 + BM - 1, slen - 1);
+      const bool active = wk1 >= max(0, kb) && wk0 <= khi && 32 * sub < rows_kt;
+      const int64_t ktok = (int64_t)b * T + s;
+      const uint32_t tl = tbase + (static_cast<uint32_t>(32 * sub) << 16) + buf * 256 + kt * KT_ROWS;
+      auto valid = [&](int t) { return key_ok && s <= t && t - s < p.window && t < T; };
+      if (active) load_key_weights<E, HPG, R>(p.pre, ktok, H, hbase, key_ok, kw1, kw2, kdd);
+      ptx::named_bar_sync(1, ncompose);  // staged weights visible
+      if (active) {
+#pragma unroll
+        for (int j = 0; j < HPG * HPG; ++j) Wreg[j] = Wz[j];
+      }
+      bool ok = ptx::mbar_wait(bar_S + 2 * buf + kt, (it >> 1) & 1, WAIT);
+      if (!ok) record_err(p, ERR_TIMEOUT_S);
+      ptx::tc_fence_after();
+
+      // ---- pass 1 (see dc_tc_kernel)
+#pragma unroll 1
+      for (int grp = g_begin; grp < g_end; ++grp) {
+        const int i0 = grp * GI;
+        float mine_m = -INFINITY, mine_s = 0.f;
+        if (active && ok) {
+          float v[HPG][GI];
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int ii = 0; ii < GI; ++ii) {
+            float a[HPG], o[HPG];
+#pragma unroll
+            for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
+            compose<HPG, R>(a, o, Wreg, rec + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+            const bool vl = valid(q0 + i0 + ii);
+#pragma unroll
+            for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : -INFINITY;
+          }
+#pragma unroll
+          for (int h = 0; h < HPG; ++h)
+#pragma unroll
+            for (int ii = 0; ii < GI; ++ii) {
+              const float mw = ptx::warp_max(v[h][ii]);
+              if (lane == h * GI + ii) mine_m = mw;
+              v[h][ii] = exp2f((v[h][ii] - (mw == -INFINITY ? 0.f : mw)) * sl2e);
+            }
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) ptx::tmem_st<GI>(tl + h * BM + i0, v[h]);
+          float x[32];
+#pragma unroll
+          for (int h = 0; h < HPG; ++h)
+#pragma unroll
+            for (int ii = 0; ii < GI; ++ii) x[h * GI + ii] = v[h][ii];
+#pragma unroll
+          for (int off = 16, cnt = 32; off >= 1; off >>= 1, cnt >>= 1) {
+            const bool upper = (lane & off) != 0;
+#pragma unroll
+            for (int j = 0; j < cnt / 2; ++j) {
+              const float send = upper ? x[j] : x[j + cnt / 2];
+              const float keep = upper ? x[j + cnt / 2] : x[j];
+              x[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            }
+          }
+          mine_s = x[0];
+        }
+        redm[rw * NQ + col_of(lane, i0)] = mine_m;
+        reds[rw * NQ + col_of(lane, i0)] = mine_s;
+      }
+      ptx::tmem_wait_st();
+      ptx::named_bar_sync(1, ncompose);
+      if (threadIdx.x < NQ) {
+        const int j = threadIdx.x;
+        float m = -INFINITY;
+        for (int w = 0; w < 4 * nkt; ++w) m = fmaxf(m, redm[w * NQ + j]);
+        float l = 0.f;
+        for (int w = 0; w < 4 * nkt; ++w) {
+          const float mw = redm[w * NQ + j];
+          const float f = mw == -INFINITY ? 0.f : exp2f((mw - m) * sl2e);
+          redm[w * NQ + j] = f;
+          l += reds[w * NQ + j] * f;
+        }
+        const float il = l > 0.f ? 1.f / l : 0.f;
+        for (int w = 0; w < 4 * nkt; ++w) redm[w * NQ + j] *= il;
+      }
+      ptx::named_bar_sync(1, ncompose);
+      // P' of key tile 0 overwrites Q: every QK product of this tile must be complete
+      if (ok && kt == 0 && nkt > 1) {
+        ok = ptx::mbar_wait(bar_S + 2 * buf + nkt - 1, (it >> 1) & 1, WAIT);
+        if (!ok) record_err(p, ERR_TIMEOUT_S);
+      }
+
+      // ---- pass 2: normalise, post-composition, P' -> SMEM
+      if (active && ok) {
+#pragma unroll
+        for (int j = 0; j < HPG * HPG; ++j) Wreg[j] = Wz[HPG * HPG + j];
+        load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
+      }
+      const float *fac = redm + rw * NQ;
+      unsigned char *pbase = p_tile(buf, kt) + (s_local & 7) * 16 + (s_local >> 3) * (BM * 16);
+#pragma unroll 1
+      for (int grp = g_begin; grp < g_end; ++grp) {
+        const int i0 = grp * GI;
+        float v[HPG][GI];
+        if (active && ok) {
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int ii = 0; ii < GI; ++ii) {
+            float a[HPG], o[HPG];
+#pragma unroll
+            for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * fac[h * BM + i0 + ii];
+            compose<HPG, R>(a, o, Wreg, rec + (BM + i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+#pragma unroll
+            for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
+          }
+        } else {
+#pragma unroll
+          for (int h = 0; h < HPG; ++h)
+#pragma unroll
+            for (int ii = 0; ii < GI; ++ii) v[h][ii] = 0.f;
+        }
+        if (s_local < rows_kt) {
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) {
+            unsigned char *tile_p = pbase + h * (rows_kt * BM * 2);
+#pragma unroll
+            for (int c = 0; c < GI; c += 8 < GI ? 8 : GI) {
+              constexpr int W8 = GI < 8 ? GI : 8;
+              uint32_t pk[W8 / 2];
+#pragma unroll
+              for (int u = 0; u < W8 / 2; ++u) {
+                const E lo = from_f<E>(v[h][c + 2 * u]), hi = from_f<E>(v[h][c + 2 * u + 1]);
+                pk[u] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&lo)) |
+                        (static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&hi)) << 16);
+              }
+              const int i = i0 + c;
+              unsigned char *dst = tile_p + (i >> 3) * 128 + (i & 7) * 2;
+              if constexpr (W8 == 8) {
+                *reinterpret_cast<uint4 *>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+              } else if constexpr (W8 == 4) {
+                *reinterpret_cast<uint2 *>(dst) = make_uint2(pk[0], pk[1]);
+              } else {
+                *reinterpret_cast<uint32_t *>(dst) = pk[0];
+              }
+            }
+          }
+        }
+      }
+      ptx::fence_proxy_async_smem();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_P + buf);
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == tma_warp) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tbase, 512);
   }
@@ -560,24 +1050,34 @@ static EncodeTiledFn get_encode() {
   return fn;
 }
 
-// [B, T, H, D] tensor as a 4-D map (D, H, T, B); box = 64 d x 1 head x rows x 1.
-static bool make_map(CUtensorMap *m, const void *base, int dtype, int B, int T, int H, int rows) {
+// [B, T, H, D] tensor (element strides sb, st, sh; d contiguous) as a 4-D map
+// (D, H, T, B); box = 64 d x 1 head x rows x 1.
+static bool make_map(CUtensorMap *m, const void *base, int dtype, int B, int T, int H, int rows, int64_t sb,
+                     int64_t st, int64_t sh, bool swizzle) {
   EncodeTiledFn enc = get_encode();
   if (!enc) return false;
   const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
-  const cuuint64_t strides[3] = {(cuuint64_t)D * 2, (cuuint64_t)H * D * 2, (cuuint64_t)T * H * D * 2};
+  const cuuint64_t strides[3] = {(cuuint64_t)sh * 2, (cuuint64_t)st * 2, (cuuint64_t)sb * 2};
   const cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
   const cuuint32_t estr[4] = {1, 1, 1, 1};
   const CUtensorMapDataType dt =
       dtype == DC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   return enc(m, dt, 4, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// key span of a query block: BM + window - 1 keys
 static int num_key_tiles(int HPG, int window) {
   const int BM = NQ / HPG;
   return (BM + window - 1 + KT_ROWS - 1) / KT_ROWS;
+}
+// rows of the last key tile, rounded up to the 16-key MMA step
+static int last_tile_rows(int HPG, int window) {
+  const int BM = NQ / HPG;
+  const int span = BM + window - 1;
+  const int r = span - KT_ROWS * (num_key_tiles(HPG, window) - 1);
+  return (r + 15) / 16 * 16;
 }
 
 static TermPtrs to_ptrs(const dc_terms &t) {
@@ -594,9 +1094,15 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   const int nkt = num_key_tiles(HPG, p.window);
   const Geo geo = make_geo(HPG, R, nkt);
   const size_t smem = geo.total + 1024;
-  CUtensorMap mq, mk, mv;
-  if (!make_map(&mq, p.q, p.dtype, p.B, p.T, p.H, BM) || !make_map(&mk, p.k, p.dtype, p.B, p.T, p.H, KT_ROWS) ||
-      !make_map(&mv, p.v, p.dtype, p.B, p.T, p.H, KT_ROWS))
+  const int rlast = last_tile_rows(HPG, p.window);
+  const int64_t sb = (int64_t)p.T * p.H * D, st_ = (int64_t)p.H * D, sh = D;
+  CUtensorMap mq, mk, mv, mkl, mvl, mo;
+  if (!make_map(&mq, p.q, p.dtype, p.B, p.T, p.H, BM, sb, st_, sh, true) ||
+      !make_map(&mk, p.k, p.dtype, p.B, p.T, p.H, KT_ROWS, sb, st_, sh, true) ||
+      !make_map(&mv, p.v, p.dtype, p.B, p.T, p.H, KT_ROWS, sb, st_, sh, true) ||
+      !make_map(&mkl, p.k, p.dtype, p.B, p.T, p.H, rlast, sb, st_, sh, true) ||
+      !make_map(&mvl, p.v, p.dtype, p.B, p.T, p.H, rlast, sb, st_, sh, true) ||
+      !make_map(&mo, p.out, p.dtype, p.B, p.T, p.H, BM, p.out_sb, p.out_st, p.out_sh, false))
     return cudaErrorInvalidValue;
   TcParams tp;
   tp.B = p.B; tp.T = p.T; tp.H = p.H; tp.G = p.G; tp.window = p.window; tp.slen_default = p.T;
@@ -605,20 +1111,69 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   tp.out = p.out;
   tp.out_sb = p.out_sb; tp.out_st = p.out_st; tp.out_sh = p.out_sh;
   tp.err_flag = p.err_flag;
-  tp.dbg = g_debug_dump;
   tp.pre = to_ptrs(p.pre);
   tp.post = to_ptrs(p.post);
-  auto kern = nkt <= 2 ? dc_tc_kernel<E, HPG, R, 288> : dc_tc_kernel<E, HPG, R, 416>;
+  // short windows (<= 2 key tiles): two warps per TMEM lane quarter and key tile
+  const int cs = nkt <= 2 ? 2 : 1;
+  auto kern = cs == 2 ? dc_tc_kernel<E, HPG, R, 2, 576> : dc_tc_kernel<E, HPG, R, 1, 448>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((p.T + BM - 1) / BM, p.B * p.G);
-  dim3 block(32 * (4 * nkt + 1));
-  kern<<<grid, block, smem, st>>>(mq, mk, mv, tp, nkt);
+  dim3 block(32 * (4 * nkt * cs + 2));  // compose warps + TMA warp + MMA warp
+  kern<<<grid, block, smem, st>>>(mq, mk, mv, mkl, mvl, mo, tp, nkt, rlast);
+  return cudaGetLastError();
+}
+
+static int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev] > 0 ? n[dev] : 148;
+}
+
+template <typename E, int HPG, int R>
+static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
+  constexpr int BM = NQ / HPG;
+  constexpr int CS = 2;
+  const int nkt = num_key_tiles(HPG, p.window);
+  const int rlast = last_tile_rows(HPG, p.window);
+  int nslot = 3;
+  if (make_geo_p(HPG, R, rlast, nslot).total + 1024 > 227 * 1024) nslot = 2;
+  const size_t smem = make_geo_p(HPG, R, rlast, nslot).total + 1024;
+  const int64_t sb = (int64_t)p.T * p.H * D, st_ = (int64_t)p.H * D, sh = D;
+  CUtensorMap mq, mk, mv, mkl, mvl, mo;
+  if (!make_map(&mq, p.q, p.dtype, p.B, p.T, p.H, BM, sb, st_, sh, true) ||
+      !make_map(&mk, p.k, p.dtype, p.B, p.T, p.H, KT_ROWS, sb, st_, sh, true) ||
+      !make_map(&mv, p.v, p.dtype, p.B, p.T, p.H, KT_ROWS, sb, st_, sh, true) ||
+      !make_map(&mkl, p.k, p.dtype, p.B, p.T, p.H, rlast, sb, st_, sh, true) ||
+      !make_map(&mvl, p.v, p.dtype, p.B, p.T, p.H, rlast, sb, st_, sh, true) ||
+      !make_map(&mo, p.out, p.dtype, p.B, p.T, p.H, BM, p.out_sb, p.out_st, p.out_sh, false))
+    return cudaErrorInvalidValue;
+  TcParams tp;
+  tp.B = p.B; tp.T = p.T; tp.H = p.H; tp.G = p.G; tp.window = p.window; tp.slen_default = p.T;
+  tp.scale = p.scale;
+  tp.seq_lens = p.seq_lens;
+  tp.out = p.out;
+  tp.out_sb = p.out_sb; tp.out_st = p.out_st; tp.out_sh = p.out_sh;
+  tp.err_flag = p.err_flag;
+  tp.pre = to_ptrs(p.pre);
+  tp.post = to_ptrs(p.post);
+  auto kern = dc_tcp_kernel<E, HPG, R, CS>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int ntiles = (p.T + BM - 1) / BM * p.B * p.G;
+  dim3 grid(ntiles < sm_count() ? ntiles : sm_count());
+  dim3 block(32 * (4 * nkt * CS + 6));
+  kern<<<grid, block, smem, st>>>(mq, mk, mv, mkl, mvl, mo, tp, nkt, rlast, nslot);
   return cudaGetLastError();
 }
 
 template <typename E, int HPG>
 static cudaError_t launch_r(const dc_attn_params &p, cudaStream_t st) {
+  if (num_key_tiles(HPG, p.window) <= 2 && !g_disable_persistent)
+    return p.R <= 1 ? launch_p<E, HPG, 1>(p, st) : launch_p<E, HPG, 2>(p, st);
   return p.R <= 1 ? launch_t<E, HPG, 1>(p, st) : launch_t<E, HPG, 2>(p, st);
 }
 
@@ -646,7 +1201,8 @@ bool tc_supports(const dc_attn_params &p, std::string *why) {
   if (!(p.scale > 0.f)) return no("non-positive softmax scale");
   if (p.pre.qmat || p.post.qmat) return no("per-query mixing matrices use the SIMT kernel");
   auto al = [](const void *x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
-  if (!al(p.q) || !al(p.k) || !al(p.v)) return no("q, k, v must be 16-byte aligned");
+  if (!al(p.q) || !al(p.k) || !al(p.v) || !al(p.out)) return no("q, k, v, out must be 16-byte aligned");
+  if (p.out_sb % 8 || p.out_st % 8 || p.out_sh % 8) return no("output strides must be multiples of 8 elements");
   return true;
 }
 
