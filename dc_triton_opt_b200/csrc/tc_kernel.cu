@@ -92,14 +92,22 @@ struct TcParams {
 __device__ int g_default_err;
 
 #ifdef DC_TIMELINE
-// development builds only: per-CTA clock64 stamps of the phases
+// development builds only: clock64 stamps of the phases (per CTA; the
+// persistent kernel records CTA 0 per tile iteration)
 __device__ unsigned long long g_timeline[8192][40];
+#define TLP_STAMP(it, i)                                                 \
+  do {                                                                   \
+    if (blockIdx.x == 0 && (it) < 8192) g_timeline[(it)][i] = clock64(); \
+  } while (0)
 #define TL_STAMP(i)                                                                   \
   do {                                                                                \
     const int cta_ = blockIdx.y * gridDim.x + blockIdx.x;                             \
     if (cta_ < 8192) g_timeline[cta_][i] = clock64();                                 \
   } while (0)
 #else
+#define TLP_STAMP(it, i) \
+  do {                   \
+  } while (0)
 #define TL_STAMP(i) \
   do {              \
   } while (0)
@@ -757,7 +765,9 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
         if (it >= 2 && !ptx::mbar_wait(bar_Ofree + buf, ((it - 2) >> 1) & 1, WAIT)) {
           ok = false; record_err(p, ERR_TIMEOUT_O); break;
         }
+        TLP_STAMP(it, 7);
         if (!ptx::mbar_wait(bar_q + buf, (it >> 1) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_Q); break; }
+        TLP_STAMP(it, 8);
         ptx::tc_fence_after();
         const uint32_t q_addr = ptx::smem_u32(smem + geo.q_off + buf * NQ * 256);
         for (int jj = 0; jj < nK && ok; ++jj, ++job) {
@@ -776,7 +786,9 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
           ptx::mma_commit(bar_free + slot);
           if (h == HPG - 1) ptx::mma_commit(bar_S + 2 * buf + kt);
         }
+        TLP_STAMP(it, 9);
         if (it >= 1 && ok) pv(it - 1);
+        TLP_STAMP(it, 10);
       }
       if (it >= 1 && ok) pv(it - 1);
     }
@@ -789,7 +801,9 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
       int q0, b, g;
       tile_coords(tile, q0, b, g);
       const int buf = it & 1;
+      if (threadIdx.x == 32 * epi_warp0) TLP_STAMP(it, 4);
       if (!ptx::mbar_wait(bar_O + buf, (it >> 1) & 1, WAIT)) { record_err(p, ERR_TIMEOUT_O); break; }
+      if (threadIdx.x == 32 * epi_warp0) TLP_STAMP(it, 5);
       ptx::tc_fence_after();
       unsigned char *stage = smem + geo.q_off + buf * NQ * 256;
 #pragma unroll 1
@@ -816,6 +830,7 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
         ptx::bulk_commit();
         ptx::bulk_wait_read0();
         ptx::mbar_arrive(bar_Qfree + buf);
+        TLP_STAMP(it, 6);
       }
     }
   } else {
@@ -882,7 +897,9 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
 #pragma unroll
         for (int j = 0; j < HPG * HPG; ++j) Wreg[j] = Wz[j];
       }
+      if (threadIdx.x == 0) TLP_STAMP(it, 0);
       bool ok = ptx::mbar_wait(bar_S + 2 * buf + kt, (it >> 1) & 1, WAIT);
+      if (threadIdx.x == 0) TLP_STAMP(it, 1);
       if (!ok) record_err(p, ERR_TIMEOUT_S);
       ptx::tc_fence_after();
 
@@ -953,6 +970,7 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
         for (int w = 0; w < 4 * nkt; ++w) redm[w * NQ + j] *= il;
       }
       ptx::named_bar_sync(1, ncompose);
+      if (threadIdx.x == 0) TLP_STAMP(it, 2);
       // P' of key tile 0 overwrites Q: every QK product of this tile must be complete
       if (ok && kt == 0 && nkt > 1) {
         ok = ptx::mbar_wait(bar_S + 2 * buf + nkt - 1, (it >> 1) & 1, WAIT);
@@ -1021,6 +1039,7 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_P + buf);
+      if (threadIdx.x == 0) TLP_STAMP(it, 3);
     }
   }
 
