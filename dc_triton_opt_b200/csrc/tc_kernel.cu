@@ -584,6 +584,52 @@ __global__ void __launch_bounds__(MAXT, 1)
 // development switch: force the one-tile-per-CTA kernel
 bool g_disable_persistent = false;
 
+// Warp-role table of the persistent kernel, built on the host.  Compose warps
+// exist only for the TMEM lane quarters that hold keys of their key tile (the
+// last key tile is usually short), and a compose warp must sit at an index
+// with warp % 4 == its lane quarter (tcgen05.ld / st address the quarter of
+// warp % 4), so the other roles fill the gaps.
+enum : uint8_t { ROLE_IDLE = 0xFF, ROLE_TMA = 0x80, ROLE_MMA = 0x81, ROLE_EPI = 0x90 /* | quarter */ };
+struct WarpRoles {
+  uint8_t role[32];  // compose: kt << 3 | cs << 2 | sub
+  int nwarps, ncw, nslots, epi_leader;
+};
+
+static WarpRoles make_roles(int nkt, int rlast, int CS) {
+  WarpRoles r;
+  for (int i = 0; i < 32; ++i) r.role[i] = ROLE_IDLE;
+  bool used[32] = {false};
+  const int nq_last = (rlast + 31) / 32;
+  r.ncw = 0;
+  for (int kt = 0; kt < nkt; ++kt) {
+    const int nq = kt < nkt - 1 ? 4 : nq_last;
+    for (int cs = 0; cs < CS; ++cs)
+      for (int sub = 0; sub < nq; ++sub) {
+        int w = sub;
+        while (used[w]) w += 4;
+        used[w] = true;
+        r.role[w] = static_cast<uint8_t>(kt << 3 | cs << 2 | sub);
+        ++r.ncw;
+      }
+  }
+  r.nslots = 4 * (nkt - 1) + nq_last;
+  auto take = [&](uint8_t role, int quarter) {
+    int w = quarter < 0 ? 0 : quarter;
+    while (used[w]) w += quarter < 0 ? 1 : 4;
+    used[w] = true;
+    r.role[w] = role;
+    return w;
+  };
+  take(ROLE_TMA, -1);
+  take(ROLE_MMA, -1);
+  r.epi_leader = take(ROLE_EPI | 0, 0);
+  for (int q = 1; q < 4; ++q) take(static_cast<uint8_t>(ROLE_EPI | q), q);
+  r.nwarps = 0;
+  for (int i = 0; i < 32; ++i)
+    if (used[i]) r.nwarps = i + 1;
+  return r;
+}
+
 struct GeoP {
   int nslot, q_off, p1_off, ring_off, wz_off, rec_off, red_off, bar_off, tmem_off, total, rec_floats, p1_bytes;
 };
@@ -607,12 +653,12 @@ __host__ __device__ inline GeoP make_geo_p(int HPG, int R, int rlast, int nslot)
   return g;
 }
 
-template <typename E, int HPG, int R, int CS>
-__global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
+template <typename E, int HPG, int R, int CS, int NW>
+__global__ void __launch_bounds__(32 * NW, 1)
     dc_tcp_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kl,
                   const __grid_constant__ CUtensorMap tm_vl, const __grid_constant__ CUtensorMap tm_o,
-                  const TcParams p, const int nkt, const int rlast, const int nslot) {
+                  const TcParams p, const int nkt, const int rlast, const int nslot, const WarpRoles roles) {
   constexpr int BM = NQ / HPG;
   constexpr int GI = 32 / HPG;
   constexpr int NG = BM / GI;
@@ -635,10 +681,12 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
   uint64_t *bar_Qfree = bars + 18;                               // [2] staging tile stored (epilogue)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + geo.tmem_off);
 
-  const int ncw = 4 * nkt * CS;  // compose warps
+  const int ncw = roles.ncw;  // compose warps
   const int ncompose = 32 * ncw;
-  const int epi_warp0 = ncw, tma_warp = ncw + 4, mma_warp = ncw + 5;
+  const int nslots = roles.nslots;  // reduction slots: one per (key tile, lane quarter) with keys
+  const int epi_warp0 = roles.epi_leader;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint8_t role = roles.role[warp];
   const int nqb = (p.T + BM - 1) / BM;
   const int ntiles = nqb * p.B * p.G;
   const int H = p.H, T = p.T;
@@ -660,7 +708,7 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
     }
     ptx::fence_mbar_init();
   }
-  if (warp == tma_warp) ptx::tmem_alloc(tmem_slot, 512);
+  if (role == ROLE_TMA) ptx::tmem_alloc(tmem_slot, 512);
   ptx::tc_fence_before();
   __syncthreads();
   ptx::tc_fence_after();
@@ -677,7 +725,7 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
     return kt == 0 ? smem + geo.q_off + buf * NQ * 256 : smem + geo.p1_off + buf * geo.p1_bytes;
   };
 
-  if (warp == tma_warp) {
+  if (role == ROLE_TMA) {
     // ================================================= TMA producer
     if (lane == 0) {
       ptx::tma_prefetch_desc(&tm_q);
@@ -727,7 +775,7 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
         for (int jj = 0; jj < nK && ok; ++jj) load_kv(true, pq0, pb, pg, jj);
     }
     __syncwarp();
-  } else if (warp == mma_warp) {
+  } else if (role == ROLE_MMA) {
     // ================================================= MMA issuer
     if (lane == 0) {
       const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
@@ -793,7 +841,7 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
       if (it >= 1 && ok) pv(it - 1);
     }
     __syncwarp();
-  } else if (warp >= epi_warp0) {
+  } else if ((role & 0xF0) == ROLE_EPI) {
     // ================================================= epilogue: O^T (lanes = d) -> SMEM -> TMA store
     const int quarter = warp & 3, d = 32 * quarter + lane;
     int it = 0;
@@ -833,10 +881,13 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
         TLP_STAMP(it, 6);
       }
     }
-  } else {
+  } else if (role != ROLE_IDLE) {
     // ================================================= compose warps
-    const int sub = warp & 3, kt = (warp >> 2) % nkt, cs = warp / (4 * nkt);
-    const int rw = warp % (4 * nkt);
+    const int sub = role & 3, kt = role >> 3, cs = (role >> 2) & 1;
+    const int rw = kt * 4 + sub;
+    int cord = 0;  // ordinal of this compose warp among the compose warps
+    for (int w = 0; w < warp; ++w) cord += roles.role[w] < 0x40;
+    const int ctid = cord * 32 + lane;  // compose-local thread index
     const int g_begin = cs * (NG / CS), g_end = g_begin + NG / CS;
     const int s_local = 32 * sub + lane;
     const int rows_kt = rows_of[kt];
@@ -855,13 +906,13 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
       // previous tile's pass 2 is finished by every compose warp before rec / red are rewritten
       ptx::named_bar_sync(1, ncompose);
       if (it == 0)
-        for (int idx = threadIdx.x; idx < 2 * HPG * HPG; idx += ncompose) {
+        for (int idx = ctid; idx < 2 * HPG * HPG; idx += ncompose) {
           const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
           const TermPtrs &tm = set ? p.post : p.pre;
           const int hp = j / HPG, h = j % HPG;
           Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
         }
-      for (int idx = threadIdx.x; idx < 2 * BM * geo.rec_floats; idx += ncompose) {
+      for (int idx = ctid; idx < 2 * BM * geo.rec_floats; idx += ncompose) {
         const int set = idx / (BM * geo.rec_floats), rem = idx % (BM * geo.rec_floats);
         const int i = rem / geo.rec_floats, j = rem % geo.rec_floats;
         const TermPtrs &tm = set ? p.post : p.pre;
@@ -955,19 +1006,18 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
       }
       ptx::tmem_wait_st();
       ptx::named_bar_sync(1, ncompose);
-      if (threadIdx.x < NQ) {
-        const int j = threadIdx.x;
+      for (int j = ctid; j < NQ; j += ncompose) {
         float m = -INFINITY;
-        for (int w = 0; w < 4 * nkt; ++w) m = fmaxf(m, redm[w * NQ + j]);
+        for (int w = 0; w < nslots; ++w) m = fmaxf(m, redm[w * NQ + j]);
         float l = 0.f;
-        for (int w = 0; w < 4 * nkt; ++w) {
+        for (int w = 0; w < nslots; ++w) {
           const float mw = redm[w * NQ + j];
           const float f = mw == -INFINITY ? 0.f : exp2f((mw - m) * sl2e);
           redm[w * NQ + j] = f;
           l += reds[w * NQ + j] * f;
         }
         const float il = l > 0.f ? 1.f / l : 0.f;
-        for (int w = 0; w < 4 * nkt; ++w) redm[w * NQ + j] *= il;
+        for (int w = 0; w < nslots; ++w) redm[w * NQ + j] *= il;
       }
       ptx::named_bar_sync(1, ncompose);
       if (threadIdx.x == 0) TLP_STAMP(it, 2);
@@ -1045,7 +1095,7 @@ __global__ void __launch_bounds__(32 * (8 * CS + 6), 1)
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (warp == tma_warp) {
+  if (role == ROLE_TMA) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tbase, 512);
   }
@@ -1179,13 +1229,14 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
   tp.err_flag = p.err_flag;
   tp.pre = to_ptrs(p.pre);
   tp.post = to_ptrs(p.post);
-  auto kern = dc_tcp_kernel<E, HPG, R, CS>;
+  const WarpRoles roles = make_roles(nkt, rlast, CS);
+  auto kern = roles.nwarps <= 18 ? dc_tcp_kernel<E, HPG, R, CS, 18> : dc_tcp_kernel<E, HPG, R, CS, 22>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int ntiles = (p.T + BM - 1) / BM * p.B * p.G;
   dim3 grid(ntiles < sm_count() ? ntiles : sm_count());
-  dim3 block(32 * (4 * nkt * CS + 6));
-  kern<<<grid, block, smem, st>>>(mq, mk, mv, mkl, mvl, mo, tp, nkt, rlast, nslot);
+  dim3 block(32 * roles.nwarps);
+  kern<<<grid, block, smem, st>>>(mq, mk, mv, mkl, mvl, mo, tp, nkt, rlast, nslot, roles);
   return cudaGetLastError();
 }
 
