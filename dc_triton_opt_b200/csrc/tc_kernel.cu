@@ -672,7 +672,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
   float *rec = reinterpret_cast<float *>(smem + geo.rec_off);
   float *red = reinterpret_cast<float *>(smem + geo.red_off);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + geo.bar_off);
-  uint64_t *bar_full = bars + 0, *bar_free = bars + 3;          // ring
+  uint64_t *bar_full = bars + 0, *bar_free = bars + 22;         // ring (up to 4 slots each)
   uint64_t *bar_q = bars + 6;                                    // [2] Q landed
   uint64_t *bar_S = bars + 8;                                    // [2][2] S of (buffer, key tile) ready
   uint64_t *bar_P = bars + 12;                                   // [2] P' written (compose warps)
@@ -693,7 +693,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
   const int rows_of[2] = {nkt == 1 ? rlast : KT_ROWS, rlast};
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < 3; ++i) {
+    for (int i = 0; i < 4; ++i) {
       ptx::mbar_init(bar_full + i, 1);
       ptx::mbar_init(bar_free + i, 1);
     }
@@ -1208,8 +1208,10 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
   constexpr int CS = 2;
   const int nkt = num_key_tiles(HPG, p.window);
   const int rlast = last_tile_rows(HPG, p.window);
+  // deepest K/V ring that fits, at most 3 slots: a 4th slot (SMEM ~226 KB)
+  // measured slower, the smaller L1 then serves spills and weight loads worse
   int nslot = 3;
-  if (make_geo_p(HPG, R, rlast, nslot).total + 1024 > 227 * 1024) nslot = 2;
+  while (nslot > 2 && make_geo_p(HPG, R, rlast, nslot).total + 1024 > 227 * 1024) --nslot;
   const size_t smem = make_geo_p(HPG, R, rlast, nslot).total + 1024;
   const int64_t sb = (int64_t)p.T * p.H * D, st_ = (int64_t)p.H * D, sh = D;
   CUtensorMap mq, mk, mv, mkl, mvl, mo;
