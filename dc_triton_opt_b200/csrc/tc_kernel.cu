@@ -642,14 +642,21 @@ __host__ __device__ inline GeoP make_geo_p(int HPG, int R, int rlast, int nslot)
   g.p1_bytes = round_up(HPG * rlast * BM * 2, 1024);
   g.p1_off = 2 * NQ * 256;                       // 2 x P'(tile 1)
   g.ring_off = g.p1_off + 2 * g.p1_bytes;
-  int o = g.ring_off + nslot * TILE_BYTES;
+  // the short last key tile of all heads may share one slot (see packed_last);
+  // the QK MMA then reads 128 rows from each head's half: pad the ring's end
+  // (the read-only over-read may run into the data placed after the ring, as
+  // long as it stays inside this CTA's shared memory)
+  int pad = 0;
+  if (HPG > 1 && HPG * rlast * 256 <= TILE_BYTES) pad = (2 * HPG - 1) * rlast * 128 + TILE_BYTES / 2 - TILE_BYTES;
+  const int ring_end = g.ring_off + nslot * TILE_BYTES;
+  int o = ring_end;
   g.rec_floats = round_up(HPG * (2 * R + 1), 4);
   g.wz_off = o;  o += 2 * HPG * HPG * 4;
   g.rec_off = round_up(o, 16); o = g.rec_off + 2 * BM * g.rec_floats * 4;
   g.red_off = o; o += 2 * 8 * NQ * 4;
   g.bar_off = round_up(o, 8); o = g.bar_off + 32 * 8;
   g.tmem_off = o; o += 16;
-  g.total = o;
+  g.total = o > ring_end + pad ? o : ring_end + pad;
   return g;
 }
 
@@ -691,6 +698,20 @@ __global__ void __launch_bounds__(32 * NW, 1)
   const int ntiles = nqb * p.B * p.G;
   const int H = p.H, T = p.T;
   const int rows_of[2] = {nkt == 1 ? rlast : KT_ROWS, rlast};
+  // K/V jobs of one tile: one per (key tile, head), except that the short last
+  // key tile of all heads is packed into a single job when it fits one slot
+  const bool packed_last = HPG > 1 && HPG * rlast * 256 <= TILE_BYTES;
+  const int nK = HPG * (nkt - 1) + (packed_last ? 1 : HPG);
+  struct Job { int kt, h0, nh, rows, half; };  // half: byte distance of the d-halves
+  auto job_of = [&](int jj) {
+    Job j;
+    if (jj < HPG * (nkt - 1)) { j.kt = jj / HPG; j.h0 = jj % HPG; j.nh = 1; }
+    else if (packed_last) { j.kt = nkt - 1; j.h0 = 0; j.nh = HPG; }
+    else { j.kt = nkt - 1; j.h0 = jj - HPG * (nkt - 1); j.nh = 1; }
+    j.rows = rows_of[j.kt];
+    j.half = (packed_last && j.kt == nkt - 1) ? j.rows * 128 : TILE_BYTES / 2;
+    return j;
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < 4; ++i) {
@@ -731,7 +752,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
       ptx::tma_prefetch_desc(&tm_q);
       ptx::tma_prefetch_desc(&tm_k);
       ptx::tma_prefetch_desc(&tm_v);
-      const int nK = HPG * nkt;
       int job = 0;
       bool ok = true;
       auto load_kv = [&](bool isv, int q0, int b, int g, int jj) {
@@ -741,14 +761,16 @@ __global__ void __launch_bounds__(32 * NW, 1)
           record_err(p, ERR_TIMEOUT_FREE);
           return;
         }
-        const int kt = jj / HPG, h = jj % HPG;
-        const bool last = kt == nkt - 1;
+        const Job jb = job_of(jj);
+        const bool last = jb.kt == nkt - 1;
         const CUtensorMap *m = isv ? (last ? &tm_vl : &tm_v) : (last ? &tm_kl : &tm_k);
         const int kb = q0 - p.window + 1;
-        ptx::mbar_expect_tx(bar_full + slot, rows_of[kt] * 256);
+        ptx::mbar_expect_tx(bar_full + slot, jb.nh * jb.rows * 256);
         unsigned char *dst = smem + geo.ring_off + slot * TILE_BYTES;
-        ptx::tma_load_4d(dst, m, bar_full + slot, 0, g * HPG + h, kb + kt * KT_ROWS, b);
-        ptx::tma_load_4d(dst + TILE_BYTES / 2, m, bar_full + slot, 64, g * HPG + h, kb + kt * KT_ROWS, b);
+        for (int u = 0; u < jb.nh; ++u)
+          for (int c = 0; c < 2; ++c)
+            ptx::tma_load_4d(dst + u * 2 * jb.half + c * jb.half, m, bar_full + slot, c * 64, g * HPG + jb.h0 + u,
+                             kb + jb.kt * KT_ROWS, b);
         ++job;
       };
       int pq0 = 0, pb = 0, pg = 0;
@@ -782,7 +804,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 128, BM);
       const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 128, BM);
       const uint32_t ring_addr = ptx::smem_u32(smem + geo.ring_off);
-      const int nK = HPG * nkt;
       int job = 0;
       bool ok = true;
       auto pv = [&](int pit) {
@@ -793,14 +814,17 @@ __global__ void __launch_bounds__(32 * NW, 1)
           const int slot = job % nslot;
           if (!ptx::mbar_wait(bar_full + slot, (job / nslot) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); return; }
           ptx::tc_fence_after();
-          const int kt = jj / HPG, h = jj % HPG;
-          const int rows = rows_of[kt];
-          const uint32_t a0 = ring_addr + slot * TILE_BYTES;
-          const uint32_t b0 = ptx::smem_u32(p_tile(buf, kt)) + h * (rows * BM * 2);
-          for (int ks = 0; ks < rows / 16; ++ks) {
-            const uint64_t ad = ptx::smem_desc(a0 + ks * 2048, TILE_BYTES / 2, 1024, 2);
-            const uint64_t bd = ptx::smem_desc(b0 + ks * (2 * BM * 16), BM * 16, 128, 0);
-            ptx::mma_f16_ss(tbase + buf * 256 + h * BM, ad, bd, idesc_pv, (kt > 0 || ks > 0));
+          const Job jb = job_of(jj);
+          for (int u = 0; u < jb.nh; ++u) {
+            const int h = jb.h0 + u;
+            const uint32_t a0 = ring_addr + slot * TILE_BYTES + u * 2 * jb.half;
+            const uint32_t b0 = ptx::smem_u32(p_tile(buf, jb.kt)) + h * (jb.rows * BM * 2);
+            for (int ks = 0; ks < jb.rows / 16; ++ks) {
+              // V: MN-major 128B swizzle, 8-key groups 1024 B apart, d halves jb.half apart
+              const uint64_t ad = ptx::smem_desc(a0 + ks * 2048, jb.half, 1024, 2);
+              const uint64_t bd = ptx::smem_desc(b0 + ks * (2 * BM * 16), BM * 16, 128, 0);
+              ptx::mma_f16_ss(tbase + buf * 256 + h * BM, ad, bd, idesc_pv, (jb.kt > 0 || ks > 0));
+            }
           }
           ptx::mma_commit(bar_free + slot);
         }
@@ -822,17 +846,20 @@ __global__ void __launch_bounds__(32 * NW, 1)
           const int slot = job % nslot;
           if (!ptx::mbar_wait(bar_full + slot, (job / nslot) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
           ptx::tc_fence_after();
-          const int kt = jj / HPG, h = jj % HPG;
-          const uint32_t a0 = ring_addr + slot * TILE_BYTES;
-          const uint32_t b0 = q_addr + h * BM * 256;
+          const Job jb = job_of(jj);
+          for (int u = 0; u < jb.nh; ++u) {
+            const int h = jb.h0 + u;
+            const uint32_t a0 = ring_addr + slot * TILE_BYTES + u * 2 * jb.half;
+            const uint32_t b0 = q_addr + h * BM * 256;
 #pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks) {
-            const uint64_t ad = ptx::smem_desc(a0 + (ks >> 2) * (TILE_BYTES / 2) + (ks & 3) * 32, 16, 1024, 2);
-            const uint64_t bd = ptx::smem_desc(b0 + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 16, 1024, 2);
-            ptx::mma_f16_ss(tbase + buf * 256 + kt * KT_ROWS + h * BM, ad, bd, idesc_qk, ks > 0);
+            for (int ks = 0; ks < D / 16; ++ks) {
+              const uint64_t ad = ptx::smem_desc(a0 + (ks >> 2) * jb.half + (ks & 3) * 32, 16, 1024, 2);
+              const uint64_t bd = ptx::smem_desc(b0 + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 16, 1024, 2);
+              ptx::mma_f16_ss(tbase + buf * 256 + jb.kt * KT_ROWS + h * BM, ad, bd, idesc_qk, ks > 0);
+            }
           }
           ptx::mma_commit(bar_free + slot);
-          if (h == HPG - 1) ptx::mma_commit(bar_S + 2 * buf + kt);
+          if (jb.h0 + jb.nh == HPG) ptx::mma_commit(bar_S + 2 * buf + jb.kt);
         }
         TLP_STAMP(it, 9);
         if (it >= 1 && ok) pv(it - 1);
@@ -969,7 +996,12 @@ __global__ void __launch_bounds__(32 * NW, 1)
             float a[HPG], o[HPG];
 #pragma unroll
             for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
+#ifndef DC_EXP_NOCOMPOSE
             compose<HPG, R>(a, o, Wreg, rec + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+#else
+#pragma unroll
+            for (int h = 0; h < HPG; ++h) o[h] = a[h];
+#endif
             const bool vl = valid(q0 + i0 + ii);
 #pragma unroll
             for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : -INFINITY;
@@ -978,9 +1010,17 @@ __global__ void __launch_bounds__(32 * NW, 1)
           for (int h = 0; h < HPG; ++h)
 #pragma unroll
             for (int ii = 0; ii < GI; ++ii) {
+#ifndef DC_EXP_NOREDUX
               const float mw = ptx::warp_max(v[h][ii]);
+#else
+              const float mw = 0.f;
+#endif
               if (lane == h * GI + ii) mine_m = mw;
+#ifndef DC_EXP_NOEXP
               v[h][ii] = exp2f((v[h][ii] - (mw == -INFINITY ? 0.f : mw)) * sl2e);
+#else
+              v[h][ii] = (v[h][ii] - (mw == -INFINITY ? 0.f : mw)) * sl2e;
+#endif
             }
 #pragma unroll
           for (int h = 0; h < HPG; ++h) ptx::tmem_st<GI>(tl + h * BM + i0, v[h]);
@@ -989,6 +1029,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
           for (int h = 0; h < HPG; ++h)
 #pragma unroll
             for (int ii = 0; ii < GI; ++ii) x[h * GI + ii] = v[h][ii];
+#ifndef DC_EXP_NOSUM
 #pragma unroll
           for (int off = 16, cnt = 32; off >= 1; off >>= 1, cnt >>= 1) {
             const bool upper = (lane & off) != 0;
@@ -999,6 +1040,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
               x[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
             }
           }
+#endif
           mine_s = x[0];
         }
         redm[rw * NQ + col_of(lane, i0)] = mine_m;
