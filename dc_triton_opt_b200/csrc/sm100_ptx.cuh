@@ -40,14 +40,36 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait for the phase with the given parity to complete.  Gives up after
-// ~max_iters polls (with nanosleep back-off) and returns false.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t max_iters = (1u << 24)) {
-  for (uint32_t i = 0; i < max_iters; ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if (i > 64) __nanosleep(i > 4096 ? 256 : 32);
+// try_wait with a suspend-time hint: the thread sleeps in hardware until the
+// phase completes or ~hint_ns elapse, instead of spinning on issue slots.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Wait for the phase with the given parity to complete.  Gives up (returns
+// false) after about `limit` / 8 microseconds of wall-clock time (default
+// ~2 s): every wait of the kernels is bounded.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = (1u << 24)) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t deadline = globaltimer_ns() + (static_cast<uint64_t>(limit) >> 3) * 1000ull;
+  while (!mbar_try_wait_sleep(bar, parity, 20000)) {
+    if (globaltimer_ns() > deadline) return false;
   }
-  return false;
+  return true;
 }
 
 // ---------------------------------------------------------------- fences

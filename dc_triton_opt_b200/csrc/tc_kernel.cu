@@ -247,7 +247,7 @@ __global__ void __launch_bounds__(MAXT, 1)
       // jobs are key-tile major: job j -> key tile j / HPG, head j % HPG; K jobs then V jobs
       for (int j = 0; j < total; ++j) {
         const int slot = j % nslot, use = j / nslot;
-        if (use > 0 && !ptx::mbar_wait(bar_free + slot, (use - 1) & 1, 1u << 26)) {
+        if (use > 0 && !ptx::mbar_wait(bar_free + slot, (use - 1) & 1, 1u << 24)) {
           record_err(p, ERR_TIMEOUT_FREE);
           break;
         }
@@ -275,12 +275,12 @@ __global__ void __launch_bounds__(MAXT, 1)
       const int nslot = geo.nslot;
       const int nK = HPG * nkt, total = 2 * nK;
       bool ok = true;
-      if (!ptx::mbar_wait(bar_q, 0, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_Q); }
+      if (!ptx::mbar_wait(bar_q, 0, 1u << 24)) { ok = false; record_err(p, ERR_TIMEOUT_Q); }
       TL_STAMP(2);
       // ---- S^T_h = K_h Q_h^T; key tile kt is signalled as soon as its heads are issued
       for (int j = 0; j < nK && ok; ++j) {
         const int slot = j % nslot;
-        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
+        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1, 1u << 24)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
         if (j < 12) TL_STAMP(12 + j);
         ptx::tc_fence_after();
         const int kt = j / HPG, h = j % HPG;
@@ -297,12 +297,12 @@ __global__ void __launch_bounds__(MAXT, 1)
       }
       TL_STAMP(3);
       // ---- O^T_h = V_h^T P'^T_h, accumulated over key tiles
-      if (ok && !ptx::mbar_wait(bar_P, 0, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_P); }
+      if (ok && !ptx::mbar_wait(bar_P, 0, 1u << 24)) { ok = false; record_err(p, ERR_TIMEOUT_P); }
       TL_STAMP(7);
       ptx::tc_fence_after();
       for (int j = nK; j < total && ok; ++j) {
         const int slot = j % nslot;
-        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
+        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1, 1u << 24)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
         ptx::tc_fence_after();
         const int jj = j - nK, kt = jj / HPG, h = jj % HPG;
         const int ksteps = (kt == nkt - 1 ? rlast : KT_ROWS) / 16;
@@ -526,7 +526,7 @@ __global__ void __launch_bounds__(MAXT, 1)
     if (threadIdx.x == 0) TL_STAMP(6);
 
     // ---- epilogue: O^T (lanes = d) -> SMEM [head][d half][query][64 d] -> TMA store
-    if (!ptx::mbar_wait(bar_O, 0, 1u << 26)) { ok = false; record_err(p, ERR_TIMEOUT_O); }
+    if (!ptx::mbar_wait(bar_O, 0, 1u << 24)) { ok = false; record_err(p, ERR_TIMEOUT_O); }
     ptx::tc_fence_after();
     if (threadIdx.x == 0) TL_STAMP(8);
     unsigned char *stage = smem + geo.q_off;  // Q is dead once every MMA has completed
@@ -734,7 +734,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t WAIT = 1u << 26;
+  const uint32_t WAIT = 1u << 24;
 
   // tile -> (query block, batch, group)
   auto tile_coords = [&](int tile, int &q0, int &b, int &g) {
