@@ -159,11 +159,7 @@ def dist_setup():
     return world, rank, local
 
 
-def shard_batch(B, world, rank):
-    """Contiguous batch slice [b0, b1) of this rank (even split, remainder to the first ranks)."""
-    base, rem = divmod(B, world)
-    b0 = rank * base + min(rank, rem)
-    return b0, b0 + base + (1 if rank < rem else 0)
+from dc_triton_opt_b200.shard import max_over_ranks, shard_batch  # noqa: E402
 
 
 _CPU_INPUTS = {}
@@ -267,12 +263,7 @@ def run_ours(args, cfg, world, rank, local):
             call()
         ev1.record(stream)
         barrier()
-    ms = ev0.elapsed_time(ev1)
-    ms_max = ms
-    if world > 1:
-        t = torch.tensor([ms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms_max = float(t.item())
+    ms_max = max_over_ranks(ev0.elapsed_time(ev1), device)
     ms_step = ms_max / args.steps
 
     # end to end: pinned host inputs -> device, forward, output -> host, every step
@@ -305,11 +296,7 @@ def run_ours(args, cfg, world, rank, local):
         e2e_step()
     ev1.record(stream)
     barrier()
-    e2e_ms = ev0.elapsed_time(ev1) / e2e_steps
-    if world > 1:
-        t = torch.tensor([e2e_ms], device=device)
-        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+    e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / e2e_steps, device)
 
     fl_rank = flops(B, H, D, G, R, pairs(T, W))
     total_fl = fl_rank * world
