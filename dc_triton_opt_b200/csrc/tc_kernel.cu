@@ -118,12 +118,43 @@ __device__ __forceinline__ void record_err(const TcParams &p, int code) {
   atomicCAS(dst, 0, code);
 }
 
+// Static head mix of a group, stored transposed with a zero diagonal:
+// wt[h * HPG + hp] = w[g, hp, h] for hp != h.  Up to HPG = 4 it is held in
+// registers; for larger groups it is read from shared memory (broadcast float4
+// loads) to keep the compose threads free of register spills.
+template <int HPG, bool REG = (HPG <= 4)>
+struct WSrc;
+template <int HPG>
+struct WSrc<HPG, true> {
+  float v[HPG * HPG];
+  __device__ __forceinline__ void load(const float *smem_wt) {
+#pragma unroll
+    for (int j = 0; j < HPG * HPG; ++j) v[j] = smem_wt[j];
+  }
+  __device__ __forceinline__ void row(int h, float (&r)[HPG]) const {
+#pragma unroll
+    for (int hp = 0; hp < HPG; ++hp) r[hp] = v[h * HPG + hp];
+  }
+};
+template <int HPG>
+struct WSrc<HPG, false> {
+  const float *p;
+  __device__ __forceinline__ void load(const float *smem_wt) { p = smem_wt; }
+  __device__ __forceinline__ void row(int h, float (&r)[HPG]) const {
+#pragma unroll
+    for (int hp = 0; hp < HPG; hp += 4) {
+      const float4 x = *reinterpret_cast<const float4 *>(p + h * HPG + hp);
+      r[hp] = x.x; r[hp + 1] = x.y; r[hp + 2] = x.z; r[hp + 3] = x.w;
+    }
+  }
+};
+
 // Composition of one (query, key) pair across the HPG heads of a group.
-// a: per-head inputs; Wz: static mix with zero diagonal; rec: per-query record
-// (dq = w[h,h] + identity + qdd[t,h]; qa = qw1[t,:,r]; qb = qw2[t,r,:]);
-// kw1/kw2/kdd: per-key weights of this thread's key.
+// a: per-head inputs; W: static mix (transposed, zero diagonal); rec:
+// per-query record (dq = w[h,h] + identity + qdd[t,h]; qa = qw1[t,:,r];
+// qb = qw2[t,r,:]); kw1/kw2/kdd: per-key weights of this thread's key.
 template <int HPG, int R>
-__device__ __forceinline__ void compose(const float (&a)[HPG], float (&o)[HPG], const float (&Wz)[HPG * HPG],
+__device__ __forceinline__ void compose(const float (&a)[HPG], float (&o)[HPG], const WSrc<HPG> &W,
                                         const float *rec, const float (&kw1)[HPG * R],
                                         const float (&kw2)[R * HPG], const float (&kdd)[HPG]) {
   float r4[round_up(HPG * (2 * R + 1), 4)];
@@ -146,10 +177,12 @@ __device__ __forceinline__ void compose(const float (&a)[HPG], float (&o)[HPG], 
   }
 #pragma unroll
   for (int h = 0; h < HPG; ++h) {
+    float wr[HPG];
+    W.row(h, wr);
     float x = (dq[h] + kdd[h]) * a[h];
 #pragma unroll
     for (int hp = 0; hp < HPG; ++hp)
-      if (hp != h) x = fmaf(Wz[hp * HPG + h], a[hp], x);
+      if (hp != h) x = fmaf(wr[hp], a[hp], x);
 #pragma unroll
     for (int r = 0; r < R; ++r) x = fmaf(qb[r * HPG + h], aq[r], fmaf(kw2[r * HPG + h], ak[r], x));
     o[h] = x;
@@ -328,7 +361,7 @@ __global__ void __launch_bounds__(MAXT, 1)
     for (int idx = threadIdx.x; idx < 2 * HPG * HPG; idx += ncompose) {
       const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
       const TermPtrs &tm = set ? p.post : p.pre;
-      const int hp = j / HPG, h = j % HPG;
+      const int h = j / HPG, hp = j % HPG;
       Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
     }
     for (int idx = threadIdx.x; idx < 2 * BM * geo.rec_floats; idx += ncompose) {
@@ -372,7 +405,7 @@ __global__ void __launch_bounds__(MAXT, 1)
     const float sl2e = p.scale * kLog2e;
     bool ok = true;
 
-    float Wreg[HPG * HPG];
+    WSrc<HPG> Wreg;
     float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
 
     auto valid = [&](int t) { return key_ok && s <= t && t - s < p.window && t < T; };
@@ -383,8 +416,7 @@ __global__ void __launch_bounds__(MAXT, 1)
     if (active) load_key_weights<E, HPG, R>(p.pre, ktok, H, hbase, key_ok, kw1, kw2, kdd);
     ptx::named_bar_sync(1, ncompose);  // staged weights visible
     if (active) {
-#pragma unroll
-      for (int j = 0; j < HPG * HPG; ++j) Wreg[j] = Wz[j];
+Wreg.load(Wz);
     }
     if (!ptx::mbar_wait(bar_S + kt, 0)) { ok = false; record_err(p, ERR_TIMEOUT_S); }
     ptx::tc_fence_after();
@@ -465,8 +497,7 @@ __global__ void __launch_bounds__(MAXT, 1)
 
     // ---- pass 2: normalise, post-composition, P' -> SMEM (PV B operand)
     if (active && ok) {
-#pragma unroll
-      for (int j = 0; j < HPG * HPG; ++j) Wreg[j] = Wz[HPG * HPG + j];
+Wreg.load(Wz + HPG * HPG);
       load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
     }
     const float *fac = redm + rw * NQ;
@@ -921,7 +952,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     const float sl2e = p.scale * kLog2e;
     float *redm = red, *reds = red + 4 * nkt * NQ;
     auto col_of = [&](int L, int i0) { return (L / GI) * BM + i0 + (L % GI); };
-    float Wreg[HPG * HPG];
+    WSrc<HPG> Wreg;
     float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
     int it = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
@@ -936,7 +967,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
         for (int idx = ctid; idx < 2 * HPG * HPG; idx += ncompose) {
           const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
           const TermPtrs &tm = set ? p.post : p.pre;
-          const int hp = j / HPG, h = j % HPG;
+          const int h = j / HPG, hp = j % HPG;
           Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
         }
       for (int idx = ctid; idx < 2 * BM * geo.rec_floats; idx += ncompose) {
@@ -972,8 +1003,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
       if (active) load_key_weights<E, HPG, R>(p.pre, ktok, H, hbase, key_ok, kw1, kw2, kdd);
       ptx::named_bar_sync(1, ncompose);  // staged weights visible
       if (active) {
-#pragma unroll
-        for (int j = 0; j < HPG * HPG; ++j) Wreg[j] = Wz[j];
+Wreg.load(Wz);
       }
       if (threadIdx.x == 0) TLP_STAMP(it, 0);
       bool ok = ptx::mbar_wait(bar_S + 2 * buf + kt, (it >> 1) & 1, WAIT);
@@ -1071,8 +1101,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
 
       // ---- pass 2: normalise, post-composition, P' -> SMEM
       if (active && ok) {
-#pragma unroll
-        for (int j = 0; j < HPG * HPG; ++j) Wreg[j] = Wz[HPG * HPG + j];
+Wreg.load(Wz + HPG * HPG);
         load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
       }
       const float *fac = redm + rw * NQ;
