@@ -178,7 +178,7 @@ def select_kernel(q, k, v, pre=None, post=None, window=None, G=1) -> str:
                     setattr(st, f.name, 16)
     rc = _lib.load().dc_attn_select_kernel(ctypes.byref(p))
     _lib.check(rc if rc < 0 else 0, "dc_attn_select_kernel")
-    return {1: "simt", 2: "tc"}[rc]
+    return {1: "simt", 2: "tc", 3: "tcs"}[rc]
 
 
 def _residual_call(q, k, v, dc_weights, scaling, window, seq_lens, G, out):

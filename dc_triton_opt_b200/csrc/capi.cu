@@ -18,6 +18,8 @@ cudaError_t launch_simt(const ParamsDev &p, int dtype, cudaStream_t st);
 size_t simt_smem_bytes(int HPG, int D, int R, int dtype);
 bool tc_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tc(const dc_attn_params &p, cudaStream_t st);
+bool tcs_supports(const dc_attn_params &p, std::string *why);
+cudaError_t launch_tcs(const dc_attn_params &p, cudaStream_t st);
 }  // namespace dcattn
 
 namespace {
@@ -79,8 +81,15 @@ int select_kernel(const dc_attn_params &p) {
     if (!tc_ok) return fail(DC_ERR_UNSUPPORTED, "tensor-core kernel does not support this call: %s", why.c_str());
     return DC_KERNEL_TC;
   }
+  std::string why_s;
+  const bool tcs_ok = dcattn::tcs_supports(p, &why_s);
+  if (p.kernel == DC_KERNEL_TCS) {
+    if (!tcs_ok)
+      return fail(DC_ERR_UNSUPPORTED, "streaming tensor-core kernel does not support this call: %s", why_s.c_str());
+    return DC_KERNEL_TCS;
+  }
   if (p.kernel != DC_KERNEL_AUTO) return fail(DC_ERR_SHAPE, "unknown kernel selector %d", p.kernel);
-  return tc_ok ? DC_KERNEL_TC : DC_KERNEL_SIMT;
+  return tc_ok ? DC_KERNEL_TC : tcs_ok ? DC_KERNEL_TCS : DC_KERNEL_SIMT;
 }
 
 int check_device() {
@@ -120,6 +129,8 @@ int dc_attn_fwd(const dc_attn_params *pp, void *stream) {
   cudaError_t e;
   if (which == DC_KERNEL_TC) {
     e = dcattn::launch_tc(p, st);
+  } else if (which == DC_KERNEL_TCS) {
+    e = dcattn::launch_tcs(p, st);
   } else {
     e = dcattn::launch_simt(dcattn::to_dev(p), p.dtype, st);
   }

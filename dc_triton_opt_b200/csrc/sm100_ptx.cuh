@@ -153,6 +153,12 @@ template <int N> __device__ __forceinline__ void tmem_st(uint32_t taddr, const f
 
 #define DC_U(x) __float_as_uint(x)
 
+template <> __device__ __forceinline__ void tmem_ld<2>(uint32_t a, float (&v)[2]) {
+  uint32_t r[2];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x2.b32 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(a));
+  v[0] = __uint_as_float(r[0]);
+  v[1] = __uint_as_float(r[1]);
+}
 template <> __device__ __forceinline__ void tmem_ld<4>(uint32_t a, float (&v)[4]) {
   uint32_t r[4];
   asm volatile("tcgen05.ld.sync.aligned.32x32b.x4.b32 {%0,%1,%2,%3}, [%4];"

@@ -1,0 +1,258 @@
+// Shared pieces of the tensor-core DC-attention kernels (sm_100a):
+// tile constants, kernel parameters, the cross-head composition of one
+// (query, key) pair, per-key weight loads, and the host-side TMA tensor maps.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace dcattn {
+namespace tc {
+
+
+constexpr int NQ = 128;          // (head, query) columns per CTA
+constexpr int KT_ROWS = 128;     // keys per key tile (TMEM lanes)
+constexpr int TILE_BYTES = KT_ROWS * 128 * 2;  // one K or V tile: 128 rows x 128 d x 2 B
+constexpr int D = 128;
+
+enum Err { ERR_TIMEOUT_Q = 1, ERR_TIMEOUT_FULL = 2, ERR_TIMEOUT_FREE = 3, ERR_TIMEOUT_S = 4,
+           ERR_TIMEOUT_P = 5, ERR_TIMEOUT_O = 6 };
+
+struct Geo {
+  int nkt, nslot;
+  int q_off, ring_off, p_off, misc_off;
+  int wz_off, rec_off, red_off, bar_off, tmem_off;
+  int rec_floats;  // per (set, query) record: dq[HPG] | qa[HPG*R] | qb[R*HPG], padded to 4
+  int total;
+};
+
+__host__ __device__ constexpr int round_up(int x, int a) { return (x + a - 1) / a * a; }
+
+__host__ __device__ inline Geo make_geo(int HPG, int R, int nkt) {
+  Geo g{};
+  const int BM = NQ / HPG;
+  g.nkt = nkt;
+  g.nslot = nkt == 3 ? 2 : 3;
+  g.q_off = 0;
+  g.ring_off = g.q_off + NQ * 256;
+  g.p_off = g.ring_off + g.nslot * TILE_BYTES;
+  g.misc_off = g.p_off + nkt * NQ * KT_ROWS * 2;
+  g.rec_floats = round_up(HPG * (2 * R + 1), 4);
+  int o = g.misc_off;
+  g.wz_off = o;   o += 2 * HPG * HPG * 4;
+  g.rec_off = round_up(o, 16); o = g.rec_off + 2 * BM * g.rec_floats * 4;
+  g.red_off = o;  o += 2 * 4 * nkt * NQ * 4;
+  g.bar_off = round_up(o, 8); o = g.bar_off + 16 * 8;
+  g.tmem_off = o; o += 16;
+  g.total = o;
+  return g;
+}
+
+struct TermPtrs {
+  int identity;
+  const float *w;
+  const void *qw1, *qw2, *kw1, *kw2, *qdd, *kdd;
+};
+
+struct TcParams {
+  int B, T, H, G, window, slen_default;
+  float scale;
+  const int32_t *seq_lens;
+  void *out;
+  int64_t out_sb, out_st, out_sh;
+  int32_t *err_flag;
+  TermPtrs pre, post;
+};
+
+static __device__ int g_default_err;
+
+#ifdef DC_TIMELINE
+// development builds only: clock64 stamps of the phases (per CTA; the
+// persistent kernel records CTA 0 per tile iteration)
+__device__ unsigned long long g_timeline[8192][40];
+#define TLP_STAMP(it, i)                                                 \
+  do {                                                                   \
+    if (blockIdx.x == 0 && (it) < 8192) g_timeline[(it)][i] = clock64(); \
+  } while (0)
+#define TL_STAMP(i)                                                                   \
+  do {                                                                                \
+    const int cta_ = blockIdx.y * gridDim.x + blockIdx.x;                             \
+    if (cta_ < 8192) g_timeline[cta_][i] = clock64();                                 \
+  } while (0)
+#else
+#define TLP_STAMP(it, i) \
+  do {                   \
+  } while (0)
+#define TL_STAMP(i) \
+  do {              \
+  } while (0)
+#endif  // error sink when the caller passes no err_flag
+
+__device__ __forceinline__ void record_err(const TcParams &p, int code) {
+  int *dst = p.err_flag ? p.err_flag : &g_default_err;
+  atomicCAS(dst, 0, code);
+}
+
+// Static head mix of a group, stored transposed with a zero diagonal:
+// wt[h * HPG + hp] = w[g, hp, h] for hp != h.  Up to HPG = 4 it is held in
+// registers; for larger groups it is read from shared memory (broadcast float4
+// loads) to keep the compose threads free of register spills.
+template <int HPG, bool REG = (HPG <= 4)>
+struct WSrc;
+template <int HPG>
+struct WSrc<HPG, true> {
+  float v[HPG * HPG];
+  __device__ __forceinline__ void load(const float *smem_wt) {
+#pragma unroll
+    for (int j = 0; j < HPG * HPG; ++j) v[j] = smem_wt[j];
+  }
+  __device__ __forceinline__ void row(int h, float (&r)[HPG]) const {
+#pragma unroll
+    for (int hp = 0; hp < HPG; ++hp) r[hp] = v[h * HPG + hp];
+  }
+};
+template <int HPG>
+struct WSrc<HPG, false> {
+  const float *p;
+  __device__ __forceinline__ void load(const float *smem_wt) { p = smem_wt; }
+  __device__ __forceinline__ void row(int h, float (&r)[HPG]) const {
+#pragma unroll
+    for (int hp = 0; hp < HPG; hp += 4) {
+      const float4 x = *reinterpret_cast<const float4 *>(p + h * HPG + hp);
+      r[hp] = x.x; r[hp + 1] = x.y; r[hp + 2] = x.z; r[hp + 3] = x.w;
+    }
+  }
+};
+
+// Composition of one (query, key) pair across the HPG heads of a group.
+// a: per-head inputs; W: static mix (transposed, zero diagonal); rec:
+// per-query record (dq = w[h,h] + identity + qdd[t,h]; qa = qw1[t,:,r];
+// qb = qw2[t,r,:]); kw1/kw2/kdd: per-key weights of this thread's key.
+template <int HPG, int R>
+__device__ __forceinline__ void compose(const float (&a)[HPG], float (&o)[HPG], const WSrc<HPG> &W,
+                                        const float *rec, const float (&kw1)[HPG * R],
+                                        const float (&kw2)[R * HPG], const float (&kdd)[HPG]) {
+  float r4[round_up(HPG * (2 * R + 1), 4)];
+#pragma unroll
+  for (int j = 0; j < round_up(HPG * (2 * R + 1), 4); j += 4) {
+    const float4 x = *reinterpret_cast<const float4 *>(rec + j);
+    r4[j] = x.x; r4[j + 1] = x.y; r4[j + 2] = x.z; r4[j + 3] = x.w;
+  }
+  const float *dq = r4, *qa = r4 + HPG, *qb = r4 + HPG + HPG * R;
+  float aq[R], ak[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) { aq[r] = 0.f; ak[r] = 0.f; }
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      aq[r] = fmaf(qa[h * R + r], a[h], aq[r]);
+      ak[r] = fmaf(kw1[h * R + r], a[h], ak[r]);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) {
+    float wr[HPG];
+    W.row(h, wr);
+    float x = (dq[h] + kdd[h]) * a[h];
+#pragma unroll
+    for (int hp = 0; hp < HPG; ++hp)
+      if (hp != h) x = fmaf(wr[hp], a[hp], x);
+#pragma unroll
+    for (int r = 0; r < R; ++r) x = fmaf(qb[r * HPG + h], aq[r], fmaf(kw2[r * HPG + h], ak[r], x));
+    o[h] = x;
+  }
+}
+
+template <typename E>
+__device__ __forceinline__ float ld_w(const void *base, int64_t idx) {
+  return to_f<E>(reinterpret_cast<const E *>(base)[idx]);
+}
+
+template <typename E, int HPG, int R>
+__device__ __forceinline__ void load_key_weights(const TermPtrs &tm, int64_t tok, int H, int hbase, bool ok,
+                                                 float (&kw1)[HPG * R], float (&kw2)[R * HPG],
+                                                 float (&kdd)[HPG]) {
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      kw1[h * R + r] = (ok && tm.kw1) ? ld_w<E>(tm.kw1, (tok * H + hbase + h) * R + r) : 0.f;
+      kw2[r * HPG + h] = (ok && tm.kw2) ? ld_w<E>(tm.kw2, (tok * R + r) * H + hbase + h) : 0.f;
+    }
+    kdd[h] = (ok && tm.kdd) ? ld_w<E>(tm.kdd, tok * H + hbase + h) : 0.f;
+  }
+}
+
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn get_encode() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void *ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// [B, T, H, D] tensor (element strides sb, st, sh; d contiguous) as a 4-D map
+// (D, H, T, B); box = 64 d x 1 head x rows x 1.
+static bool make_map(CUtensorMap *m, const void *base, int dtype, int B, int T, int H, int rows, int64_t sb,
+                     int64_t st, int64_t sh, bool swizzle) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)sh * 2, (cuuint64_t)st * 2, (cuuint64_t)sb * 2};
+  const cuuint32_t box[4] = {64, 1, (cuuint32_t)rows, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == DC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(m, dt, 4, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             swizzle ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// key span of a query block: BM + window - 1 keys
+static int num_key_tiles(int HPG, int window) {
+  const int BM = NQ / HPG;
+  return (BM + window - 1 + KT_ROWS - 1) / KT_ROWS;
+}
+// rows of the last key tile, rounded up to the 16-key MMA step
+static int last_tile_rows(int HPG, int window) {
+  const int BM = NQ / HPG;
+  const int span = BM + window - 1;
+  const int r = span - KT_ROWS * (num_key_tiles(HPG, window) - 1);
+  return (r + 15) / 16 * 16;
+}
+
+static TermPtrs to_ptrs(const dc_terms &t) {
+  TermPtrs r;
+  r.identity = t.identity;
+  r.w = t.w;
+  r.qw1 = t.qw1; r.qw2 = t.qw2; r.kw1 = t.kw1; r.kw2 = t.kw2; r.qdd = t.qdd; r.kdd = t.kdd;
+  return r;
+}
+
+
+static int sm_count() {
+  static int n[64] = {0};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) cudaDeviceGetAttribute(&n[dev], cudaDevAttrMultiProcessorCount, dev);
+  return n[dev] > 0 ? n[dev] : 148;
+}
+
+}  // namespace tc
+}  // namespace dcattn

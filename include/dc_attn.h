@@ -69,7 +69,10 @@ enum dc_status {
 enum dc_kernel {
   DC_KERNEL_AUTO = 0, /* fastest kernel that supports the request            */
   DC_KERNEL_SIMT = 1, /* general CUDA-core kernel: every term, any window    */
-  DC_KERNEL_TC = 2    /* tcgen05/TMEM/TMA kernel (windowed layers)           */
+  DC_KERNEL_TC = 2,   /* tcgen05/TMEM/TMA kernel, single pass (windows up to
+                         three key tiles, heads per group <= 8)              */
+  DC_KERNEL_TCS = 3   /* tcgen05 two-pass streaming kernel (any window incl.
+                         full causal, heads per group <= 16)                 */
 };
 
 /* One composition term set (pre: on logits, post: on probabilities).

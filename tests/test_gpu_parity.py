@@ -221,9 +221,12 @@ def test_stream_semantics():
 
 
 @pytest.mark.parametrize("G,window,expect", [(8, 128, "tc"), (4, 256, "tc"), (32, 128, "tc"), (16, 200, "tc"),
-                                              (1, 128, "simt"), (8, None, "simt")])
+                                              (1, 128, "simt"), (8, None, "tcs"), (2, 128, "tcs"),
+                                              (8, 1024, "tcs")])
 def test_auto_dispatch(G, window, expect):
-    """AUTO runs the tensor-core kernel for windowed layers with <= 8 heads per group."""
+    """AUTO picks the single-pass tensor-core kernel for windows within three key
+    tiles and <= 8 heads per group, the two-pass streaming kernel for full-causal
+    layers, long windows and 16 heads per group, and the SIMT kernel otherwise."""
     q = torch.empty(1, 64, 32, 128, dtype=torch.bfloat16, device=DEV)
     pre = dc.DCTerms(qw1=torch.empty(1, 64, 32, 1, dtype=torch.bfloat16, device=DEV),
                      qw2=torch.empty(1, 64, 1, 32, dtype=torch.bfloat16, device=DEV))
@@ -241,3 +244,34 @@ def test_tc_kernel_vs_oracle(G, R, window, T):
     ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, window, G, None)
     got = run_general(q, k, v, pre, post, 128 ** -0.5, window, G, None, "bf16", "tc")
     assert_close(got, ref, f"tc G{G} R{R} W{window} T{T}")
+
+
+@pytest.mark.parametrize("G,R,window,T,B,seq_lens", [
+    (8, 1, None, 300, 1, None),      # full causal, HPG 4, ragged T, 3 key tiles at the end
+    (4, 2, None, 260, 2, [260, 131]),  # full causal, HPG 8, seq_lens
+    (2, 1, 128, 200, 1, None),       # HPG 16 windowed
+    (2, 2, None, 150, 1, None),      # HPG 16 full causal
+    (32, 1, 500, 700, 1, None),      # HPG 1, window longer than three key tiles
+    (16, 2, 64, 96, 1, None),        # HPG 2, one key tile
+    (8, 1, 1, 64, 1, None),          # window 1
+])
+def test_tcs_kernel_vs_oracle(G, R, window, T, B, seq_lens):
+    """Two-pass streaming tensor-core kernel, every term, BASELINE distributions."""
+    dt = torch.bfloat16
+    q, k, v, pre, post = O.make_inputs(B, T, 32, 128, G, R, seed=G * 11 + R + T)
+    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens)
+    got = run_general(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens, "bf16", "tcs")
+    assert_close(got, ref, f"tcs G{G} R{R} W{window} T{T}")
+
+
+def test_tcs_matches_tc_on_windowed_layer():
+    """Both tensor-core kernels on the same windowed layer agree closely."""
+    dt = torch.bfloat16
+    q, k, v, pre, post = O.make_inputs(1, 384, 32, 128, 8, 1, seed=99)
+    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    a = run_general(q, k, v, pre, post, 128 ** -0.5, 128, 8, None, "bf16", "tc")
+    b = run_general(q, k, v, pre, post, 128 ** -0.5, 128, 8, None, "bf16", "tcs")
+    assert_close(a, b, "tc vs tcs", max_abs=2e-2)
