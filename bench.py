@@ -345,7 +345,7 @@ def main():
     ap.add_argument("--window", type=int, default=None)
     ap.add_argument("--B", type=int, default=None)
     ap.add_argument("--T", type=int, default=None)
-    ap.add_argument("--kernel", default="auto", choices=["auto", "simt", "tc", "tcs"])
+    ap.add_argument("--kernel", default="auto", choices=["auto", "simt", "tc", "tcs", "tcm"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     cfg = dict(WORKLOADS[args.workload])

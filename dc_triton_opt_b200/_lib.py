@@ -15,8 +15,8 @@ LIB_PATH = os.path.join(PKG, "libdcattn.so")
 ABI_VERSION = 1
 
 DC_DTYPE_BF16, DC_DTYPE_FP16 = 0, 1
-DC_KERNEL_AUTO, DC_KERNEL_SIMT, DC_KERNEL_TC, DC_KERNEL_TCS = 0, 1, 2, 3
-KERNELS = {"auto": DC_KERNEL_AUTO, "simt": DC_KERNEL_SIMT, "tc": DC_KERNEL_TC, "tcs": DC_KERNEL_TCS}
+DC_KERNEL_AUTO, DC_KERNEL_SIMT, DC_KERNEL_TC, DC_KERNEL_TCS, DC_KERNEL_TCM = 0, 1, 2, 3, 4
+KERNELS = {"auto": DC_KERNEL_AUTO, "simt": DC_KERNEL_SIMT, "tc": DC_KERNEL_TC, "tcs": DC_KERNEL_TCS, "tcm": DC_KERNEL_TCM}
 STATUS = {0: "DC_OK", -1: "DC_ERR_NULL", -2: "DC_ERR_SHAPE", -3: "DC_ERR_DTYPE",
           -4: "DC_ERR_UNSUPPORTED", -5: "DC_ERR_ALIGN", -6: "DC_ERR_LAUNCH", -7: "DC_ERR_DEVICE"}
 EXPORTS = ("dc_attn_fwd", "dc_attn_fwd_residual", "dc_attn_select_kernel",

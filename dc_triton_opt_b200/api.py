@@ -159,7 +159,7 @@ def dc_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
 
 
 def select_kernel(q, k, v, pre=None, post=None, window=None, G=1) -> str:
-    """Which kernel ``kernel='auto'`` runs for these arguments ('tc' or 'simt')."""
+    """Which kernel ``kernel='auto'`` runs for these arguments ('tc', 'tcm', 'tcs' or 'simt')."""
     B, T, H, D = q.shape
     p = _lib.DcAttnParams()
     p.abi_version = _lib.ABI_VERSION
@@ -178,7 +178,7 @@ def select_kernel(q, k, v, pre=None, post=None, window=None, G=1) -> str:
                     setattr(st, f.name, 16)
     rc = _lib.load().dc_attn_select_kernel(ctypes.byref(p))
     _lib.check(rc if rc < 0 else 0, "dc_attn_select_kernel")
-    return {1: "simt", 2: "tc", 3: "tcs"}[rc]
+    return {1: "simt", 2: "tc", 3: "tcs", 4: "tcm"}[rc]
 
 
 def _residual_call(q, k, v, dc_weights, scaling, window, seq_lens, G, out):

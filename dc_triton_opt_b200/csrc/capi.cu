@@ -22,6 +22,8 @@ bool tcs_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tcs(const dc_attn_params &p, cudaStream_t st);
 bool tcs32_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tcs32(const dc_attn_params &p, cudaStream_t st);
+bool tcm_supports(const dc_attn_params &p, std::string *why);
+cudaError_t launch_tcm(const dc_attn_params &p, cudaStream_t st);
 }  // namespace dcattn
 
 namespace {
@@ -92,8 +94,15 @@ int select_kernel(const dc_attn_params &p) {
       return fail(DC_ERR_UNSUPPORTED, "streaming tensor-core kernel does not support this call: %s", why_s.c_str());
     return DC_KERNEL_TCS;
   }
+  std::string why_m;
+  const bool tcm_ok = dcattn::tcm_supports(p, &why_m);
+  if (p.kernel == DC_KERNEL_TCM) {
+    if (!tcm_ok)
+      return fail(DC_ERR_UNSUPPORTED, "tensor-core-mix kernel does not support this call: %s", why_m.c_str());
+    return DC_KERNEL_TCM;
+  }
   if (p.kernel != DC_KERNEL_AUTO) return fail(DC_ERR_SHAPE, "unknown kernel selector %d", p.kernel);
-  return tc_ok ? DC_KERNEL_TC : tcs_ok ? DC_KERNEL_TCS : DC_KERNEL_SIMT;
+  return tc_ok ? DC_KERNEL_TC : tcm_ok ? DC_KERNEL_TCM : tcs_ok ? DC_KERNEL_TCS : DC_KERNEL_SIMT;
 }
 
 int check_device() {
@@ -133,6 +142,8 @@ int dc_attn_fwd(const dc_attn_params *pp, void *stream) {
   cudaError_t e;
   if (which == DC_KERNEL_TC) {
     e = dcattn::launch_tc(p, st);
+  } else if (which == DC_KERNEL_TCM) {
+    e = dcattn::launch_tcm(p, st);
   } else if (which == DC_KERNEL_TCS) {
     e = (p.H / p.G == 32) ? dcattn::launch_tcs32(p, st) : dcattn::launch_tcs(p, st);
   } else {

@@ -1,0 +1,726 @@
+// Two-pass streaming DC-attention forward with the static head mix on the
+// tensor cores, for 16 or 32 heads per group (sm_100a).
+//
+// At 16-32 heads per group the static HPG x HPG mix costs HPG^2 MACs per
+// (query, key) pair, as much as QK^T itself; on CUDA cores it dominates the
+// kernel.  Here it is a tcgen05 MMA per query:
+//     D_i[key, h] = sum_h' A_i[key, h'] W[h', h]     (M = 64 keys, K = HPG)
+// where A_i is the (pre-composition logits | probabilities) tile of query i,
+// written by the compose threads to shared memory as fp16.  The diagonal of W,
+// the query- and key-wise rank-R terms and the qdd/kdd gates stay on the CUDA
+// cores in fp32; only the off-diagonal mix (|W| ~ 0.02) is rounded to fp16.
+//
+// Tiles and TMEM (512 columns x 128 lanes), BM = 256 / HPG queries per CTA:
+//   S  [0,128)    QK^T of a 64-key tile: head h is an M = 64 MMA whose rows
+//                 land in lane half h / (HPG/2) of every lane quarter, column
+//                 (h % (HPG/2)) * BM + query.  Thread (quarter q, lane l) thus
+//                 holds key 16 q + l % 16 for the heads of half l / 16.
+//   D  [128,256)  mix output: query i, output half v at lane half v, columns
+//                 128 + i * HPG/2 + (h % (HPG/2)); same thread <-> key mapping.
+//   O  [256,512)  O^T: head h, d half c (lane half c), column 256 + h*BM + i.
+// Pass A: QK, pre mix, running softmax statistics per (head, query).
+// Pass B: QK, pre mix, normalise, post mix, P' -> PV.
+// Math follows dc_attention_torch.py:159-258 (grouped residual form) extended
+// to the static-W / rank-R / gate terms of the general DC formulation.
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include <string>
+#include <type_traits>
+
+#include "tc_common.cuh"
+
+namespace dcattn {
+namespace tcm {
+
+using namespace tc;
+
+constexpr int KT = 64;             // keys per tile
+constexpr int KJOB = KT * 256;     // one ring job: one head, 64 keys x 128 d
+constexpr int NCW = 8;             // compose warps (2 per lane quarter)
+constexpr int NSLOT = 3;
+constexpr uint32_t S_COL = 0, D_COL = 128, O_COL = 256;
+
+template <int HPG>
+struct Shape {
+  static constexpr int BM = 256 / HPG;        // queries per CTA
+  static constexpr int HH = HPG / 2;          // heads per lane half
+  static constexpr int NQG = 64 / HPG;        // queries per compose sub-group (32 values per thread)
+  static constexpr int NSG = (BM / 2) / NQG;  // sub-groups per compose warp
+  static constexpr int KB = HPG / 8;          // 16-byte k-blocks per mix-operand row
+  static constexpr int ATILE = KT * HPG * 2;  // bytes of one query's mix operand
+  static constexpr int PHEAD = KT * BM * 2;   // bytes of one head's P' tile
+  static constexpr int NCOL = HPG * BM;       // (head, query) columns
+};
+
+struct GeoM {
+  int q_off, ring_off, a_off, p_off, bm_off, rec_off, stat_off, bar_off, tmem_off, total, recf;
+};
+
+template <int HPG, int R>
+__host__ __device__ inline GeoM make_geo_m() {
+  using SH = Shape<HPG>;
+  GeoM g{};
+  g.q_off = 0;                                  // Q: HPG x BM x 256 B (64 KB); output staging at the end
+  g.ring_off = HPG * SH::BM * 256;
+  g.a_off = g.ring_off + NSLOT * KJOB;          // mix operands, BM x 64 keys x HPG fp16 (32 KB)
+  g.p_off = g.a_off + SH::BM * SH::ATILE;       // P': HPG x 64 keys x BM (32 KB); pass-A stats exchange
+  g.bm_off = g.p_off + HPG * SH::PHEAD;         // mix B operands: 2 sets x HPG x HPG fp16
+  int o = g.bm_off + 2 * HPG * HPG * 2;
+  g.recf = round_up(HPG * (2 * R + 1), 4);
+  g.rec_off = round_up(o, 16); o = g.rec_off + 2 * SH::BM * g.recf * 4;
+  g.stat_off = o; o += 2 * SH::NCOL * 4;
+  g.bar_off = round_up(o, 8); o = g.bar_off + 24 * 8;
+  g.tmem_off = o; o += 16;
+  g.total = o;
+  return g;
+}
+
+// N consecutive per-token weights (bf16/fp16, 16-byte aligned) as floats.
+template <typename E, int N>
+__device__ __forceinline__ void ld_row(const void *base, int64_t idx, float (&w)[N]) {
+  static_assert(N % 8 == 0, "rows are read 8 elements at a time");
+  const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const E *>(base) + idx);
+#pragma unroll
+  for (int c = 0; c < N / 8; ++c) {
+    const uint4 raw = __ldg(src + c);
+    const E *e = reinterpret_cast<const E *>(&raw);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) w[c * 8 + j] = to_f<E>(e[j]);
+  }
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
+  const __half2 h = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<const uint32_t *>(&h);
+}
+
+template <typename E>
+__device__ __forceinline__ uint32_t pack_e2(float lo, float hi) {
+  const E a = from_f<E>(lo), b = from_f<E>(hi);
+  return static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&a)) |
+         (static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&b)) << 16);
+}
+
+template <typename E, int HPG, int R>
+__global__ void __launch_bounds__(32 * (NCW + 2), 1)
+    dc_tcm_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                  const TcParams p) {
+  using SH = Shape<HPG>;
+  constexpr int BM = SH::BM, HH = SH::HH, NQG = SH::NQG, NSG = SH::NSG, KB = SH::KB;
+  constexpr int ATILE = SH::ATILE, PHEAD = SH::PHEAD, NCOL = SH::NCOL;
+  static_assert(HH * NQG == 32, "a compose sub-group is 32 values per thread");
+
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                          ~static_cast<uintptr_t>(1023));
+  const GeoM geo = make_geo_m<HPG, R>();
+  const int recf = geo.recf;
+  float *rec = reinterpret_cast<float *>(smem + geo.rec_off);
+  float *redm = reinterpret_cast<float *>(smem + geo.p_off), *reds = redm + 4 * NCOL;
+  float *mval = reinterpret_cast<float *>(smem + geo.stat_off), *linv = mval + NCOL;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + geo.bar_off);
+  uint64_t *bar_full = bars + 0, *bar_free = bars + 3, *bar_q = bars + 6, *bar_S = bars + 7;
+  uint64_t *bar_Sfree = bars + 8, *bar_P = bars + 9, *bar_Pfree = bars + 10, *bar_O = bars + 11;
+  uint64_t *bar_A = bars + 12, *bar_D = bars + 16;  // per compose sub-group (4 each)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + geo.tmem_off);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tma_warp = NCW, mma_warp = NCW + 1;
+  const int nqb = (p.T + BM - 1) / BM;
+  const int qb = nqb - 1 - static_cast<int>(blockIdx.x);  // longest spans first
+  const int b = blockIdx.y / p.G, g = blockIdx.y % p.G;
+  const int q0 = qb * BM, H = p.H, T = p.T, hbase = g * HPG;
+  const int k_lo = p.window > 0 ? max(0, q0 - p.window + 1) : 0;
+  const int span = min(q0 + BM, T) - k_lo;
+  const int nkt = (span + KT - 1) / KT;
+  const int rlast = ((span - KT * (nkt - 1)) + 15) / 16 * 16;
+  const int slen = p.seq_lens ? min(max(p.seq_lens[b], 0), T) : T;
+  const uint32_t WAIT = 1u << 24;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < NSLOT; ++i) {
+      ptx::mbar_init(bar_full + i, 1);
+      ptx::mbar_init(bar_free + i, 1);
+    }
+    ptx::mbar_init(bar_q, 1);
+    ptx::mbar_init(bar_S, 1);
+    ptx::mbar_init(bar_Sfree, NCW);
+    ptx::mbar_init(bar_P, NCW);
+    ptx::mbar_init(bar_Pfree, 1);
+    ptx::mbar_init(bar_O, 1);
+    for (int i = 0; i < 4; ++i) {
+      ptx::mbar_init(bar_A + i, 4);
+      ptx::mbar_init(bar_D + i, 1);
+    }
+    ptx::fence_mbar_init();
+  }
+  if (warp == tma_warp) ptx::tmem_alloc(tmem_slot, 512);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tbase = *tmem_slot;
+
+  if (warp == tma_warp) {
+    // ============================================================ TMA producer
+    // job order: pass A K(0..nkt-1); pass B K(0), then per tile K(kt+1), V(kt)
+    if (lane == 0) {
+      ptx::tma_prefetch_desc(&tm_q);
+      ptx::tma_prefetch_desc(&tm_k);
+      ptx::tma_prefetch_desc(&tm_v);
+      ptx::mbar_expect_tx(bar_q, HPG * BM * 256);
+      for (int h = 0; h < HPG; ++h)
+        for (int c = 0; c < 2; ++c)
+          ptx::tma_load_4d(smem + geo.q_off + h * BM * 256 + c * BM * 128, &tm_q, bar_q, c * 64, hbase + h, q0, b);
+      int job = 0;
+      bool ok = true;
+      auto load_tile = [&](const CUtensorMap *m, int kt) {
+        for (int h = 0; h < HPG && ok; ++h, ++job) {
+          const int slot = job % NSLOT, use = job / NSLOT;
+          if (use > 0 && !ptx::mbar_wait(bar_free + slot, (use - 1) & 1, WAIT)) {
+            ok = false;
+            record_err(p, ERR_TIMEOUT_FREE);
+            return;
+          }
+          ptx::mbar_expect_tx(bar_full + slot, KJOB);
+          unsigned char *dst = smem + geo.ring_off + slot * KJOB;
+          ptx::tma_load_4d(dst, m, bar_full + slot, 0, hbase + h, k_lo + kt * KT, b);
+          ptx::tma_load_4d(dst + KJOB / 2, m, bar_full + slot, 64, hbase + h, k_lo + kt * KT, b);
+        }
+      };
+      for (int kt = 0; kt < nkt; ++kt) load_tile(&tm_k, kt);
+      load_tile(&tm_k, 0);
+      for (int kt = 0; kt < nkt; ++kt) {
+        if (kt + 1 < nkt) load_tile(&tm_k, kt + 1);
+        load_tile(&tm_v, kt);
+      }
+    }
+    __syncwarp();
+  } else if (warp == mma_warp) {
+    // ============================================================ MMA issuer
+    if (lane == 0) {
+      const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
+      const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 64, BM);
+      const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 64, BM);
+      const uint32_t idesc_mix = ptx::idesc_f16(0, 0, 0, 64, HH);  // fp16 x fp16
+      const uint32_t q_addr = ptx::smem_u32(smem + geo.q_off);
+      const uint32_t ring_addr = ptx::smem_u32(smem + geo.ring_off);
+      const uint32_t a_addr = ptx::smem_u32(smem + geo.a_off);
+      const uint32_t p_addr = ptx::smem_u32(smem + geo.p_off);
+      const uint32_t bm_addr = ptx::smem_u32(smem + geo.bm_off);
+      int job = 0, sidx = 0;
+      bool ok = ptx::mbar_wait(bar_q, 0, WAIT);
+      if (!ok) record_err(p, ERR_TIMEOUT_Q);
+      ptx::tc_fence_after();
+      auto ring_wait = [&]() -> uint32_t {
+        const int slot = job % NSLOT;
+        if (!ptx::mbar_wait(bar_full + slot, (job / NSLOT) & 1, WAIT)) {
+          ok = false;
+          record_err(p, ERR_TIMEOUT_FULL);
+        }
+        ptx::tc_fence_after();
+        return ring_addr + slot * KJOB;
+      };
+      auto qk = [&]() {
+        if (sidx >= 1 && !ptx::mbar_wait(bar_Sfree, (sidx - 1) & 1, WAIT)) {
+          ok = false;
+          record_err(p, ERR_TIMEOUT_S);
+        }
+        ++sidx;
+        if (!ok) return;
+        ptx::tc_fence_after();
+        for (int h = 0; h < HPG && ok; ++h, ++job) {
+          const uint32_t a0 = ring_wait();
+          if (!ok) return;
+          const uint32_t b0 = q_addr + h * BM * 256;
+          const uint32_t d = tbase + (static_cast<uint32_t>(16 * (h / HH)) << 16) + S_COL + (h % HH) * BM;
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks) {
+            const uint64_t ad = ptx::smem_desc(a0 + (ks >> 2) * (KJOB / 2) + (ks & 3) * 32, 16, 1024, 2);
+            const uint64_t bd = ptx::smem_desc(b0 + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 16, 1024, 2);
+            ptx::mma_f16_ss(d, ad, bd, idesc_qk, ks > 0);
+          }
+          ptx::mma_commit(bar_free + (job % NSLOT));
+        }
+        ptx::mma_commit(bar_S);
+      };
+      // one round of head mixes (set 0 = pre, 1 = post) for the four sub-groups
+      auto mixes = [&](int set, int round) {
+        for (int sgl = 0; sgl < NSG; ++sgl)
+          for (int cs = 0; cs < 2; ++cs) {
+            const int sg = cs * NSG + sgl;
+            if (!ok) return;
+            if (!ptx::mbar_wait(bar_A + sg, round & 1, WAIT)) {
+              ok = false;
+              record_err(p, ERR_TIMEOUT_P);
+              return;
+            }
+            ptx::tc_fence_after();
+            for (int ii = 0; ii < NQG; ++ii) {
+              const int i = sg * NQG + ii;
+#pragma unroll
+              for (int v = 0; v < 2; ++v)
+#pragma unroll
+                for (int ks = 0; ks < HPG / 16; ++ks) {
+                  const uint64_t ad = ptx::smem_desc(a_addr + i * ATILE + ks * 256, 128, KB * 128, 0);
+                  const uint64_t bd =
+                      ptx::smem_desc(bm_addr + set * (HPG * HPG * 2) + v * (HH * HPG * 2) + ks * 256, 128, KB * 128, 0);
+                  ptx::mma_f16_ss(tbase + (static_cast<uint32_t>(16 * v) << 16) + D_COL + i * HH, ad, bd, idesc_mix,
+                                  ks > 0);
+                }
+            }
+            ptx::mma_commit(bar_D + sg);
+          }
+      };
+      auto pv = [&](int kt) {
+        if (!ok) return;
+        if (!ptx::mbar_wait(bar_P, kt & 1, WAIT)) {
+          ok = false;
+          record_err(p, ERR_TIMEOUT_P);
+          return;
+        }
+        ptx::tc_fence_after();
+        const int rows = kt == nkt - 1 ? rlast : KT;
+        for (int h = 0; h < HPG && ok; ++h, ++job) {
+          const uint32_t a0 = ring_wait();
+          if (!ok) return;
+          const uint32_t b0 = p_addr + h * PHEAD;
+#pragma unroll
+          for (int c = 0; c < 2; ++c)
+            for (int ks = 0; ks < rows / 16; ++ks) {
+              const uint64_t ad = ptx::smem_desc(a0 + c * (KJOB / 2) + ks * 2048, KJOB / 2, 1024, 2);
+              const uint64_t bd = ptx::smem_desc(b0 + ks * (2 * BM * 16), BM * 16, 128, 0);
+              ptx::mma_f16_ss(tbase + (static_cast<uint32_t>(16 * c) << 16) + O_COL + h * BM, ad, bd, idesc_pv,
+                              (kt > 0 || ks > 0));
+            }
+          ptx::mma_commit(bar_free + (job % NSLOT));
+        }
+        ptx::mma_commit(bar_Pfree);
+      };
+      for (int kt = 0; kt < nkt && ok; ++kt) {
+        qk();
+        mixes(0, kt);
+      }
+      if (ok) qk();
+      for (int kt = 0; kt < nkt && ok; ++kt) {
+        mixes(0, nkt + 2 * kt);
+        mixes(1, nkt + 2 * kt + 1);
+        if (kt + 1 < nkt) qk();
+        pv(kt);
+      }
+      ptx::mma_commit(bar_O);
+    }
+    __syncwarp();
+  } else {
+    // ============================================================ compose warps
+    const int qtr = warp & 3, cs = warp >> 2;
+    const int u = lane >> 4, r16 = lane & 15;
+    const int key_local = 16 * qtr + r16;
+    const int ctid = threadIdx.x;
+    const float sl2e = p.scale * kLog2e;
+    const uint32_t tl = tbase + (static_cast<uint32_t>(32 * qtr) << 16);
+    unsigned char *atile = smem + geo.a_off;
+    unsigned char *ptile = smem + geo.p_off;
+
+    // ---- static mix operands (fp16, K-major, no swizzle) and per-query records
+    for (int idx = ctid; idx < 2 * HPG * HPG; idx += 32 * NCW) {
+      const int set = idx / (HPG * HPG), rem = idx % (HPG * HPG);
+      const int hout = rem / HPG, kin = rem % HPG;  // B[n][k] of output half hout / HH
+      const TermPtrs &tm = set ? p.post : p.pre;
+      const float wv = (kin == hout || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + kin) * HPG + hout];
+      const int v = hout / HH, n = hout % HH;
+      __half *dst = reinterpret_cast<__half *>(smem + geo.bm_off + set * (HPG * HPG * 2) + v * (HH * HPG * 2) +
+                                               ((n / 8) * KB + kin / 8) * 128 + (n % 8) * 16 + (kin % 8) * 2);
+      *dst = __float2half_rn(wv);
+    }
+    for (int idx = ctid; idx < 2 * BM * recf; idx += 32 * NCW) {
+      const int set = idx / (BM * recf), rem = idx % (BM * recf);
+      const int i = rem / recf, j = rem % recf;
+      const TermPtrs &tm = set ? p.post : p.pre;
+      const int t = q0 + i;
+      float val = 0.f;
+      if (t < T) {
+        const int64_t tok = (int64_t)b * T + t;
+        if (j < HPG) {
+          val = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)g * HPG + j) * HPG + j] : 0.f) +
+                (tm.qdd ? ld_w<E>(tm.qdd, tok * H + hbase + j) : 0.f);
+        } else if (j < HPG + HPG * R) {
+          const int h = (j - HPG) / R, r = (j - HPG) % R;
+          val = tm.qw1 ? ld_w<E>(tm.qw1, (tok * H + hbase + h) * R + r) : 0.f;
+        } else if (j < HPG + 2 * HPG * R) {
+          const int r = (j - HPG - HPG * R) / HPG, h = (j - HPG - HPG * R) % HPG;
+          val = tm.qw2 ? ld_w<E>(tm.qw2, (tok * R + r) * H + hbase + h) : 0.f;
+        }
+      }
+      rec[idx] = val;
+    }
+    ptx::fence_proxy_async_smem();
+    ptx::named_bar_sync(1, 32 * NCW);
+
+    bool ok = true;
+    auto wait_or_fail = [&](uint64_t *bar, int parity, int code) {
+      if (ok && !ptx::mbar_wait(bar, parity, WAIT)) {
+        ok = false;
+        record_err(p, code);
+      }
+    };
+    auto arrive = [&](uint64_t *bar) {
+      ptx::fence_proxy_async_smem();
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar);
+    };
+    auto valid = [&](int s, int t) {
+      return s <= t && (p.window <= 0 || t - s < p.window) && t < T;
+    };
+
+    // load S (this thread's key, its lane half's heads) for NQG queries
+    auto load_s = [&](int i0, float (&a)[HH][NQG]) {
+#pragma unroll
+      for (int j = 0; j < HH; ++j) ptx::tmem_ld<NQG>(tl + S_COL + j * BM + i0, a[j]);
+    };
+    // rank-R reductions over all HPG heads (two lane halves) and the mix operand rows
+    auto reduce_and_stage = [&](const TermPtrs &tm, int set, int i0, int64_t tok, bool key_ok,
+                                const float (&a)[HH][NQG], float (&aq)[NQG][R], float (&ak)[NQG][R]) {
+      const float *rb = rec + (set * BM + i0) * recf;
+#pragma unroll
+      for (int i = 0; i < NQG; ++i)
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float sq = 0.f;
+#pragma unroll
+          for (int j = 0; j < HH; ++j) sq = fmaf(rb[i * recf + HPG + (HH * u + j) * R + r], a[j][i], sq);
+          aq[i][r] = sq;
+          ak[i][r] = 0.f;
+        }
+      if (key_ok && tm.kw1) {
+        float w[HH * R];
+        ld_row<E, HH * R>(tm.kw1, (tok * H + hbase + HH * u) * R, w);
+#pragma unroll
+        for (int i = 0; i < NQG; ++i)
+#pragma unroll
+          for (int r = 0; r < R; ++r) {
+            float sk = 0.f;
+#pragma unroll
+            for (int j = 0; j < HH; ++j) sk = fmaf(w[j * R + r], a[j][i], sk);
+            ak[i][r] = sk;
+          }
+      }
+#pragma unroll
+      for (int i = 0; i < NQG; ++i)
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          aq[i][r] += __shfl_xor_sync(0xffffffffu, aq[i][r], 16);
+          ak[i][r] += __shfl_xor_sync(0xffffffffu, ak[i][r], 16);
+        }
+#pragma unroll
+      for (int i = 0; i < NQG; ++i) {
+        unsigned char *row = atile + (i0 + i) * ATILE + (key_local >> 3) * (KB * 128) + (key_local & 7) * 16;
+#pragma unroll
+        for (int kb = 0; kb < HH / 8; ++kb) {
+          uint4 v;
+          v.x = pack_h2(a[kb * 8 + 0][i], a[kb * 8 + 1][i]);
+          v.y = pack_h2(a[kb * 8 + 2][i], a[kb * 8 + 3][i]);
+          v.z = pack_h2(a[kb * 8 + 4][i], a[kb * 8 + 5][i]);
+          v.w = pack_h2(a[kb * 8 + 6][i], a[kb * 8 + 7][i]);
+          *reinterpret_cast<uint4 *>(row + (u * (HH / 8) + kb) * 128) = v;
+        }
+      }
+    };
+    // composed values x = mix (TMEM D) + diagonal gates * a + rank-R expansions
+    auto finish = [&](const TermPtrs &tm, int set, int i0, int64_t tok, bool key_ok, const float (&dm)[NQG][HH],
+                      const float (&a)[HH][NQG], const float (&aq)[NQG][R], const float (&ak)[NQG][R],
+                      float (&x)[HH][NQG]) {
+      const float *rb = rec + (set * BM + i0) * recf;
+      float kd[HH];
+      if (key_ok && tm.kdd) {
+        ld_row<E, HH>(tm.kdd, tok * H + hbase + HH * u, kd);
+      } else {
+#pragma unroll
+        for (int j = 0; j < HH; ++j) kd[j] = 0.f;
+      }
+#pragma unroll
+      for (int i = 0; i < NQG; ++i)
+#pragma unroll
+        for (int j = 0; j < HH; ++j) {
+          float xv = fmaf(rb[i * recf + HH * u + j] + kd[j], a[j][i], dm[i][j]);
+#pragma unroll
+          for (int r = 0; r < R; ++r) xv = fmaf(rb[i * recf + HPG + HPG * R + r * HPG + HH * u + j], aq[i][r], xv);
+          x[j][i] = xv;
+        }
+      if (key_ok && tm.kw1) {
+#pragma unroll
+        for (int r = 0; r < R; ++r) {
+          float k2[HH];
+          ld_row<E, HH>(tm.kw2, (tok * R + r) * H + hbase + HH * u, k2);
+#pragma unroll
+          for (int i = 0; i < NQG; ++i)
+#pragma unroll
+            for (int j = 0; j < HH; ++j) x[j][i] = fmaf(k2[j], ak[i][r], x[j][i]);
+        }
+      }
+    };
+    auto load_d = [&](int i0, float (&dm)[NQG][HH]) {
+#pragma unroll
+      for (int i = 0; i < NQG; ++i) ptx::tmem_ld<HH>(tl + D_COL + (i0 + i) * HH, dm[i]);
+    };
+
+    float m_run[NSG][2], l_run[NSG][2];
+#pragma unroll
+    for (int k = 0; k < NSG; ++k) { m_run[k][0] = m_run[k][1] = -INFINITY; l_run[k][0] = l_run[k][1] = 0.f; }
+
+    // ============================== pass A: statistics of the composed logits
+    for (int kt = 0; kt < nkt; ++kt) {
+      const int s = k_lo + kt * KT + key_local;
+      const bool key_ok = s < slen;
+      const int64_t tok = (int64_t)b * T + s;
+      wait_or_fail(bar_S, kt & 1, ERR_TIMEOUT_S);
+      ptx::tc_fence_after();
+      float aq[NSG][NQG][R], ak[NSG][NQG][R];
+#pragma unroll
+      for (int sgl = 0; sgl < NSG; ++sgl) {
+        const int i0 = (cs * NSG + sgl) * NQG;
+        float a[HH][NQG];
+        load_s(i0, a);
+        ptx::tmem_wait_ld();
+        reduce_and_stage(p.pre, 0, i0, tok, key_ok, a, aq[sgl], ak[sgl]);
+        arrive(bar_A + cs * NSG + sgl);
+      }
+#pragma unroll
+      for (int sgl = 0; sgl < NSG; ++sgl) {
+        const int sg = cs * NSG + sgl, i0 = sg * NQG;
+        wait_or_fail(bar_D + sg, kt & 1, ERR_TIMEOUT_P);
+        ptx::tc_fence_after();
+        float dm[NQG][HH], a[HH][NQG], x[HH][NQG];
+        load_d(i0, dm);
+        load_s(i0, a);
+        ptx::tmem_wait_ld();
+        finish(p.pre, 0, i0, tok, key_ok, dm, a, aq[sgl], ak[sgl], x);
+        // masked max / exp / transposed sum over the 16 keys of this lane half
+        float e[32], mt[2] = {-INFINITY, -INFINITY};
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const int j = c / NQG, i = c % NQG;
+          const float v = (key_ok && valid(s, q0 + i0 + i)) ? x[j][i] : -INFINITY;
+          const float m0 = ptx::warp_max(u == 0 ? v : -INFINITY);
+          const float m1 = ptx::warp_max(u == 1 ? v : -INFINITY);
+          const float mw = u ? m1 : m0;
+          if (r16 == (c >> 1)) mt[c & 1] = mw;
+          e[c] = exp2f((v - (mw == -INFINITY ? 0.f : mw)) * sl2e);
+        }
+#pragma unroll
+        for (int off = 8, cnt = 32; off >= 1; off >>= 1, cnt >>= 1) {
+          const bool upper = (lane & off) != 0;
+#pragma unroll
+          for (int jj = 0; jj < cnt / 2; ++jj) {
+            const float send = upper ? e[jj] : e[jj + cnt / 2];
+            const float keep = upper ? e[jj + cnt / 2] : e[jj];
+            e[jj] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < 2; ++k)
+          if (mt[k] != -INFINITY) {
+            const float mn = fmaxf(m_run[sgl][k], mt[k]);
+            l_run[sgl][k] = (m_run[sgl][k] == -INFINITY ? 0.f : l_run[sgl][k] * exp2f((m_run[sgl][k] - mn) * sl2e)) +
+                            e[k] * exp2f((mt[k] - mn) * sl2e);
+            m_run[sgl][k] = mn;
+          }
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_Sfree);
+    }
+    // ---- combine the lane quarters
+#pragma unroll
+    for (int sgl = 0; sgl < NSG; ++sgl)
+#pragma unroll
+      for (int k = 0; k < 2; ++k) {
+        const int c = 2 * r16 + k, j = c / NQG, i = c % NQG;
+        const int col = (HH * u + j) * BM + (cs * NSG + sgl) * NQG + i;
+        redm[qtr * NCOL + col] = m_run[sgl][k];
+        reds[qtr * NCOL + col] = l_run[sgl][k];
+      }
+    ptx::named_bar_sync(1, 32 * NCW);
+    for (int jc = ctid; jc < NCOL; jc += 32 * NCW) {
+      float m = -INFINITY;
+      for (int q = 0; q < 4; ++q) m = fmaxf(m, redm[q * NCOL + jc]);
+      float l = 0.f;
+      for (int q = 0; q < 4; ++q) {
+        const float mq = redm[q * NCOL + jc];
+        if (mq != -INFINITY) l += reds[q * NCOL + jc] * exp2f((mq - m) * sl2e);
+      }
+      mval[jc] = m == -INFINITY ? 0.f : m * sl2e;
+      linv[jc] = l > 0.f ? 1.f / l : 0.f;
+    }
+    ptx::named_bar_sync(1, 32 * NCW);
+
+    // ============================== pass B: probabilities, post mix, P'V
+    for (int kt = 0; kt < nkt; ++kt) {
+      const int s = k_lo + kt * KT + key_local;
+      const bool key_ok = s < slen;
+      const int64_t tok = (int64_t)b * T + s;
+      const int rpre = nkt + 2 * kt, rpost = rpre + 1;
+      wait_or_fail(bar_S, (nkt + kt) & 1, ERR_TIMEOUT_S);
+      ptx::tc_fence_after();
+      float aq[NSG][NQG][R], ak[NSG][NQG][R];
+#pragma unroll
+      for (int sgl = 0; sgl < NSG; ++sgl) {
+        const int i0 = (cs * NSG + sgl) * NQG;
+        float a[HH][NQG];
+        load_s(i0, a);
+        ptx::tmem_wait_ld();
+        reduce_and_stage(p.pre, 0, i0, tok, key_ok, a, aq[sgl], ak[sgl]);
+        arrive(bar_A + cs * NSG + sgl);
+      }
+      float pr[NSG][HH][NQG], pq[NSG][NQG][R], pk[NSG][NQG][R];
+#pragma unroll
+      for (int sgl = 0; sgl < NSG; ++sgl) {
+        const int sg = cs * NSG + sgl, i0 = sg * NQG;
+        wait_or_fail(bar_D + sg, rpre & 1, ERR_TIMEOUT_P);
+        ptx::tc_fence_after();
+        float dm[NQG][HH], a[HH][NQG], x[HH][NQG];
+        load_d(i0, dm);
+        load_s(i0, a);
+        ptx::tmem_wait_ld();
+        finish(p.pre, 0, i0, tok, key_ok, dm, a, aq[sgl], ak[sgl], x);
+#pragma unroll
+        for (int j = 0; j < HH; ++j)
+#pragma unroll
+          for (int i = 0; i < NQG; ++i) {
+            const int col = (HH * u + j) * BM + i0 + i;
+            pr[sgl][j][i] = (key_ok && valid(s, q0 + i0 + i)) ? exp2f(fmaf(x[j][i], sl2e, -mval[col])) * linv[col]
+                                                             : 0.f;
+          }
+        reduce_and_stage(p.post, 1, i0, tok, key_ok, pr[sgl], pq[sgl], pk[sgl]);
+        arrive(bar_A + sg);
+      }
+      ptx::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) ptx::mbar_arrive(bar_Sfree);
+      if (kt >= 1) wait_or_fail(bar_Pfree, (kt - 1) & 1, ERR_TIMEOUT_P);
+#pragma unroll
+      for (int sgl = 0; sgl < NSG; ++sgl) {
+        const int sg = cs * NSG + sgl, i0 = sg * NQG;
+        wait_or_fail(bar_D + sg, rpost & 1, ERR_TIMEOUT_P);
+        ptx::tc_fence_after();
+        float dm[NQG][HH], x[HH][NQG];
+        load_d(i0, dm);
+        ptx::tmem_wait_ld();
+        finish(p.post, 1, i0, tok, key_ok, dm, pr[sgl], pq[sgl], pk[sgl], x);
+        unsigned char *prow = ptile + (key_local & 7) * 16 + (key_local >> 3) * (BM * 16);
+#pragma unroll
+        for (int j = 0; j < HH; ++j)
+#pragma unroll
+          for (int i = 0; i < NQG; i += 2) {
+            const int qi = i0 + i;
+            *reinterpret_cast<uint32_t *>(prow + (HH * u + j) * PHEAD + (qi >> 3) * 128 + (qi & 7) * 2) =
+                pack_e2<E>(x[j][i], x[j][i + 1]);
+          }
+      }
+      arrive(bar_P);
+    }
+
+    // ============================== epilogue: O^T -> SMEM [head][d half][query][64 d] -> TMA store
+    wait_or_fail(bar_O, 0, ERR_TIMEOUT_O);
+    ptx::tc_fence_after();
+    unsigned char *stage = smem + geo.q_off;
+    const int d = 64 * u + 16 * qtr + r16;
+    if (ok) {
+#pragma unroll 1
+      for (int h = cs; h < HPG; h += 2) {
+        float v[BM];
+        ptx::tmem_ld<BM>(tl + O_COL + h * BM, v);
+        ptx::tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < BM; ++i)
+          *reinterpret_cast<E *>(stage + (h * 2 + (d >> 6)) * (BM * 128) + i * 128 + (d & 63) * 2) = from_f<E>(v[i]);
+      }
+    }
+    ptx::fence_proxy_async_smem();
+    ptx::named_bar_sync(1, 32 * NCW);
+    if (threadIdx.x == 0 && ok) {
+      for (int h = 0; h < HPG; ++h)
+        for (int c = 0; c < 2; ++c)
+          ptx::tma_store_4d(&tm_o, stage + (h * 2 + c) * (BM * 128), c * 64, hbase + h, q0, b);
+      ptx::bulk_commit();
+      ptx::bulk_wait_read0();
+    }
+  }
+
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == tma_warp) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tbase, 512);
+  }
+}
+
+template <typename E, int HPG, int R>
+static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
+  using SH = Shape<HPG>;
+  const GeoM geo = make_geo_m<HPG, R>();
+  const size_t smem = geo.total + 1024;
+  const int64_t sb = (int64_t)p.T * p.H * D, st_ = (int64_t)p.H * D, sh = D;
+  CUtensorMap mq, mk, mv, mo;
+  if (!make_map(&mq, p.q, p.dtype, p.B, p.T, p.H, SH::BM, sb, st_, sh, true) ||
+      !make_map(&mk, p.k, p.dtype, p.B, p.T, p.H, KT, sb, st_, sh, true) ||
+      !make_map(&mv, p.v, p.dtype, p.B, p.T, p.H, KT, sb, st_, sh, true) ||
+      !make_map(&mo, p.out, p.dtype, p.B, p.T, p.H, SH::BM, p.out_sb, p.out_st, p.out_sh, false))
+    return cudaErrorInvalidValue;
+  TcParams tp;
+  tp.B = p.B; tp.T = p.T; tp.H = p.H; tp.G = p.G; tp.window = p.window; tp.slen_default = p.T;
+  tp.scale = p.scale;
+  tp.seq_lens = p.seq_lens;
+  tp.out = p.out;
+  tp.out_sb = p.out_sb; tp.out_st = p.out_st; tp.out_sh = p.out_sh;
+  tp.err_flag = p.err_flag;
+  tp.pre = to_ptrs(p.pre);
+  tp.post = to_ptrs(p.post);
+  auto kern = dc_tcm_kernel<E, HPG, R>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid((p.T + SH::BM - 1) / SH::BM, p.B * p.G);
+  kern<<<grid, 32 * (NCW + 2), smem, st>>>(mq, mk, mv, mo, tp);
+  return cudaGetLastError();
+}
+
+template <typename E, int HPG>
+static cudaError_t launch_h(const dc_attn_params &p, cudaStream_t st) {
+  return p.R <= 1 ? launch_t<E, HPG, 1>(p, st) : launch_t<E, HPG, 2>(p, st);
+}
+
+template <typename E>
+static cudaError_t launch_e(const dc_attn_params &p, cudaStream_t st) {
+  return p.H / p.G == 32 ? launch_h<E, 32>(p, st) : launch_h<E, 16>(p, st);
+}
+
+}  // namespace tcm
+
+bool tcm_supports(const dc_attn_params &p, std::string *why) {
+  auto no = [&](const char *m) { if (why) *why = m; return false; };
+  if (p.D != 128) return no("D must be 128");
+  if (p.G <= 0 || (p.H / p.G != 16 && p.H / p.G != 32)) return no("heads per group must be 16 or 32");
+  if (p.R > 2) return no("rank R > 2");
+  if (!(p.scale > 0.f)) return no("non-positive softmax scale");
+  if (p.pre.qmat || p.post.qmat) return no("per-query mixing matrices use the SIMT kernel");
+  auto al = [](const void *x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
+  if (!al(p.q) || !al(p.k) || !al(p.v) || !al(p.out)) return no("q, k, v, out must be 16-byte aligned");
+  if (p.out_sb % 8 || p.out_st % 8 || p.out_sh % 8) return no("output strides must be multiples of 8 elements");
+  if (p.H % 8) return no("H must be a multiple of 8");
+  for (const dc_terms *t : {&p.pre, &p.post}) {
+    for (const void *w : {t->kw1, t->kw2, t->kdd})
+      if (w && !al(w)) return no("key-wise weights must be 16-byte aligned");
+    if ((t->kw1 == nullptr) != (t->kw2 == nullptr)) return no("kw1 and kw2 must be given together");
+  }
+  return true;
+}
+
+cudaError_t launch_tcm(const dc_attn_params &p, cudaStream_t st) {
+  if (p.dtype == DC_DTYPE_BF16) return tcm::launch_e<__nv_bfloat16>(p, st);
+  return tcm::launch_e<__half>(p, st);
+}
+
+}  // namespace dcattn

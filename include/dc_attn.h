@@ -71,8 +71,10 @@ enum dc_kernel {
   DC_KERNEL_SIMT = 1, /* general CUDA-core kernel: every term, any window    */
   DC_KERNEL_TC = 2,   /* tcgen05/TMEM/TMA kernel, single pass (windows up to
                          three key tiles, heads per group <= 8)              */
-  DC_KERNEL_TCS = 3   /* tcgen05 two-pass streaming kernel (any window incl.
-                         full causal, heads per group <= 16)                 */
+  DC_KERNEL_TCS = 3,  /* tcgen05 two-pass streaming kernel (any window incl.
+                         full causal, heads per group <= 32)                 */
+  DC_KERNEL_TCM = 4   /* two-pass streaming kernel with the static head mix
+                         on the tensor cores (16 or 32 heads per group)     */
 };
 
 /* One composition term set (pre: on logits, post: on probabilities).

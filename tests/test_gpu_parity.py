@@ -221,12 +221,13 @@ def test_stream_semantics():
 
 
 @pytest.mark.parametrize("G,window,expect", [(8, 128, "tc"), (4, 256, "tc"), (32, 128, "tc"), (16, 200, "tc"),
-                                              (1, 128, "tcs"), (1, None, "tcs"), (8, None, "tcs"), (2, 128, "tcs"),
+                                              (1, 128, "tcm"), (1, None, "tcm"), (8, None, "tcs"), (2, 128, "tcm"),
                                               (8, 1024, "tcs")])
 def test_auto_dispatch(G, window, expect):
     """AUTO picks the single-pass tensor-core kernel for windows within three key
-    tiles and <= 8 heads per group, and the two-pass streaming kernels for
-    full-causal layers, long windows and 16 or 32 heads per group."""
+    tiles and <= 8 heads per group, the tensor-core-mix streaming kernel for 16
+    or 32 heads per group, and the streaming kernel for the other full-causal
+    layers and long windows."""
     q = torch.empty(1, 64, 32, 128, dtype=torch.bfloat16, device=DEV)
     pre = dc.DCTerms(qw1=torch.empty(1, 64, 32, 1, dtype=torch.bfloat16, device=DEV),
                      qw2=torch.empty(1, 64, 1, 32, dtype=torch.bfloat16, device=DEV))
@@ -293,3 +294,24 @@ def test_tcs32_kernel_vs_oracle(H, G, R, window, T, B, seq_lens, dtype):
     ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens)
     got = run_general(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens, dtype, "tcs")
     assert_close(got, ref, f"tcs32 H{H} G{G} R{R} W{window} T{T}")
+
+
+@pytest.mark.parametrize("H,G,R,window,T,B,seq_lens,dtype", [
+    (32, 1, 1, 128, 200, 1, None, "bf16"),          # config-0 layer shape, ragged T
+    (32, 1, 2, None, 300, 1, None, "bf16"),         # full causal, five key tiles at the end
+    (32, 1, 1, 64, 150, 2, [150, 77], "fp16"),      # seq_lens, fp16
+    (64, 2, 1, 100, 130, 1, None, "bf16"),          # two groups of 32 (head offset of the key weights)
+    (32, 1, 2, 1, 40, 1, None, "bf16"),             # window 1
+    (32, 2, 1, 128, 260, 1, None, "bf16"),          # 16 heads per group
+    (32, 2, 2, None, 200, 2, [200, 90], "fp16"),    # 16 heads per group, full causal, seq_lens
+    (32, 2, 2, 256, 300, 1, None, "bf16"),          # 16 heads per group, config-2 window
+])
+def test_tcm_kernel_vs_oracle(H, G, R, window, T, B, seq_lens, dtype):
+    """Streaming kernel with the static head mix as a tcgen05 MMA, every term."""
+    dt = TORCH_DT[dtype]
+    q, k, v, pre, post = O.make_inputs(B, T, H, 128, G, R, seed=H + G * 3 + R + T)
+    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens)
+    got = run_general(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens, dtype, "tcm")
+    assert_close(got, ref, f"tcm H{H} G{G} R{R} W{window} T{T}")
