@@ -248,6 +248,20 @@ __device__ __forceinline__ uint64_t smem_desc(uint32_t saddr, uint32_t lbo, uint
   return d;
 }
 
+// Descriptor of the same matrix moved by `bytes` (a multiple of 16): the start
+// address field holds address >> 4, so offsets add into the low bits.
+__device__ __forceinline__ uint64_t desc_add(uint64_t d, uint32_t bytes) { return d + (bytes >> 4); }
+
+// One lane of a converged warp (elect.sync): the warp runs the issue loop's
+// control flow together and a single lane issues each tcgen05 instruction.
+__device__ __forceinline__ bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .pred P;\n\telect.sync _|P, 0xffffffff;\n\tselp.b32 %0, 1, 0, P;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation.
 // ab_fmt: 0 = f16, 1 = bf16.  major: 0 = K-major, 1 = MN-major.
 __host__ __device__ constexpr uint32_t idesc_f16(uint32_t ab_fmt, uint32_t a_major, uint32_t b_major, uint32_t M,

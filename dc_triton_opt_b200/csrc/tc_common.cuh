@@ -84,7 +84,17 @@ __device__ unsigned long long g_timeline[8192][40];
     const int cta_ = blockIdx.y * gridDim.x + blockIdx.x;                             \
     if (cta_ < 8192) g_timeline[cta_][i] = clock64();                                 \
   } while (0)
+#define TL_VAL(i, v)                                                                  \
+  do {                                                                                \
+    const int cta_ = blockIdx.y * gridDim.x + blockIdx.x;                             \
+    if (cta_ < 8192) g_timeline[cta_][i] = (v);                                       \
+  } while (0)
+#define TL_CLK() clock64()
 #else
+#define TL_VAL(i, v) \
+  do {               \
+  } while (0)
+#define TL_CLK() 0ll
 #define TLP_STAMP(it, i) \
   do {                   \
   } while (0)

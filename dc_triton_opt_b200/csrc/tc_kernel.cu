@@ -121,64 +121,77 @@ __global__ void __launch_bounds__(MAXT, 1)
     }
     __syncwarp();
   } else if (warp == ctrl_warp + 1) {
-    // ================================================= MMA issuer (one thread)
-    if (lane == 0) {
-      const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
-      const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 128, BM);
-      const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 128, BM);
-      const uint32_t q_addr = ptx::smem_u32(smem + geo.q_off);
-      const uint32_t ring_addr = ptx::smem_u32(smem + geo.ring_off);
-      const uint32_t p_addr = ptx::smem_u32(smem + geo.p_off);
-      const int nslot = geo.nslot;
-      const int nK = HPG * nkt, total = 2 * nK;
-      bool ok = true;
-      if (!ptx::mbar_wait(bar_q, 0, 1u << 24)) { ok = false; record_err(p, ERR_TIMEOUT_Q); }
-      TL_STAMP(2);
-      // ---- S^T_h = K_h Q_h^T; key tile kt is signalled as soon as its heads are issued
-      for (int j = 0; j < nK && ok; ++j) {
-        const int slot = j % nslot;
-        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1, 1u << 24)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
-        if (j < 12) TL_STAMP(12 + j);
-        ptx::tc_fence_after();
-        const int kt = j / HPG, h = j % HPG;
-        const uint32_t a0 = ring_addr + slot * TILE_BYTES;
-        const uint32_t b0 = q_addr + h * BM * 256;
+    // ================================================= MMA issuer
+    // Whole warp runs the loops; one elected lane issues each tcgen05 op.
+    const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
+    const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 128, BM);
+    const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 128, BM);
+    const uint64_t qd0 = ptx::smem_desc(ptx::smem_u32(smem + geo.q_off), 16, 1024, 2);
+    const uint64_t kd0 = ptx::smem_desc(ptx::smem_u32(smem + geo.ring_off), 16, 1024, 2);
+    // V tile, MN-major 128B swizzle: 8-key groups 1024 B apart, d halves 16 KB apart
+    const uint64_t vd0 = ptx::smem_desc(ptx::smem_u32(smem + geo.ring_off), TILE_BYTES / 2, 1024, 2);
+    // P' tile, MN-major no swizzle: 8x8 core matrices, query blocks 128 B apart,
+    // 8-key blocks BM*16 B apart
+    const uint64_t pd0 = ptx::smem_desc(ptx::smem_u32(smem + geo.p_off), BM * 16, 128, 0);
+    const int nslot = geo.nslot;
+    const int nK = HPG * nkt, total = 2 * nK;
+    bool ok = true;
+    auto wait_u = [&](uint64_t *bar, int parity, int code) {
+      const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait(bar, parity, 1u << 24));
+      if (ok && !got) {
+        ok = false;
+        if (lane == 0) record_err(p, code);
+      }
+      return ok;
+    };
+    wait_u(bar_q, 0, ERR_TIMEOUT_Q);
+    if (lane == 0) TL_STAMP(2);
+    // ---- S^T_h = K_h Q_h^T; key tile kt is signalled as soon as its heads are issued
+    for (int j = 0; j < nK && ok; ++j) {
+      const int slot = j % nslot;
+      if (!wait_u(bar_full + slot, (j / nslot) & 1, ERR_TIMEOUT_FULL)) break;
+      if (lane == 0 && j < 12) TL_STAMP(12 + j);
+      ptx::tc_fence_after();
+      const int kt = j / HPG, h = j % HPG;
+      const uint64_t ad = ptx::desc_add(kd0, slot * TILE_BYTES);
+      const uint64_t bd = ptx::desc_add(qd0, h * BM * 256);
+      const uint32_t dd = tbase + kt * KT_ROWS + h * BM;
 #pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks) {
-          const uint64_t ad = ptx::smem_desc(a0 + (ks >> 2) * (TILE_BYTES / 2) + (ks & 3) * 32, 16, 1024, 2);
-          const uint64_t bd = ptx::smem_desc(b0 + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 16, 1024, 2);
-          ptx::mma_f16_ss(tbase + kt * KT_ROWS + h * BM, ad, bd, idesc_qk, ks > 0);
-        }
+      for (int ks = 0; ks < D / 16; ++ks)
+        if (ptx::elect_one())
+          ptx::mma_f16_ss(dd, ptx::desc_add(ad, (ks >> 2) * (TILE_BYTES / 2) + (ks & 3) * 32),
+                          ptx::desc_add(bd, (ks >> 2) * (BM * 128) + (ks & 3) * 32), idesc_qk, ks > 0);
+      if (ptx::elect_one()) {
         ptx::mma_commit(bar_free + slot);
         if (h == HPG - 1) ptx::mma_commit(bar_S + kt);
       }
-      TL_STAMP(3);
-      // ---- O^T_h = V_h^T P'^T_h, accumulated over key tiles
-      if (ok && !ptx::mbar_wait(bar_P, 0, 1u << 24)) { ok = false; record_err(p, ERR_TIMEOUT_P); }
-      TL_STAMP(7);
-      ptx::tc_fence_after();
-      for (int j = nK; j < total && ok; ++j) {
-        const int slot = j % nslot;
-        if (!ptx::mbar_wait(bar_full + slot, (j / nslot) & 1, 1u << 24)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
-        ptx::tc_fence_after();
-        const int jj = j - nK, kt = jj / HPG, h = jj % HPG;
-        const int ksteps = (kt == nkt - 1 ? rlast : KT_ROWS) / 16;
-        const uint32_t a0 = ring_addr + slot * TILE_BYTES;
-        const uint32_t b0 = p_addr + (h * nkt + kt) * (KT_ROWS * BM * 2);
-        for (int ks = 0; ks < ksteps; ++ks) {
-          // V tile, MN-major 128B swizzle: 8-key groups 1024 B apart, d halves 16 KB apart
-          const uint64_t ad = ptx::smem_desc(a0 + ks * 2048, TILE_BYTES / 2, 1024, 2);
-          // P' tile, MN-major no swizzle: 8x8 core matrices, query blocks 128 B apart,
-          // 8-key blocks BM*16 B apart
-          const uint64_t bd = ptx::smem_desc(b0 + ks * (2 * BM * 16), BM * 16, 128, 0);
-          ptx::mma_f16_ss(tbase + o_col + h * BM, ad, bd, idesc_pv, (kt > 0 || ks > 0));
-        }
-        ptx::mma_commit(bar_free + slot);
-      }
-      ptx::mma_commit(bar_O);
-      TL_STAMP(10);
+      __syncwarp();
     }
+    if (lane == 0) TL_STAMP(3);
+    // ---- O^T_h = V_h^T P'^T_h, accumulated over key tiles
+    if (ok) wait_u(bar_P, 0, ERR_TIMEOUT_P);
+    if (lane == 0) TL_STAMP(7);
+    ptx::tc_fence_after();
+    for (int j = nK; j < total && ok; ++j) {
+      const int slot = j % nslot;
+      if (!wait_u(bar_full + slot, (j / nslot) & 1, ERR_TIMEOUT_FULL)) break;
+      ptx::tc_fence_after();
+      const int jj = j - nK, kt = jj / HPG, h = jj % HPG;
+      const int ksteps = (kt == nkt - 1 ? rlast : KT_ROWS) / 16;
+      const uint64_t ad = ptx::desc_add(vd0, slot * TILE_BYTES);
+      const uint64_t bd = ptx::desc_add(pd0, (h * nkt + kt) * (KT_ROWS * BM * 2));
+      const uint32_t dd = tbase + o_col + h * BM;
+#pragma unroll
+      for (int ks = 0; ks < KT_ROWS / 16; ++ks)
+        if (ks < ksteps && ptx::elect_one())
+          ptx::mma_f16_ss(dd, ptx::desc_add(ad, ks * 2048), ptx::desc_add(bd, ks * (2 * BM * 16)), idesc_pv,
+                          (kt > 0 || ks > 0));
+      if (ptx::elect_one()) ptx::mma_commit(bar_free + slot);
+      __syncwarp();
+    }
+    if (ptx::elect_one()) ptx::mma_commit(bar_O);
     __syncwarp();
+    if (lane == 0) TL_STAMP(10);
   } else {
     // ================================================= compose warps
     // stage the static mix and the per-query weights (fp32) while the first loads fly
@@ -654,75 +667,90 @@ __global__ void __launch_bounds__(32 * NW, 1)
     __syncwarp();
   } else if (role == ROLE_MMA) {
     // ================================================= MMA issuer
-    if (lane == 0) {
-      const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
-      const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 128, BM);
-      const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 128, BM);
-      const uint32_t ring_addr = ptx::smem_u32(smem + geo.ring_off);
-      int job = 0;
-      bool ok = true;
-      auto pv = [&](int pit) {
-        const int buf = pit & 1;
-        if (!ptx::mbar_wait(bar_P + buf, (pit >> 1) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_P); return; }
+    // Whole warp runs the loops; one elected lane issues each tcgen05 op, with
+    // descriptors formed as base + offset (cheap to issue back to back).
+    const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
+    const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 128, BM);
+    const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 128, BM);
+    const uint32_t ring_addr = ptx::smem_u32(smem + geo.ring_off);
+    int job = 0;
+    bool ok = true;
+    auto wait_u = [&](uint64_t *bar, int parity, int code) {
+      const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait(bar, parity, WAIT));
+      if (ok && !got) {
+        ok = false;
+        if (lane == 0) record_err(p, code);
+      }
+      return ok;
+    };
+    auto pv = [&](int pit) {
+      const int buf = pit & 1;
+      if (!wait_u(bar_P + buf, (pit >> 1) & 1, ERR_TIMEOUT_P)) return;
+      ptx::tc_fence_after();
+      for (int jj = 0; jj < nK && ok; ++jj, ++job) {
+        const int slot = job % nslot;
+        if (!wait_u(bar_full + slot, (job / nslot) & 1, ERR_TIMEOUT_FULL)) return;
         ptx::tc_fence_after();
-        for (int jj = 0; jj < nK && ok; ++jj, ++job) {
-          const int slot = job % nslot;
-          if (!ptx::mbar_wait(bar_full + slot, (job / nslot) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); return; }
-          ptx::tc_fence_after();
-          const Job jb = job_of(jj);
-          for (int u = 0; u < jb.nh; ++u) {
-            const int h = jb.h0 + u;
-            const uint32_t a0 = ring_addr + slot * TILE_BYTES + u * 2 * jb.half;
-            const uint32_t b0 = ptx::smem_u32(p_tile(buf, jb.kt)) + h * (jb.rows * BM * 2);
-            for (int ks = 0; ks < jb.rows / 16; ++ks) {
-              // V: MN-major 128B swizzle, 8-key groups 1024 B apart, d halves jb.half apart
-              const uint64_t ad = ptx::smem_desc(a0 + ks * 2048, jb.half, 1024, 2);
-              const uint64_t bd = ptx::smem_desc(b0 + ks * (2 * BM * 16), BM * 16, 128, 0);
-              ptx::mma_f16_ss(tbase + buf * 256 + h * BM, ad, bd, idesc_pv, (jb.kt > 0 || ks > 0));
-            }
-          }
-          ptx::mma_commit(bar_free + slot);
-        }
-        ptx::mma_commit(bar_O + buf);
-      };
-      int it = 0;
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
-        const int buf = it & 1;
-        // TMEM buffer free once the epilogue of tile it-2 has read its O
-        if (it >= 2 && !ptx::mbar_wait(bar_Ofree + buf, ((it - 2) >> 1) & 1, WAIT)) {
-          ok = false; record_err(p, ERR_TIMEOUT_O); break;
-        }
-        TLP_STAMP(it, 7);
-        if (!ptx::mbar_wait(bar_q + buf, (it >> 1) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_Q); break; }
-        TLP_STAMP(it, 8);
-        ptx::tc_fence_after();
-        const uint32_t q_addr = ptx::smem_u32(smem + geo.q_off + buf * NQ * 256);
-        for (int jj = 0; jj < nK && ok; ++jj, ++job) {
-          const int slot = job % nslot;
-          if (!ptx::mbar_wait(bar_full + slot, (job / nslot) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_FULL); break; }
-          ptx::tc_fence_after();
-          const Job jb = job_of(jj);
-          for (int u = 0; u < jb.nh; ++u) {
-            const int h = jb.h0 + u;
-            const uint32_t a0 = ring_addr + slot * TILE_BYTES + u * 2 * jb.half;
-            const uint32_t b0 = q_addr + h * BM * 256;
+        const Job jb = job_of(jj);
+        const int nks = jb.rows / 16;
+        for (int u = 0; u < jb.nh; ++u) {
+          const int h = jb.h0 + u;
+          // V: MN-major 128B swizzle, 8-key groups 1024 B apart, d halves jb.half apart
+          const uint64_t ad = ptx::smem_desc(ring_addr + slot * TILE_BYTES + u * 2 * jb.half, jb.half, 1024, 2);
+          const uint64_t bd =
+              ptx::smem_desc(ptx::smem_u32(p_tile(buf, jb.kt)) + h * (jb.rows * BM * 2), BM * 16, 128, 0);
+          const uint32_t dd = tbase + buf * 256 + h * BM;
 #pragma unroll
-            for (int ks = 0; ks < D / 16; ++ks) {
-              const uint64_t ad = ptx::smem_desc(a0 + (ks >> 2) * jb.half + (ks & 3) * 32, 16, 1024, 2);
-              const uint64_t bd = ptx::smem_desc(b0 + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 16, 1024, 2);
-              ptx::mma_f16_ss(tbase + buf * 256 + jb.kt * KT_ROWS + h * BM, ad, bd, idesc_qk, ks > 0);
-            }
-          }
+          for (int ks = 0; ks < KT_ROWS / 16; ++ks)
+            if (ks < nks && ptx::elect_one())
+              ptx::mma_f16_ss(dd, ptx::desc_add(ad, ks * 2048), ptx::desc_add(bd, ks * (2 * BM * 16)), idesc_pv,
+                              (jb.kt > 0 || ks > 0));
+          __syncwarp();
+        }
+        if (ptx::elect_one()) ptx::mma_commit(bar_free + slot);
+        __syncwarp();
+      }
+      if (ptx::elect_one()) ptx::mma_commit(bar_O + buf);
+      __syncwarp();
+    };
+    int it = 0;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+      const int buf = it & 1;
+      // TMEM buffer free once the epilogue of tile it-2 has read its O
+      if (it >= 2 && !wait_u(bar_Ofree + buf, ((it - 2) >> 1) & 1, ERR_TIMEOUT_O)) break;
+      if (lane == 0) TLP_STAMP(it, 7);
+      if (!wait_u(bar_q + buf, (it >> 1) & 1, ERR_TIMEOUT_Q)) break;
+      if (lane == 0) TLP_STAMP(it, 8);
+      ptx::tc_fence_after();
+      const uint64_t qd0 = ptx::smem_desc(ptx::smem_u32(smem + geo.q_off + buf * NQ * 256), 16, 1024, 2);
+      for (int jj = 0; jj < nK && ok; ++jj, ++job) {
+        const int slot = job % nslot;
+        if (!wait_u(bar_full + slot, (job / nslot) & 1, ERR_TIMEOUT_FULL)) break;
+        ptx::tc_fence_after();
+        const Job jb = job_of(jj);
+        for (int u = 0; u < jb.nh; ++u) {
+          const int h = jb.h0 + u;
+          const uint64_t ad = ptx::smem_desc(ring_addr + slot * TILE_BYTES + u * 2 * jb.half, 16, 1024, 2);
+          const uint64_t bd = ptx::desc_add(qd0, h * BM * 256);
+          const uint32_t dd = tbase + buf * 256 + jb.kt * KT_ROWS + h * BM;
+#pragma unroll
+          for (int ks = 0; ks < D / 16; ++ks)
+            if (ptx::elect_one())
+              ptx::mma_f16_ss(dd, ptx::desc_add(ad, (ks >> 2) * jb.half + (ks & 3) * 32),
+                              ptx::desc_add(bd, (ks >> 2) * (BM * 128) + (ks & 3) * 32), idesc_qk, ks > 0);
+          __syncwarp();
+        }
+        if (ptx::elect_one()) {
           ptx::mma_commit(bar_free + slot);
           if (jb.h0 + jb.nh == HPG) ptx::mma_commit(bar_S + 2 * buf + jb.kt);
         }
-        TLP_STAMP(it, 9);
-        if (it >= 1 && ok) pv(it - 1);
-        TLP_STAMP(it, 10);
+        __syncwarp();
       }
+      if (lane == 0) TLP_STAMP(it, 9);
       if (it >= 1 && ok) pv(it - 1);
+      if (lane == 0) TLP_STAMP(it, 10);
     }
-    __syncwarp();
+    if (it >= 1 && ok) pv(it - 1);
   } else if ((role & 0xF0) == ROLE_EPI) {
     // ================================================= epilogue: O^T (lanes = d) -> SMEM -> TMA store
     const int quarter = warp & 3, d = 32 * quarter + lane;

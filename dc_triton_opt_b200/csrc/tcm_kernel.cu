@@ -39,7 +39,14 @@ using namespace tc;
 constexpr int KT = 64;             // keys per tile
 constexpr int KJOB = KT * 256;     // one ring job: one head, 64 keys x 128 d
 constexpr int NCW = 8;             // compose warps (2 per lane quarter)
-constexpr int NSLOT = 3;
+#ifndef TCM_NSLOT
+#define TCM_NSLOT 4
+#endif
+constexpr int NSLOT = TCM_NSLOT;  // K/V ring slots (16 KB each)
+// Heads whose MMAs are interleaved: the K steps of one head accumulate into one
+// TMEM tile and serialise, so independent heads are issued K step by K step.
+constexpr int HJ = 2;
+static_assert(NSLOT >= HJ, "an interleaved group needs its jobs resident");
 constexpr uint32_t S_COL = 0, D_COL = 128, O_COL = 256;
 
 template <int HPG>
@@ -71,7 +78,7 @@ __host__ __device__ inline GeoM make_geo_m() {
   g.recf = round_up(HPG * (2 * R + 1), 4);
   g.rec_off = round_up(o, 16); o = g.rec_off + 2 * SH::BM * g.recf * 4;
   g.stat_off = o; o += 2 * SH::NCOL * 4;
-  g.bar_off = round_up(o, 8); o = g.bar_off + 24 * 8;
+  g.bar_off = round_up(o, 8); o = g.bar_off + (2 * NSLOT + 14) * 8;
   g.tmem_off = o; o += 16;
   g.total = o;
   return g;
@@ -122,9 +129,9 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
   float *redm = reinterpret_cast<float *>(smem + geo.p_off), *reds = redm + 4 * NCOL;
   float *mval = reinterpret_cast<float *>(smem + geo.stat_off), *linv = mval + NCOL;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + geo.bar_off);
-  uint64_t *bar_full = bars + 0, *bar_free = bars + 3, *bar_q = bars + 6, *bar_S = bars + 7;
-  uint64_t *bar_Sfree = bars + 8, *bar_P = bars + 9, *bar_Pfree = bars + 10, *bar_O = bars + 11;
-  uint64_t *bar_A = bars + 12, *bar_D = bars + 16;  // per compose sub-group (4 each)
+  uint64_t *bar_full = bars + 0, *bar_free = bars + NSLOT, *bar_q = bars + 2 * NSLOT, *bar_S = bar_q + 1;
+  uint64_t *bar_Sfree = bar_q + 2, *bar_P = bar_q + 3, *bar_Pfree = bar_q + 4, *bar_O = bar_q + 5;
+  uint64_t *bar_A = bar_q + 6, *bar_D = bar_q + 10;  // per compose sub-group (4 each)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + geo.tmem_off);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -200,119 +207,147 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
     __syncwarp();
   } else if (warp == mma_warp) {
     // ============================================================ MMA issuer
-    if (lane == 0) {
-      const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
-      const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 64, BM);
-      const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 64, BM);
-      const uint32_t idesc_mix = ptx::idesc_f16(0, 0, 0, 64, HH);  // fp16 x fp16
-      const uint32_t q_addr = ptx::smem_u32(smem + geo.q_off);
-      const uint32_t ring_addr = ptx::smem_u32(smem + geo.ring_off);
-      const uint32_t a_addr = ptx::smem_u32(smem + geo.a_off);
-      const uint32_t p_addr = ptx::smem_u32(smem + geo.p_off);
-      const uint32_t bm_addr = ptx::smem_u32(smem + geo.bm_off);
-      int job = 0, sidx = 0;
-      bool ok = ptx::mbar_wait(bar_q, 0, WAIT);
-      if (!ok) record_err(p, ERR_TIMEOUT_Q);
+    // The whole warp runs the issue loops (uniform control flow) and one
+    // elected lane issues each tcgen05 instruction; descriptors are bases plus
+    // compile-time offsets, so an MMA costs a few instructions to issue.
+    const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
+    const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 64, BM);
+    const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 64, BM);
+    const uint32_t idesc_mix = ptx::idesc_f16(0, 0, 0, 64, HH);  // fp16 x fp16
+    const uint64_t dq0 = ptx::smem_desc(ptx::smem_u32(smem + geo.q_off), 16, 1024, 2);      // Q: K-major SW128
+    const uint64_t dk0 = ptx::smem_desc(ptx::smem_u32(smem + geo.ring_off), 16, 1024, 2);   // K: K-major SW128
+    const uint64_t dv0 = ptx::smem_desc(ptx::smem_u32(smem + geo.ring_off), KJOB / 2, 1024, 2);  // V: MN-major
+    const uint64_t dp0 = ptx::smem_desc(ptx::smem_u32(smem + geo.p_off), BM * 16, 128, 0);  // P': MN-major
+    const uint64_t da0 = ptx::smem_desc(ptx::smem_u32(smem + geo.a_off), 128, KB * 128, 0); // mix A: K-major
+    const uint64_t db0 = ptx::smem_desc(ptx::smem_u32(smem + geo.bm_off), 128, KB * 128, 0);
+    int job = 0, sidx = 0;
+    long long w_ring = 0, w_a = 0, w_other = 0;  // timeline: cycles waited (development builds)
+    bool ok = true;
+    auto wait_u = [&](uint64_t *bar, int parity, int code, long long &acc) {
+      const long long t0 = TL_CLK();
+      const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait(bar, parity, WAIT));
+      if (ok && !got) {
+        ok = false;
+        if (lane == 0) record_err(p, code);
+      }
+      acc += TL_CLK() - t0;
+    };
+    wait_u(bar_q, 0, ERR_TIMEOUT_Q, w_other);
+    ptx::tc_fence_after();
+    auto qk = [&]() {
+      if (sidx >= 1) wait_u(bar_Sfree, (sidx - 1) & 1, ERR_TIMEOUT_S, w_other);
+      ++sidx;
+      if (!ok) return;
       ptx::tc_fence_after();
-      auto ring_wait = [&]() -> uint32_t {
-        const int slot = job % NSLOT;
-        if (!ptx::mbar_wait(bar_full + slot, (job / NSLOT) & 1, WAIT)) {
-          ok = false;
-          record_err(p, ERR_TIMEOUT_FULL);
-        }
-        ptx::tc_fence_after();
-        return ring_addr + slot * KJOB;
-      };
-      auto qk = [&]() {
-        if (sidx >= 1 && !ptx::mbar_wait(bar_Sfree, (sidx - 1) & 1, WAIT)) {
-          ok = false;
-          record_err(p, ERR_TIMEOUT_S);
-        }
-        ++sidx;
+      for (int h0 = 0; h0 < HPG; h0 += HJ, job += HJ) {
+        for (int hh = 0; hh < HJ; ++hh) wait_u(bar_full + ((job + hh) % NSLOT), ((job + hh) / NSLOT) & 1, ERR_TIMEOUT_FULL, w_ring);
         if (!ok) return;
         ptx::tc_fence_after();
-        for (int h = 0; h < HPG && ok; ++h, ++job) {
-          const uint32_t a0 = ring_wait();
-          if (!ok) return;
-          const uint32_t b0 = q_addr + h * BM * 256;
-          const uint32_t d = tbase + (static_cast<uint32_t>(16 * (h / HH)) << 16) + S_COL + (h % HH) * BM;
+        uint64_t ka[HJ], qa[HJ];
+        uint32_t dd[HJ];
 #pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks) {
-            const uint64_t ad = ptx::smem_desc(a0 + (ks >> 2) * (KJOB / 2) + (ks & 3) * 32, 16, 1024, 2);
-            const uint64_t bd = ptx::smem_desc(b0 + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 16, 1024, 2);
-            ptx::mma_f16_ss(d, ad, bd, idesc_qk, ks > 0);
-          }
-          ptx::mma_commit(bar_free + (job % NSLOT));
+        for (int hh = 0; hh < HJ; ++hh) {
+          const int h = h0 + hh;
+          ka[hh] = ptx::desc_add(dk0, ((job + hh) % NSLOT) * KJOB);
+          qa[hh] = ptx::desc_add(dq0, h * BM * 256);
+          dd[hh] = tbase + (static_cast<uint32_t>(16 * (h / HH)) << 16) + S_COL + (h % HH) * BM;
         }
-        ptx::mma_commit(bar_S);
-      };
-      // one round of head mixes (set 0 = pre, 1 = post) for the four sub-groups
-      auto mixes = [&](int set, int round) {
-        for (int sgl = 0; sgl < NSG; ++sgl)
-          for (int cs = 0; cs < 2; ++cs) {
-            const int sg = cs * NSG + sgl;
-            if (!ok) return;
-            if (!ptx::mbar_wait(bar_A + sg, round & 1, WAIT)) {
-              ok = false;
-              record_err(p, ERR_TIMEOUT_P);
-              return;
-            }
-            ptx::tc_fence_after();
-            for (int ii = 0; ii < NQG; ++ii) {
-              const int i = sg * NQG + ii;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+#pragma unroll
+          for (int hh = 0; hh < HJ; ++hh)
+            if (ptx::elect_one())
+              ptx::mma_f16_ss(dd[hh], ptx::desc_add(ka[hh], (ks >> 2) * (KJOB / 2) + (ks & 3) * 32),
+                              ptx::desc_add(qa[hh], (ks >> 2) * (BM * 128) + (ks & 3) * 32), idesc_qk, ks > 0);
+        if (ptx::elect_one())
+          for (int hh = 0; hh < HJ; ++hh) ptx::mma_commit(bar_free + ((job + hh) % NSLOT));
+        __syncwarp();
+      }
+      if (ptx::elect_one()) ptx::mma_commit(bar_S);
+      __syncwarp();
+      if (lane == 0 && sidx <= 6) TL_STAMP(28 + sidx);
+    };
+    // one round of head mixes (set 0 = pre, 1 = post) for the four sub-groups
+    auto mixes = [&](int set, int round) {
+      for (int sgl = 0; sgl < NSG; ++sgl)
+        for (int cs = 0; cs < 2; ++cs) {
+          const int sg = cs * NSG + sgl;
+          wait_u(bar_A + sg, round & 1, ERR_TIMEOUT_P, w_a);
+          if (!ok) return;
+          ptx::tc_fence_after();
+          const uint64_t aq = ptx::desc_add(da0, sg * NQG * ATILE);
+          const uint64_t bq = ptx::desc_add(db0, set * (HPG * HPG * 2));
+          const uint32_t dq = tbase + D_COL + sg * NQG * HH;
+#pragma unroll
+          for (int ks = 0; ks < HPG / 16; ++ks)
+#pragma unroll
+            for (int ii = 0; ii < NQG; ++ii)
 #pragma unroll
               for (int v = 0; v < 2; ++v)
-#pragma unroll
-                for (int ks = 0; ks < HPG / 16; ++ks) {
-                  const uint64_t ad = ptx::smem_desc(a_addr + i * ATILE + ks * 256, 128, KB * 128, 0);
-                  const uint64_t bd =
-                      ptx::smem_desc(bm_addr + set * (HPG * HPG * 2) + v * (HH * HPG * 2) + ks * 256, 128, KB * 128, 0);
-                  ptx::mma_f16_ss(tbase + (static_cast<uint32_t>(16 * v) << 16) + D_COL + i * HH, ad, bd, idesc_mix,
-                                  ks > 0);
-                }
-            }
-            ptx::mma_commit(bar_D + sg);
-          }
-      };
-      auto pv = [&](int kt) {
+                if (ptx::elect_one())
+                  ptx::mma_f16_ss(dq + (static_cast<uint32_t>(16 * v) << 16) + ii * HH,
+                                  ptx::desc_add(aq, ii * ATILE + ks * 256),
+                                  ptx::desc_add(bq, v * (HH * HPG * 2) + ks * 256), idesc_mix, ks > 0);
+          if (ptx::elect_one()) ptx::mma_commit(bar_D + sg);
+          __syncwarp();
+        }
+    };
+    auto pv = [&](int kt) {
+      wait_u(bar_P, kt & 1, ERR_TIMEOUT_P, w_other);
+      if (!ok) return;
+      ptx::tc_fence_after();
+      const int nks = (kt == nkt - 1 ? rlast : KT) / 16;
+      for (int h0 = 0; h0 < HPG; h0 += HJ, job += HJ) {
+        for (int hh = 0; hh < HJ; ++hh) wait_u(bar_full + ((job + hh) % NSLOT), ((job + hh) / NSLOT) & 1, ERR_TIMEOUT_FULL, w_ring);
         if (!ok) return;
-        if (!ptx::mbar_wait(bar_P, kt & 1, WAIT)) {
-          ok = false;
-          record_err(p, ERR_TIMEOUT_P);
-          return;
-        }
         ptx::tc_fence_after();
-        const int rows = kt == nkt - 1 ? rlast : KT;
-        for (int h = 0; h < HPG && ok; ++h, ++job) {
-          const uint32_t a0 = ring_wait();
-          if (!ok) return;
-          const uint32_t b0 = p_addr + h * PHEAD;
+        uint64_t va[HJ], pa[HJ];
+        uint32_t dd[HJ];
 #pragma unroll
-          for (int c = 0; c < 2; ++c)
-            for (int ks = 0; ks < rows / 16; ++ks) {
-              const uint64_t ad = ptx::smem_desc(a0 + c * (KJOB / 2) + ks * 2048, KJOB / 2, 1024, 2);
-              const uint64_t bd = ptx::smem_desc(b0 + ks * (2 * BM * 16), BM * 16, 128, 0);
-              ptx::mma_f16_ss(tbase + (static_cast<uint32_t>(16 * c) << 16) + O_COL + h * BM, ad, bd, idesc_pv,
-                              (kt > 0 || ks > 0));
-            }
-          ptx::mma_commit(bar_free + (job % NSLOT));
+        for (int hh = 0; hh < HJ; ++hh) {
+          const int h = h0 + hh;
+          va[hh] = ptx::desc_add(dv0, ((job + hh) % NSLOT) * KJOB);
+          pa[hh] = ptx::desc_add(dp0, h * PHEAD);
+          dd[hh] = tbase + O_COL + h * BM;
         }
-        ptx::mma_commit(bar_Pfree);
-      };
-      for (int kt = 0; kt < nkt && ok; ++kt) {
-        qk();
-        mixes(0, kt);
+#pragma unroll
+        for (int ks = 0; ks < KT / 16; ++ks) {
+          if (ks < nks) {
+#pragma unroll
+            for (int hh = 0; hh < HJ; ++hh)
+#pragma unroll
+              for (int c = 0; c < 2; ++c)
+                if (ptx::elect_one())
+                  ptx::mma_f16_ss(dd[hh] + (static_cast<uint32_t>(16 * c) << 16),
+                                  ptx::desc_add(va[hh], c * (KJOB / 2) + ks * 2048),
+                                  ptx::desc_add(pa[hh], ks * (2 * BM * 16)), idesc_pv, (kt > 0 || ks > 0));
+          }
+        }
+        if (ptx::elect_one())
+          for (int hh = 0; hh < HJ; ++hh) ptx::mma_commit(bar_free + ((job + hh) % NSLOT));
+        __syncwarp();
       }
-      if (ok) qk();
-      for (int kt = 0; kt < nkt && ok; ++kt) {
-        mixes(0, nkt + 2 * kt);
-        mixes(1, nkt + 2 * kt + 1);
-        if (kt + 1 < nkt) qk();
-        pv(kt);
-      }
-      ptx::mma_commit(bar_O);
+      if (ptx::elect_one()) ptx::mma_commit(bar_Pfree);
+      __syncwarp();
+    };
+    for (int kt = 0; kt < nkt && ok; ++kt) {
+      qk();
+      mixes(0, kt);
     }
+    if (ok) qk();
+    for (int kt = 0; kt < nkt && ok; ++kt) {
+      mixes(0, nkt + 2 * kt);
+      mixes(1, nkt + 2 * kt + 1);
+      if (kt + 1 < nkt) qk();
+      pv(kt);
+    }
+    if (ptx::elect_one()) ptx::mma_commit(bar_O);
     __syncwarp();
+    if (lane == 0) {
+      TL_VAL(35, w_ring);
+      TL_VAL(36, w_a);
+      TL_VAL(37, w_other);
+    }
   } else {
     // ============================================================ compose warps
     const int qtr = warp & 3, cs = warp >> 2;
@@ -360,11 +395,14 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
     ptx::named_bar_sync(1, 32 * NCW);
 
     bool ok = true;
+    long long w_comp = 0;  // timeline: cycles waited (development builds)
     auto wait_or_fail = [&](uint64_t *bar, int parity, int code) {
+      const long long t0 = TL_CLK();
       if (ok && !ptx::mbar_wait(bar, parity, WAIT)) {
         ok = false;
         record_err(p, code);
       }
+      w_comp += TL_CLK() - t0;
     };
     auto arrive = [&](uint64_t *bar) {
       ptx::fence_proxy_async_smem();
@@ -471,6 +509,8 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
 #pragma unroll
     for (int k = 0; k < NSG; ++k) { m_run[k][0] = m_run[k][1] = -INFINITY; l_run[k][0] = l_run[k][1] = 0.f; }
 
+    const bool tlw = warp == 0 && lane == 0;  // timeline stamps (development builds)
+    if (tlw) TL_STAMP(0);
     // ============================== pass A: statistics of the composed logits
     for (int kt = 0; kt < nkt; ++kt) {
       const int s = k_lo + kt * KT + key_local;
@@ -478,6 +518,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       const int64_t tok = (int64_t)b * T + s;
       wait_or_fail(bar_S, kt & 1, ERR_TIMEOUT_S);
       ptx::tc_fence_after();
+      if (tlw && kt < 3) TL_STAMP(1 + 4 * kt);
       float aq[NSG][NQG][R], ak[NSG][NQG][R];
 #pragma unroll
       for (int sgl = 0; sgl < NSG; ++sgl) {
@@ -488,6 +529,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
         reduce_and_stage(p.pre, 0, i0, tok, key_ok, a, aq[sgl], ak[sgl]);
         arrive(bar_A + cs * NSG + sgl);
       }
+      if (tlw && kt < 3) TL_STAMP(2 + 4 * kt);
 #pragma unroll
       for (int sgl = 0; sgl < NSG; ++sgl) {
         const int sg = cs * NSG + sgl, i0 = sg * NQG;
@@ -529,6 +571,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
             m_run[sgl][k] = mn;
           }
       }
+      if (tlw && kt < 3) TL_STAMP(3 + 4 * kt);
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_Sfree);
@@ -556,6 +599,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       linv[jc] = l > 0.f ? 1.f / l : 0.f;
     }
     ptx::named_bar_sync(1, 32 * NCW);
+    if (tlw) TL_STAMP(12);
 
     // ============================== pass B: probabilities, post mix, P'V
     for (int kt = 0; kt < nkt; ++kt) {
@@ -565,6 +609,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       const int rpre = nkt + 2 * kt, rpost = rpre + 1;
       wait_or_fail(bar_S, (nkt + kt) & 1, ERR_TIMEOUT_S);
       ptx::tc_fence_after();
+      if (tlw && kt < 3) TL_STAMP(13 + 5 * kt);
       float aq[NSG][NQG][R], ak[NSG][NQG][R];
 #pragma unroll
       for (int sgl = 0; sgl < NSG; ++sgl) {
@@ -575,6 +620,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
         reduce_and_stage(p.pre, 0, i0, tok, key_ok, a, aq[sgl], ak[sgl]);
         arrive(bar_A + cs * NSG + sgl);
       }
+      if (tlw && kt < 3) TL_STAMP(14 + 5 * kt);
       float pr[NSG][HH][NQG], pq[NSG][NQG][R], pk[NSG][NQG][R];
 #pragma unroll
       for (int sgl = 0; sgl < NSG; ++sgl) {
@@ -597,10 +643,12 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
         reduce_and_stage(p.post, 1, i0, tok, key_ok, pr[sgl], pq[sgl], pk[sgl]);
         arrive(bar_A + sg);
       }
+      if (tlw && kt < 3) TL_STAMP(15 + 5 * kt);
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_Sfree);
       if (kt >= 1) wait_or_fail(bar_Pfree, (kt - 1) & 1, ERR_TIMEOUT_P);
+      if (tlw && kt < 3) TL_STAMP(16 + 5 * kt);
 #pragma unroll
       for (int sgl = 0; sgl < NSG; ++sgl) {
         const int sg = cs * NSG + sgl, i0 = sg * NQG;
@@ -621,6 +669,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
           }
       }
       arrive(bar_P);
+      if (tlw && kt < 3) TL_STAMP(17 + 5 * kt);
     }
 
     // ============================== epilogue: O^T -> SMEM [head][d half][query][64 d] -> TMA store
@@ -648,6 +697,8 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       ptx::bulk_commit();
       ptx::bulk_wait_read0();
     }
+    if (tlw) TL_STAMP(28);
+    if (tlw) TL_VAL(38, w_comp);
   }
 
   ptx::tc_fence_before();

@@ -167,81 +167,78 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
     __syncwarp();
   } else if (warp == mma_warp) {
     // ================================================= MMA issuer
-    if (lane == 0) {
-      const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
-      const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 128, BM);
-      const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 128, BM);
-      const uint32_t q_addr = ptx::smem_u32(smem + geo.q_off);
-      const uint32_t ring_addr = ptx::smem_u32(smem + geo.ring_off);
-      const uint32_t p_addr = ptx::smem_u32(smem + geo.p_off);
-      int job = 0;
-      bool ok = ptx::mbar_wait(bar_q, 0, WAIT);
-      if (!ok) record_err(p, ERR_TIMEOUT_Q);
-      ptx::tc_fence_after();
-      auto qk = [&](int sidx) {
-        const int sb = sidx % NSB;
-        if (sidx >= NSB && !ptx::mbar_wait(bar_Sfree + sb, ((sidx - NSB) / NSB) & 1, WAIT)) {
-          ok = false;
-          record_err(p, ERR_TIMEOUT_S);
-          return;
-        }
-        ptx::tc_fence_after();
-        for (int h = 0; h < HPG && ok; ++h, ++job) {
-          const int slot = job % NSLOT;
-          if (!ptx::mbar_wait(bar_full + slot, (job / NSLOT) & 1, WAIT)) {
-            ok = false;
-            record_err(p, ERR_TIMEOUT_FULL);
-            return;
-          }
-          ptx::tc_fence_after();
-          const uint32_t a0 = ring_addr + slot * TILE_BYTES;
-          const uint32_t b0 = q_addr + h * BM * 256;
-#pragma unroll
-          for (int ks = 0; ks < D / 16; ++ks) {
-            const uint64_t ad = ptx::smem_desc(a0 + (ks >> 2) * (TILE_BYTES / 2) + (ks & 3) * 32, 16, 1024, 2);
-            const uint64_t bd = ptx::smem_desc(b0 + (ks >> 2) * (BM * 128) + (ks & 3) * 32, 16, 1024, 2);
-            ptx::mma_f16_ss(tbase + sb * NQT + h * BM, ad, bd, idesc_qk, ks > 0);
-          }
-          ptx::mma_commit(bar_free + slot);
-        }
-        ptx::mma_commit(bar_S + sb);
-      };
-      auto pv = [&](int kt) {
-        const int pb = kt % NPB;
-        if (!ptx::mbar_wait(bar_P + pb, (kt / NPB) & 1, WAIT)) {
-          ok = false;
-          record_err(p, ERR_TIMEOUT_P);
-          return;
-        }
-        ptx::tc_fence_after();
-        const int rows = kt == nkt - 1 ? rlast : KT_ROWS;
-        for (int h = 0; h < HPG && ok; ++h, ++job) {
-          const int slot = job % NSLOT;
-          if (!ptx::mbar_wait(bar_full + slot, (job / NSLOT) & 1, WAIT)) {
-            ok = false;
-            record_err(p, ERR_TIMEOUT_FULL);
-            return;
-          }
-          ptx::tc_fence_after();
-          const uint32_t a0 = ring_addr + slot * TILE_BYTES;
-          const uint32_t b0 = p_addr + pb * (KT_ROWS * NQT * 2) + h * (KT_ROWS * BM * 2);
-          for (int ks = 0; ks < rows / 16; ++ks) {
-            const uint64_t ad = ptx::smem_desc(a0 + ks * 2048, TILE_BYTES / 2, 1024, 2);
-            const uint64_t bd = ptx::smem_desc(b0 + ks * (2 * BM * 16), BM * 16, 128, 0);
-            ptx::mma_f16_ss(tbase + o_col + h * BM, ad, bd, idesc_pv, (kt > 0 || ks > 0));
-          }
-          ptx::mma_commit(bar_free + slot);
-        }
-        ptx::mma_commit(bar_Pfree + pb);
-      };
-      for (int kt = 0; kt < nkt && ok; ++kt) qk(kt);
-      for (int kt = 0; kt < nkt && ok; ++kt) {
-        qk(nkt + kt);
-        if (kt >= 1 && ok) pv(kt - 1);
+    // Whole warp runs the loops; one elected lane issues each tcgen05 op.
+    const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
+    const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 128, BM);
+    const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 128, BM);
+    const uint64_t qd0 = ptx::smem_desc(ptx::smem_u32(smem + geo.q_off), 16, 1024, 2);
+    const uint64_t kd0 = ptx::smem_desc(ptx::smem_u32(smem + geo.ring_off), 16, 1024, 2);
+    const uint64_t vd0 = ptx::smem_desc(ptx::smem_u32(smem + geo.ring_off), TILE_BYTES / 2, 1024, 2);
+    const uint64_t pd0 = ptx::smem_desc(ptx::smem_u32(smem + geo.p_off), BM * 16, 128, 0);
+    int job = 0;
+    bool ok = true;
+    auto wait_u = [&](uint64_t *bar, int parity, int code) {
+      const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait(bar, parity, WAIT));
+      if (ok && !got) {
+        ok = false;
+        if (lane == 0) record_err(p, code);
       }
-      if (ok) pv(nkt - 1);
-      ptx::mma_commit(bar_O);
+      return ok;
+    };
+    wait_u(bar_q, 0, ERR_TIMEOUT_Q);
+    ptx::tc_fence_after();
+    auto qk = [&](int sidx) {
+      const int sb = sidx % NSB;
+      if (sidx >= NSB && !wait_u(bar_Sfree + sb, ((sidx - NSB) / NSB) & 1, ERR_TIMEOUT_S)) return;
+      ptx::tc_fence_after();
+      for (int h = 0; h < HPG && ok; ++h, ++job) {
+        const int slot = job % NSLOT;
+        if (!wait_u(bar_full + slot, (job / NSLOT) & 1, ERR_TIMEOUT_FULL)) return;
+        ptx::tc_fence_after();
+        const uint64_t ad = ptx::desc_add(kd0, slot * TILE_BYTES);
+        const uint64_t bd = ptx::desc_add(qd0, h * BM * 256);
+        const uint32_t dd = tbase + sb * NQT + h * BM;
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          if (ptx::elect_one())
+            ptx::mma_f16_ss(dd, ptx::desc_add(ad, (ks >> 2) * (TILE_BYTES / 2) + (ks & 3) * 32),
+                            ptx::desc_add(bd, (ks >> 2) * (BM * 128) + (ks & 3) * 32), idesc_qk, ks > 0);
+        if (ptx::elect_one()) ptx::mma_commit(bar_free + slot);
+        __syncwarp();
+      }
+      if (ptx::elect_one()) ptx::mma_commit(bar_S + sb);
+      __syncwarp();
+    };
+    auto pv = [&](int kt) {
+      const int pb = kt % NPB;
+      if (!wait_u(bar_P + pb, (kt / NPB) & 1, ERR_TIMEOUT_P)) return;
+      ptx::tc_fence_after();
+      const int nks = (kt == nkt - 1 ? rlast : KT_ROWS) / 16;
+      for (int h = 0; h < HPG && ok; ++h, ++job) {
+        const int slot = job % NSLOT;
+        if (!wait_u(bar_full + slot, (job / NSLOT) & 1, ERR_TIMEOUT_FULL)) return;
+        ptx::tc_fence_after();
+        const uint64_t ad = ptx::desc_add(vd0, slot * TILE_BYTES);
+        const uint64_t bd = ptx::desc_add(pd0, pb * (KT_ROWS * NQT * 2) + h * (KT_ROWS * BM * 2));
+        const uint32_t dd = tbase + o_col + h * BM;
+#pragma unroll
+        for (int ks = 0; ks < KT_ROWS / 16; ++ks)
+          if (ks < nks && ptx::elect_one())
+            ptx::mma_f16_ss(dd, ptx::desc_add(ad, ks * 2048), ptx::desc_add(bd, ks * (2 * BM * 16)), idesc_pv,
+                            (kt > 0 || ks > 0));
+        if (ptx::elect_one()) ptx::mma_commit(bar_free + slot);
+        __syncwarp();
+      }
+      if (ptx::elect_one()) ptx::mma_commit(bar_Pfree + pb);
+      __syncwarp();
+    };
+    for (int kt = 0; kt < nkt && ok; ++kt) qk(kt);
+    for (int kt = 0; kt < nkt && ok; ++kt) {
+      qk(nkt + kt);
+      if (kt >= 1 && ok) pv(kt - 1);
     }
+    if (ok) pv(nkt - 1);
+    if (ptx::elect_one()) ptx::mma_commit(bar_O);
     __syncwarp();
   } else {
     // ================================================= compose warps
