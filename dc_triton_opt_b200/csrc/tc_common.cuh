@@ -90,11 +90,20 @@ __device__ unsigned long long g_timeline[8192][40];
     if (cta_ < 8192) g_timeline[cta_][i] = (v);                                       \
   } while (0)
 #define TL_CLK() clock64()
+// per-job times of one CTA (development builds): [0] producer issue, [1] consumer ready
+__device__ long long g_jobt[2][256];
+#define TL_JOB(k, j)                                                                      \
+  do {                                                                                    \
+    if (blockIdx.x == 5 && blockIdx.y == 0 && (j) < 256) g_jobt[k][j] = clock64();        \
+  } while (0)
 #else
 #define TL_VAL(i, v) \
   do {               \
   } while (0)
 #define TL_CLK() 0ll
+#define TL_JOB(k, j) \
+  do {               \
+  } while (0)
 #define TLP_STAMP(it, i) \
   do {                   \
   } while (0)

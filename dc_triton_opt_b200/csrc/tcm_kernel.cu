@@ -39,15 +39,27 @@ using namespace tc;
 constexpr int KT = 64;             // keys per tile
 constexpr int KJOB = KT * 256;     // one ring job: one head, 64 keys x 128 d
 constexpr int NCW = 8;             // compose warps (2 per lane quarter)
-#ifndef TCM_NSLOT
-#define TCM_NSLOT 4
+#ifndef TCM_NSK
+#define TCM_NSK 3
 #endif
-constexpr int NSLOT = TCM_NSLOT;  // K/V ring slots (16 KB each)
+#ifndef TCM_NSV
+#define TCM_NSV 2
+#endif
+// Separate K and V rings (16 KB slots), each with one producer warp and one
+// MMA warp consuming it in order: an mbarrier parity wait is only unambiguous
+// for a consumer at most one phase behind, so a ring never has two consumers.
+constexpr int NSK = TCM_NSK, NSV = TCM_NSV;
+// Pass A streams K alone and P' is idle until pass B, so the pass-A K ring
+// also uses the P' buffer as two more slots.
+constexpr int NKA = NSK + 2;
 // Heads whose MMAs are interleaved: the K steps of one head accumulate into one
 // TMEM tile and serialise, so independent heads are issued K step by K step.
-constexpr int HJ = 2;
-static_assert(NSLOT >= HJ, "an interleaved group needs its jobs resident");
+constexpr int HJ = 1;
+static_assert(NSK >= HJ && NSV >= HJ, "an interleaved group needs its jobs resident");
 constexpr uint32_t S_COL = 0, D_COL = 128, O_COL = 256;
+// Pass A double-buffers S in the O columns (idle until pass B): S tile n of
+// pass A uses buffer n & 1; pass B uses buffer 0 only.
+__host__ __device__ constexpr uint32_t s_col(int buf) { return buf ? O_COL : S_COL; }
 
 template <int HPG>
 struct Shape {
@@ -62,7 +74,7 @@ struct Shape {
 };
 
 struct GeoM {
-  int q_off, ring_off, a_off, p_off, bm_off, rec_off, stat_off, bar_off, tmem_off, total, recf;
+  int q_off, kring_off, vring_off, a_off, p_off, bm_off, rec_off, stat_off, bar_off, tmem_off, total, recf;
 };
 
 template <int HPG, int R>
@@ -70,32 +82,53 @@ __host__ __device__ inline GeoM make_geo_m() {
   using SH = Shape<HPG>;
   GeoM g{};
   g.q_off = 0;                                  // Q: HPG x BM x 256 B (64 KB); output staging at the end
-  g.ring_off = HPG * SH::BM * 256;
-  g.a_off = g.ring_off + NSLOT * KJOB;          // mix operands, BM x 64 keys x HPG fp16 (32 KB)
+  g.kring_off = HPG * SH::BM * 256;
+  g.vring_off = g.kring_off + NSK * KJOB;
+  g.a_off = g.vring_off + NSV * KJOB;           // mix operands, BM x 64 keys x HPG fp16 (32 KB)
   g.p_off = g.a_off + SH::BM * SH::ATILE;       // P': HPG x 64 keys x BM (32 KB); pass-A stats exchange
   g.bm_off = g.p_off + HPG * SH::PHEAD;         // mix B operands: 2 sets x HPG x HPG fp16
   int o = g.bm_off + 2 * HPG * HPG * 2;
   g.recf = round_up(HPG * (2 * R + 1), 4);
   g.rec_off = round_up(o, 16); o = g.rec_off + 2 * SH::BM * g.recf * 4;
   g.stat_off = o; o += 2 * SH::NCOL * 4;
-  g.bar_off = round_up(o, 8); o = g.bar_off + (2 * NSLOT + 14) * 8;
+  g.bar_off = round_up(o, 8); o = g.bar_off + (2 * (NKA + NSK + NSV) + 16) * 8;
   g.tmem_off = o; o += 16;
   g.total = o;
   return g;
 }
 
-// N consecutive per-token weights (bf16/fp16, 16-byte aligned) as floats.
-template <typename E, int N>
-__device__ __forceinline__ void ld_row(const void *base, int64_t idx, float (&w)[N]) {
-  static_assert(N % 8 == 0, "rows are read 8 elements at a time");
-  const uint4 *src = reinterpret_cast<const uint4 *>(reinterpret_cast<const E *>(base) + idx);
+// The key-wise weights of one key for the HH heads of a lane half, packed as
+// loaded (bf16/fp16); issued at the start of a tile, unpacked where used.
+template <int HH, int R>
+struct KeyW {
+  uint4 w1[HH * R / 8];  // kw1[tok, h, r]   flat (h, r)
+  uint4 w2[R * HH / 8];  // kw2[tok, r, h]   flat (r, h)
+  uint4 dd[HH / 8];      // kdd[tok, h]
+};
+
+template <typename E>
+__device__ __forceinline__ float unpack_e(const uint4 *v, int j) {
+  const E *e = reinterpret_cast<const E *>(v + j / 8);
+  return to_f<E>(e[j % 8]);
+}
+
+template <typename E, int HH, int R>
+__device__ __forceinline__ void load_keyw(KeyW<HH, R> &kw, const TermPtrs &tm, int64_t tok, int H, int h0,
+                                          bool key_ok) {
+  const uint4 z = make_uint4(0, 0, 0, 0);
+  const bool k1 = key_ok && tm.kw1, kd = key_ok && tm.kdd;
+  const uint4 *w1 = reinterpret_cast<const uint4 *>(reinterpret_cast<const E *>(tm.kw1) + (tok * H + h0) * R);
+  const uint4 *dd = reinterpret_cast<const uint4 *>(reinterpret_cast<const E *>(tm.kdd) + tok * H + h0);
 #pragma unroll
-  for (int c = 0; c < N / 8; ++c) {
-    const uint4 raw = __ldg(src + c);
-    const E *e = reinterpret_cast<const E *>(&raw);
+  for (int c = 0; c < HH * R / 8; ++c) kw.w1[c] = k1 ? __ldg(w1 + c) : z;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) w[c * 8 + j] = to_f<E>(e[j]);
+  for (int r = 0; r < R; ++r) {
+    const uint4 *w2 = reinterpret_cast<const uint4 *>(reinterpret_cast<const E *>(tm.kw2) + (tok * R + r) * H + h0);
+#pragma unroll
+    for (int c = 0; c < HH / 8; ++c) kw.w2[r * (HH / 8) + c] = k1 ? __ldg(w2 + c) : z;
   }
+#pragma unroll
+  for (int c = 0; c < HH / 8; ++c) kw.dd[c] = kd ? __ldg(dd + c) : z;
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
@@ -111,9 +144,10 @@ __device__ __forceinline__ uint32_t pack_e2(float lo, float hi) {
 }
 
 template <typename E, int HPG, int R>
-__global__ void __launch_bounds__(32 * (NCW + 2), 1)
+__global__ void __launch_bounds__(32 * (NCW + 4), 1)
     dc_tcm_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_k16,
+                  const __grid_constant__ CUtensorMap tm_v16, const __grid_constant__ CUtensorMap tm_o,
                   const TcParams p) {
   using SH = Shape<HPG>;
   constexpr int BM = SH::BM, HH = SH::HH, NQG = SH::NQG, NSG = SH::NSG, KB = SH::KB;
@@ -129,13 +163,24 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
   float *redm = reinterpret_cast<float *>(smem + geo.p_off), *reds = redm + 4 * NCOL;
   float *mval = reinterpret_cast<float *>(smem + geo.stat_off), *linv = mval + NCOL;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + geo.bar_off);
-  uint64_t *bar_full = bars + 0, *bar_free = bars + NSLOT, *bar_q = bars + 2 * NSLOT, *bar_S = bar_q + 1;
-  uint64_t *bar_Sfree = bar_q + 2, *bar_P = bar_q + 3, *bar_Pfree = bar_q + 4, *bar_O = bar_q + 5;
-  uint64_t *bar_A = bar_q + 6, *bar_D = bar_q + 10;  // per compose sub-group (4 each)
+  uint64_t *bar_afull = bars + 0, *bar_afree = bar_afull + NKA;        // pass-A K ring
+  uint64_t *bar_kfull = bar_afree + NKA, *bar_kfree = bar_kfull + NSK;  // pass-B K ring
+  uint64_t *bar_vfull = bar_kfree + NSK, *bar_vfree = bar_vfull + NSV, *bar_q = bar_vfree + NSV;
+  uint64_t *bar_S = bar_q + 1, *bar_Sfree = bar_q + 3;  // two S buffers each
+  uint64_t *bar_P = bar_q + 5, *bar_Pfree = bar_q + 6, *bar_O = bar_q + 7;
+  uint64_t *bar_A = bar_q + 8, *bar_D = bar_q + 12;  // per compose sub-group (4 each)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + geo.tmem_off);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int tma_warp = NCW, mma_warp = NCW + 1;
+  const int tma_warp = NCW, mma_warp = NCW + 1, pv_warp = NCW + 2, mix_warp = NCW + 3;
+  // Heads are visited in a per-CTA rotated order, so CTAs that run together
+  // (neighbouring query blocks, overlapping key spans) read different heads'
+  // K/V rows at any moment instead of hitting the same lines.
+  const int hrot = (blockIdx.x * 7) % HPG;
+  // byte offset of K slot `slot` of the pass-A (ring_a) or pass-B ring
+  auto kslot_off = [&](bool ring_a, int slot) {
+    return ring_a && slot >= NSK ? geo.p_off + (slot - NSK) * KJOB : geo.kring_off + slot * KJOB;
+  };
   const int nqb = (p.T + BM - 1) / BM;
   const int qb = nqb - 1 - static_cast<int>(blockIdx.x);  // longest spans first
   const int b = blockIdx.y / p.G, g = blockIdx.y % p.G;
@@ -148,13 +193,23 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
   const uint32_t WAIT = 1u << 24;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NSLOT; ++i) {
-      ptx::mbar_init(bar_full + i, 1);
-      ptx::mbar_init(bar_free + i, 1);
+    for (int i = 0; i < NKA; ++i) {
+      ptx::mbar_init(bar_afull + i, 1);
+      ptx::mbar_init(bar_afree + i, 1);
+    }
+    for (int i = 0; i < NSK; ++i) {
+      ptx::mbar_init(bar_kfull + i, 1);
+      ptx::mbar_init(bar_kfree + i, 1);
+    }
+    for (int i = 0; i < NSV; ++i) {
+      ptx::mbar_init(bar_vfull + i, 1);
+      ptx::mbar_init(bar_vfree + i, 1);
     }
     ptx::mbar_init(bar_q, 1);
-    ptx::mbar_init(bar_S, 1);
-    ptx::mbar_init(bar_Sfree, NCW);
+    for (int i = 0; i < 2; ++i) {
+      ptx::mbar_init(bar_S + i, 1);
+      ptx::mbar_init(bar_Sfree + i, NCW);
+    }
     ptx::mbar_init(bar_P, NCW);
     ptx::mbar_init(bar_Pfree, 1);
     ptx::mbar_init(bar_O, 1);
@@ -171,56 +226,85 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
   const uint32_t tbase = *tmem_slot;
 
   if (warp == tma_warp) {
-    // ============================================================ TMA producer
-    // job order: pass A K(0..nkt-1); pass B K(0), then per tile K(kt+1), V(kt)
-    if (lane == 0) {
-      ptx::tma_prefetch_desc(&tm_q);
-      ptx::tma_prefetch_desc(&tm_k);
-      ptx::tma_prefetch_desc(&tm_v);
-      ptx::mbar_expect_tx(bar_q, HPG * BM * 256);
-      for (int h = 0; h < HPG; ++h)
-        for (int c = 0; c < 2; ++c)
-          ptx::tma_load_4d(smem + geo.q_off + h * BM * 256 + c * BM * 128, &tm_q, bar_q, c * 64, hbase + h, q0, b);
-      int job = 0;
+    // ============================================================ TMA producers
+    // Lane 0 fills the K ring: pass A K(0..nkt-1), then pass B K(0..nkt-1);
+    // lane 1 the V ring: V(0..nkt-1).  The last key tile loads only the rows
+    // the span needs (16-row boxes); the MMAs never read past them except for
+    // masked keys.
+    if (lane < 2) {
+      const bool isv = lane == 1;
+      if (!isv) {
+        ptx::tma_prefetch_desc(&tm_q);
+        ptx::tma_prefetch_desc(&tm_k);
+        ptx::mbar_expect_tx(bar_q, HPG * BM * 256);
+        for (int h = 0; h < HPG; ++h)
+          for (int c = 0; c < 2; ++c)
+            ptx::tma_load_4d(smem + geo.q_off + h * BM * 256 + c * BM * 128, &tm_q, bar_q, c * 64, hbase + h, q0,
+                             b);
+      } else {
+        ptx::tma_prefetch_desc(&tm_v);
+      }
       bool ok = true;
-      auto load_tile = [&](const CUtensorMap *m, int kt) {
-        for (int h = 0; h < HPG && ok; ++h, ++job) {
-          const int slot = job % NSLOT, use = job / NSLOT;
-          if (use > 0 && !ptx::mbar_wait(bar_free + slot, (use - 1) & 1, WAIT)) {
+      // one key tile (all heads) into a ring; job counts that ring's jobs
+      auto load_tile = [&](int kt, int &job, uint64_t *full, uint64_t *freeb, int nslot, bool ring_a) {
+        const int rows = kt == nkt - 1 ? rlast : KT;
+        const CUtensorMap *m = isv ? (rows == KT ? &tm_v : &tm_v16) : (rows == KT ? &tm_k : &tm_k16);
+        const int nbox = rows == KT ? 1 : rows / 16;
+        for (int hi = 0; hi < HPG && ok; ++hi, ++job) {
+          const int h = (hi + hrot) % HPG;
+          const int slot = job % nslot, use = job / nslot;
+          if (use > 0 && !ptx::mbar_wait(freeb + slot, (use - 1) & 1, WAIT)) {
             ok = false;
             record_err(p, ERR_TIMEOUT_FREE);
             return;
           }
-          ptx::mbar_expect_tx(bar_full + slot, KJOB);
-          unsigned char *dst = smem + geo.ring_off + slot * KJOB;
-          ptx::tma_load_4d(dst, m, bar_full + slot, 0, hbase + h, k_lo + kt * KT, b);
-          ptx::tma_load_4d(dst + KJOB / 2, m, bar_full + slot, 64, hbase + h, k_lo + kt * KT, b);
+          ptx::mbar_expect_tx(full + slot, rows * 256);
+          if (!isv && ring_a) TL_JOB(0, job);
+          unsigned char *dst = smem + (isv ? geo.vring_off + slot * KJOB : kslot_off(ring_a, slot));
+          for (int x = 0; x < nbox; ++x)
+            for (int c = 0; c < 2; ++c)
+              ptx::tma_load_4d(dst + c * (KJOB / 2) + x * 2048, m, full + slot, c * 64, hbase + h,
+                               k_lo + kt * KT + x * 16, b);
         }
       };
-      for (int kt = 0; kt < nkt; ++kt) load_tile(&tm_k, kt);
-      load_tile(&tm_k, 0);
-      for (int kt = 0; kt < nkt; ++kt) {
-        if (kt + 1 < nkt) load_tile(&tm_k, kt + 1);
-        load_tile(&tm_v, kt);
+      if (isv) {
+        int job = 0;
+        for (int kt = 0; kt < nkt; ++kt) load_tile(kt, job, bar_vfull, bar_vfree, NSV, false);
+      } else {
+        int job = 0;
+        for (int kt = 0; kt < nkt; ++kt) load_tile(kt, job, bar_afull, bar_afree, NKA, true);
+        // the pass-B ring reuses the K slots: wait for their last pass-A use
+        const int na = job;
+        for (int sl = 0; sl < NSK && ok; ++sl)
+          if (sl < na) {
+            const int j = sl + ((na - 1 - sl) / NKA) * NKA;
+            if (!ptx::mbar_wait(bar_afree + sl, (j / NKA) & 1, WAIT)) {
+              ok = false;
+              record_err(p, ERR_TIMEOUT_FREE);
+            }
+          }
+        job = 0;
+        for (int kt = 0; kt < nkt; ++kt) load_tile(kt, job, bar_kfull, bar_kfree, NSK, false);
       }
     }
     __syncwarp();
-  } else if (warp == mma_warp) {
-    // ============================================================ MMA issuer
-    // The whole warp runs the issue loops (uniform control flow) and one
+  } else if (warp == mma_warp || warp == pv_warp || warp == mix_warp) {
+    // ============================================================ MMA issuers
+    // Three warps: QK^T, P'V and the head mixes, so no chain waits behind
+    // another (the mixes sit on the compose threads' critical path).  Each warp runs its loops converged and one
     // elected lane issues each tcgen05 instruction; descriptors are bases plus
-    // compile-time offsets, so an MMA costs a few instructions to issue.
+    // compile-time offsets.  Ring jobs (K or V of one head) are consumed by
+    // index, in the producer's order.
     const uint32_t ab_fmt = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
     const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 64, BM);
     const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 64, BM);
     const uint32_t idesc_mix = ptx::idesc_f16(0, 0, 0, 64, HH);  // fp16 x fp16
     const uint64_t dq0 = ptx::smem_desc(ptx::smem_u32(smem + geo.q_off), 16, 1024, 2);      // Q: K-major SW128
-    const uint64_t dk0 = ptx::smem_desc(ptx::smem_u32(smem + geo.ring_off), 16, 1024, 2);   // K: K-major SW128
-    const uint64_t dv0 = ptx::smem_desc(ptx::smem_u32(smem + geo.ring_off), KJOB / 2, 1024, 2);  // V: MN-major
+    const uint64_t dsm = ptx::smem_desc(ptx::smem_u32(smem), 16, 1024, 2);  // K: K-major SW128, + slot offset
+    const uint64_t dv0 = ptx::smem_desc(ptx::smem_u32(smem + geo.vring_off), KJOB / 2, 1024, 2);  // V: MN-major
     const uint64_t dp0 = ptx::smem_desc(ptx::smem_u32(smem + geo.p_off), BM * 16, 128, 0);  // P': MN-major
     const uint64_t da0 = ptx::smem_desc(ptx::smem_u32(smem + geo.a_off), 128, KB * 128, 0); // mix A: K-major
     const uint64_t db0 = ptx::smem_desc(ptx::smem_u32(smem + geo.bm_off), 128, KB * 128, 0);
-    int job = 0, sidx = 0;
     long long w_ring = 0, w_a = 0, w_other = 0;  // timeline: cycles waited (development builds)
     bool ok = true;
     auto wait_u = [&](uint64_t *bar, int parity, int code, long long &acc) {
@@ -232,40 +316,16 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       }
       acc += TL_CLK() - t0;
     };
-    wait_u(bar_q, 0, ERR_TIMEOUT_Q, w_other);
-    ptx::tc_fence_after();
-    auto qk = [&]() {
-      if (sidx >= 1) wait_u(bar_Sfree, (sidx - 1) & 1, ERR_TIMEOUT_S, w_other);
-      ++sidx;
-      if (!ok) return;
+    // ring jobs are consumed in order: wait for a job's data, release its slot
+    auto wait_jobs = [&](int job, uint64_t *full, int nslot) {
+      for (int hh = 0; hh < HJ; ++hh)
+        wait_u(full + ((job + hh) % nslot), ((job + hh) / nslot) & 1, ERR_TIMEOUT_FULL, w_ring);
       ptx::tc_fence_after();
-      for (int h0 = 0; h0 < HPG; h0 += HJ, job += HJ) {
-        for (int hh = 0; hh < HJ; ++hh) wait_u(bar_full + ((job + hh) % NSLOT), ((job + hh) / NSLOT) & 1, ERR_TIMEOUT_FULL, w_ring);
-        if (!ok) return;
-        ptx::tc_fence_after();
-        uint64_t ka[HJ], qa[HJ];
-        uint32_t dd[HJ];
-#pragma unroll
-        for (int hh = 0; hh < HJ; ++hh) {
-          const int h = h0 + hh;
-          ka[hh] = ptx::desc_add(dk0, ((job + hh) % NSLOT) * KJOB);
-          qa[hh] = ptx::desc_add(dq0, h * BM * 256);
-          dd[hh] = tbase + (static_cast<uint32_t>(16 * (h / HH)) << 16) + S_COL + (h % HH) * BM;
-        }
-#pragma unroll
-        for (int ks = 0; ks < D / 16; ++ks)
-#pragma unroll
-          for (int hh = 0; hh < HJ; ++hh)
-            if (ptx::elect_one())
-              ptx::mma_f16_ss(dd[hh], ptx::desc_add(ka[hh], (ks >> 2) * (KJOB / 2) + (ks & 3) * 32),
-                              ptx::desc_add(qa[hh], (ks >> 2) * (BM * 128) + (ks & 3) * 32), idesc_qk, ks > 0);
-        if (ptx::elect_one())
-          for (int hh = 0; hh < HJ; ++hh) ptx::mma_commit(bar_free + ((job + hh) % NSLOT));
-        __syncwarp();
-      }
-      if (ptx::elect_one()) ptx::mma_commit(bar_S);
+    };
+    auto free_jobs = [&](int job, uint64_t *freeb, int nslot) {
+      if (ptx::elect_one())
+        for (int hh = 0; hh < HJ; ++hh) ptx::mma_commit(freeb + ((job + hh) % nslot));
       __syncwarp();
-      if (lane == 0 && sidx <= 6) TL_STAMP(28 + sidx);
     };
     // one round of head mixes (set 0 = pre, 1 = post) for the four sub-groups
     auto mixes = [&](int set, int round) {
@@ -292,62 +352,101 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
           __syncwarp();
         }
     };
-    auto pv = [&](int kt) {
-      wait_u(bar_P, kt & 1, ERR_TIMEOUT_P, w_other);
-      if (!ok) return;
+    if (warp == mma_warp) {
+      wait_u(bar_q, 0, ERR_TIMEOUT_Q, w_other);
       ptx::tc_fence_after();
-      const int nks = (kt == nkt - 1 ? rlast : KT) / 16;
-      for (int h0 = 0; h0 < HPG; h0 += HJ, job += HJ) {
-        for (int hh = 0; hh < HJ; ++hh) wait_u(bar_full + ((job + hh) % NSLOT), ((job + hh) / NSLOT) & 1, ERR_TIMEOUT_FULL, w_ring);
+      int scnt[2] = {0, 0}, sidx = 0;
+      // S^T = K Q^T of one key tile into S buffer buf, K jobs from job0 of
+      // the pass-A (ring_a) or pass-B ring
+      auto qk = [&](int buf, int job0, bool ring_a) {
+        uint64_t *full = ring_a ? bar_afull : bar_kfull, *freeb = ring_a ? bar_afree : bar_kfree;
+        const int nslot = ring_a ? NKA : NSK;
+        if (scnt[buf] >= 1) wait_u(bar_Sfree + buf, (scnt[buf] - 1) & 1, ERR_TIMEOUT_S, w_other);
+        ++scnt[buf];
+        ++sidx;
         if (!ok) return;
         ptx::tc_fence_after();
-        uint64_t va[HJ], pa[HJ];
-        uint32_t dd[HJ];
+        for (int h0 = 0, job = job0; h0 < HPG; h0 += HJ, job += HJ) {
+          wait_jobs(job, full, nslot);
+          if (!ok) return;
+          if (lane == 0 && ring_a) TL_JOB(1, job);
+          uint64_t ka[HJ], qa[HJ];
+          uint32_t dd[HJ];
 #pragma unroll
-        for (int hh = 0; hh < HJ; ++hh) {
-          const int h = h0 + hh;
-          va[hh] = ptx::desc_add(dv0, ((job + hh) % NSLOT) * KJOB);
-          pa[hh] = ptx::desc_add(dp0, h * PHEAD);
-          dd[hh] = tbase + O_COL + h * BM;
-        }
+          for (int hh = 0; hh < HJ; ++hh) {
+            const int h = (h0 + hh + hrot) % HPG;
+            ka[hh] = ptx::desc_add(dsm, kslot_off(ring_a, (job + hh) % nslot));
+            qa[hh] = ptx::desc_add(dq0, h * BM * 256);
+            dd[hh] = tbase + (static_cast<uint32_t>(16 * (h / HH)) << 16) + s_col(buf) + (h % HH) * BM;
+          }
 #pragma unroll
-        for (int ks = 0; ks < KT / 16; ++ks) {
-          if (ks < nks) {
+          for (int ks = 0; ks < D / 16; ++ks)
 #pragma unroll
             for (int hh = 0; hh < HJ; ++hh)
-#pragma unroll
-              for (int c = 0; c < 2; ++c)
-                if (ptx::elect_one())
-                  ptx::mma_f16_ss(dd[hh] + (static_cast<uint32_t>(16 * c) << 16),
-                                  ptx::desc_add(va[hh], c * (KJOB / 2) + ks * 2048),
-                                  ptx::desc_add(pa[hh], ks * (2 * BM * 16)), idesc_pv, (kt > 0 || ks > 0));
-          }
+              if (ptx::elect_one())
+                ptx::mma_f16_ss(dd[hh], ptx::desc_add(ka[hh], (ks >> 2) * (KJOB / 2) + (ks & 3) * 32),
+                                ptx::desc_add(qa[hh], (ks >> 2) * (BM * 128) + (ks & 3) * 32), idesc_qk, ks > 0);
+          free_jobs(job, freeb, nslot);
         }
-        if (ptx::elect_one())
-          for (int hh = 0; hh < HJ; ++hh) ptx::mma_commit(bar_free + ((job + hh) % NSLOT));
+        if (ptx::elect_one()) ptx::mma_commit(bar_S + buf);
+        __syncwarp();
+        if (lane == 0 && sidx <= 6) TL_STAMP(28 + sidx);
+      };
+      // pass A: S tiles alternate between the two buffers; pass B: buffer 0
+      for (int kt = 0; kt < nkt && ok; ++kt) qk(kt & 1, kt * HPG, true);
+      for (int kt = 0; kt < nkt && ok; ++kt) qk(0, kt * HPG, false);
+    } else if (warp == mix_warp) {
+      for (int kt = 0; kt < nkt && ok; ++kt) mixes(0, kt);
+      for (int kt = 0; kt < nkt && ok; ++kt) {
+        mixes(0, nkt + 2 * kt);
+        mixes(1, nkt + 2 * kt + 1);
+      }
+    } else {
+      // O^T += V^T P'^T per key tile of pass B
+      for (int kt = 0; kt < nkt && ok; ++kt) {
+        wait_u(bar_P, kt & 1, ERR_TIMEOUT_P, w_other);
+        if (!ok) break;
+        ptx::tc_fence_after();
+        const int nks = (kt == nkt - 1 ? rlast : KT) / 16;
+        const int job0 = kt * HPG;
+        for (int h0 = 0, job = job0; h0 < HPG; h0 += HJ, job += HJ) {
+          wait_jobs(job, bar_vfull, NSV);
+          if (!ok) break;
+          uint64_t va[HJ], pa[HJ];
+          uint32_t dd[HJ];
+#pragma unroll
+          for (int hh = 0; hh < HJ; ++hh) {
+            const int h = (h0 + hh + hrot) % HPG;
+            va[hh] = ptx::desc_add(dv0, ((job + hh) % NSV) * KJOB);
+            pa[hh] = ptx::desc_add(dp0, h * PHEAD);
+            dd[hh] = tbase + O_COL + h * BM;
+          }
+#pragma unroll
+          for (int ks = 0; ks < KT / 16; ++ks) {
+            if (ks < nks) {
+#pragma unroll
+              for (int hh = 0; hh < HJ; ++hh)
+#pragma unroll
+                for (int c = 0; c < 2; ++c)
+                  if (ptx::elect_one())
+                    ptx::mma_f16_ss(dd[hh] + (static_cast<uint32_t>(16 * c) << 16),
+                                    ptx::desc_add(va[hh], c * (KJOB / 2) + ks * 2048),
+                                    ptx::desc_add(pa[hh], ks * (2 * BM * 16)), idesc_pv, (kt > 0 || ks > 0));
+            }
+          }
+          free_jobs(job, bar_vfree, NSV);
+        }
+        if (ptx::elect_one()) ptx::mma_commit(bar_Pfree);
         __syncwarp();
       }
-      if (ptx::elect_one()) ptx::mma_commit(bar_Pfree);
+      if (ptx::elect_one()) ptx::mma_commit(bar_O);
       __syncwarp();
-    };
-    for (int kt = 0; kt < nkt && ok; ++kt) {
-      qk();
-      mixes(0, kt);
     }
-    if (ok) qk();
-    for (int kt = 0; kt < nkt && ok; ++kt) {
-      mixes(0, nkt + 2 * kt);
-      mixes(1, nkt + 2 * kt + 1);
-      if (kt + 1 < nkt) qk();
-      pv(kt);
-    }
-    if (ptx::elect_one()) ptx::mma_commit(bar_O);
-    __syncwarp();
-    if (lane == 0) {
+    if (lane == 0 && warp == mma_warp) {
       TL_VAL(35, w_ring);
-      TL_VAL(36, w_a);
       TL_VAL(37, w_other);
     }
+    if (lane == 0 && warp == mix_warp) TL_VAL(36, w_a);
   } else {
     // ============================================================ compose warps
     const int qtr = warp & 3, cs = warp >> 2;
@@ -415,13 +514,13 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
     };
 
     // load S (this thread's key, its lane half's heads) for NQG queries
-    auto load_s = [&](int i0, float (&a)[HH][NQG]) {
+    auto load_s = [&](int sbuf, int i0, float (&a)[HH][NQG]) {
 #pragma unroll
-      for (int j = 0; j < HH; ++j) ptx::tmem_ld<NQG>(tl + S_COL + j * BM + i0, a[j]);
+      for (int j = 0; j < HH; ++j) ptx::tmem_ld<NQG>(tl + s_col(sbuf) + j * BM + i0, a[j]);
     };
     // rank-R reductions over all HPG heads (two lane halves) and the mix operand rows
-    auto reduce_and_stage = [&](const TermPtrs &tm, int set, int i0, int64_t tok, bool key_ok,
-                                const float (&a)[HH][NQG], float (&aq)[NQG][R], float (&ak)[NQG][R]) {
+    auto reduce_and_stage = [&](const KeyW<HH, R> &kw, int set, int i0, const float (&a)[HH][NQG],
+                                float (&aq)[NQG][R], float (&ak)[NQG][R]) {
       const float *rb = rec + (set * BM + i0) * recf;
 #pragma unroll
       for (int i = 0; i < NQG; ++i)
@@ -431,21 +530,11 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
 #pragma unroll
           for (int j = 0; j < HH; ++j) sq = fmaf(rb[i * recf + HPG + (HH * u + j) * R + r], a[j][i], sq);
           aq[i][r] = sq;
-          ak[i][r] = 0.f;
+          float sk = 0.f;
+#pragma unroll
+          for (int j = 0; j < HH; ++j) sk = fmaf(unpack_e<E>(kw.w1, j * R + r), a[j][i], sk);
+          ak[i][r] = sk;
         }
-      if (key_ok && tm.kw1) {
-        float w[HH * R];
-        ld_row<E, HH * R>(tm.kw1, (tok * H + hbase + HH * u) * R, w);
-#pragma unroll
-        for (int i = 0; i < NQG; ++i)
-#pragma unroll
-          for (int r = 0; r < R; ++r) {
-            float sk = 0.f;
-#pragma unroll
-            for (int j = 0; j < HH; ++j) sk = fmaf(w[j * R + r], a[j][i], sk);
-            ak[i][r] = sk;
-          }
-      }
 #pragma unroll
       for (int i = 0; i < NQG; ++i)
 #pragma unroll
@@ -468,35 +557,23 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       }
     };
     // composed values x = mix (TMEM D) + diagonal gates * a + rank-R expansions
-    auto finish = [&](const TermPtrs &tm, int set, int i0, int64_t tok, bool key_ok, const float (&dm)[NQG][HH],
+    auto finish = [&](const KeyW<HH, R> &kw, int set, int i0, const float (&dm)[NQG][HH],
                       const float (&a)[HH][NQG], const float (&aq)[NQG][R], const float (&ak)[NQG][R],
                       float (&x)[HH][NQG]) {
       const float *rb = rec + (set * BM + i0) * recf;
-      float kd[HH];
-      if (key_ok && tm.kdd) {
-        ld_row<E, HH>(tm.kdd, tok * H + hbase + HH * u, kd);
-      } else {
 #pragma unroll
-        for (int j = 0; j < HH; ++j) kd[j] = 0.f;
-      }
+      for (int j = 0; j < HH; ++j) {
+        const float kd = unpack_e<E>(kw.dd, j);
+        float k2[R];
 #pragma unroll
-      for (int i = 0; i < NQG; ++i)
+        for (int r = 0; r < R; ++r) k2[r] = unpack_e<E>(kw.w2, r * HH + j);
 #pragma unroll
-        for (int j = 0; j < HH; ++j) {
-          float xv = fmaf(rb[i * recf + HH * u + j] + kd[j], a[j][i], dm[i][j]);
+        for (int i = 0; i < NQG; ++i) {
+          float xv = fmaf(rb[i * recf + HH * u + j] + kd, a[j][i], dm[i][j]);
 #pragma unroll
-          for (int r = 0; r < R; ++r) xv = fmaf(rb[i * recf + HPG + HPG * R + r * HPG + HH * u + j], aq[i][r], xv);
+          for (int r = 0; r < R; ++r)
+            xv = fmaf(rb[i * recf + HPG + HPG * R + r * HPG + HH * u + j], aq[i][r], fmaf(k2[r], ak[i][r], xv));
           x[j][i] = xv;
-        }
-      if (key_ok && tm.kw1) {
-#pragma unroll
-        for (int r = 0; r < R; ++r) {
-          float k2[HH];
-          ld_row<E, HH>(tm.kw2, (tok * R + r) * H + hbase + HH * u, k2);
-#pragma unroll
-          for (int i = 0; i < NQG; ++i)
-#pragma unroll
-            for (int j = 0; j < HH; ++j) x[j][i] = fmaf(k2[j], ak[i][r], x[j][i]);
         }
       }
     };
@@ -505,6 +582,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       for (int i = 0; i < NQG; ++i) ptx::tmem_ld<HH>(tl + D_COL + (i0 + i) * HH, dm[i]);
     };
 
+    int scnt[2] = {0, 0};  // uses of each S buffer so far (barrier phases)
     float m_run[NSG][2], l_run[NSG][2];
 #pragma unroll
     for (int k = 0; k < NSG; ++k) { m_run[k][0] = m_run[k][1] = -INFINITY; l_run[k][0] = l_run[k][1] = 0.f; }
@@ -516,7 +594,10 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       const int s = k_lo + kt * KT + key_local;
       const bool key_ok = s < slen;
       const int64_t tok = (int64_t)b * T + s;
-      wait_or_fail(bar_S, kt & 1, ERR_TIMEOUT_S);
+      KeyW<HH, R> kwp;
+      load_keyw<E, HH, R>(kwp, p.pre, tok, H, hbase + HH * u, key_ok);
+      const int sbuf = kt & 1;
+      wait_or_fail(bar_S + sbuf, scnt[sbuf] & 1, ERR_TIMEOUT_S);
       ptx::tc_fence_after();
       if (tlw && kt < 3) TL_STAMP(1 + 4 * kt);
       float aq[NSG][NQG][R], ak[NSG][NQG][R];
@@ -524,9 +605,9 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       for (int sgl = 0; sgl < NSG; ++sgl) {
         const int i0 = (cs * NSG + sgl) * NQG;
         float a[HH][NQG];
-        load_s(i0, a);
+        load_s(sbuf, i0, a);
         ptx::tmem_wait_ld();
-        reduce_and_stage(p.pre, 0, i0, tok, key_ok, a, aq[sgl], ak[sgl]);
+        reduce_and_stage(kwp, 0, i0, a, aq[sgl], ak[sgl]);
         arrive(bar_A + cs * NSG + sgl);
       }
       if (tlw && kt < 3) TL_STAMP(2 + 4 * kt);
@@ -537,9 +618,9 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
         ptx::tc_fence_after();
         float dm[NQG][HH], a[HH][NQG], x[HH][NQG];
         load_d(i0, dm);
-        load_s(i0, a);
+        load_s(sbuf, i0, a);
         ptx::tmem_wait_ld();
-        finish(p.pre, 0, i0, tok, key_ok, dm, a, aq[sgl], ak[sgl], x);
+        finish(kwp, 0, i0, dm, a, aq[sgl], ak[sgl], x);
         // masked max / exp / transposed sum over the 16 keys of this lane half
         float e[32], mt[2] = {-INFINITY, -INFINITY};
 #pragma unroll
@@ -574,7 +655,8 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       if (tlw && kt < 3) TL_STAMP(3 + 4 * kt);
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_Sfree);
+      if (lane == 0) ptx::mbar_arrive(bar_Sfree + sbuf);
+      ++scnt[sbuf];
     }
     // ---- combine the lane quarters
 #pragma unroll
@@ -607,7 +689,10 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       const bool key_ok = s < slen;
       const int64_t tok = (int64_t)b * T + s;
       const int rpre = nkt + 2 * kt, rpost = rpre + 1;
-      wait_or_fail(bar_S, (nkt + kt) & 1, ERR_TIMEOUT_S);
+      KeyW<HH, R> kwp, kwq;
+      load_keyw<E, HH, R>(kwp, p.pre, tok, H, hbase + HH * u, key_ok);
+      const int sbuf = 0;
+      wait_or_fail(bar_S + sbuf, scnt[sbuf] & 1, ERR_TIMEOUT_S);
       ptx::tc_fence_after();
       if (tlw && kt < 3) TL_STAMP(13 + 5 * kt);
       float aq[NSG][NQG][R], ak[NSG][NQG][R];
@@ -615,12 +700,13 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       for (int sgl = 0; sgl < NSG; ++sgl) {
         const int i0 = (cs * NSG + sgl) * NQG;
         float a[HH][NQG];
-        load_s(i0, a);
+        load_s(sbuf, i0, a);
         ptx::tmem_wait_ld();
-        reduce_and_stage(p.pre, 0, i0, tok, key_ok, a, aq[sgl], ak[sgl]);
+        reduce_and_stage(kwp, 0, i0, a, aq[sgl], ak[sgl]);
         arrive(bar_A + cs * NSG + sgl);
       }
       if (tlw && kt < 3) TL_STAMP(14 + 5 * kt);
+      load_keyw<E, HH, R>(kwq, p.post, tok, H, hbase + HH * u, key_ok);
       float pr[NSG][HH][NQG], pq[NSG][NQG][R], pk[NSG][NQG][R];
 #pragma unroll
       for (int sgl = 0; sgl < NSG; ++sgl) {
@@ -629,9 +715,9 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
         ptx::tc_fence_after();
         float dm[NQG][HH], a[HH][NQG], x[HH][NQG];
         load_d(i0, dm);
-        load_s(i0, a);
+        load_s(sbuf, i0, a);
         ptx::tmem_wait_ld();
-        finish(p.pre, 0, i0, tok, key_ok, dm, a, aq[sgl], ak[sgl], x);
+        finish(kwp, 0, i0, dm, a, aq[sgl], ak[sgl], x);
 #pragma unroll
         for (int j = 0; j < HH; ++j)
 #pragma unroll
@@ -640,13 +726,14 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
             pr[sgl][j][i] = (key_ok && valid(s, q0 + i0 + i)) ? exp2f(fmaf(x[j][i], sl2e, -mval[col])) * linv[col]
                                                              : 0.f;
           }
-        reduce_and_stage(p.post, 1, i0, tok, key_ok, pr[sgl], pq[sgl], pk[sgl]);
+        reduce_and_stage(kwq, 1, i0, pr[sgl], pq[sgl], pk[sgl]);
         arrive(bar_A + sg);
       }
       if (tlw && kt < 3) TL_STAMP(15 + 5 * kt);
       ptx::tc_fence_before();
       __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_Sfree);
+      if (lane == 0) ptx::mbar_arrive(bar_Sfree + sbuf);
+      ++scnt[sbuf];
       if (kt >= 1) wait_or_fail(bar_Pfree, (kt - 1) & 1, ERR_TIMEOUT_P);
       if (tlw && kt < 3) TL_STAMP(16 + 5 * kt);
 #pragma unroll
@@ -657,7 +744,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
         float dm[NQG][HH], x[HH][NQG];
         load_d(i0, dm);
         ptx::tmem_wait_ld();
-        finish(p.post, 1, i0, tok, key_ok, dm, pr[sgl], pq[sgl], pk[sgl], x);
+        finish(kwq, 1, i0, dm, pr[sgl], pq[sgl], pk[sgl], x);
         unsigned char *prow = ptile + (key_local & 7) * 16 + (key_local >> 3) * (BM * 16);
 #pragma unroll
         for (int j = 0; j < HH; ++j)
@@ -715,10 +802,12 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   const GeoM geo = make_geo_m<HPG, R>();
   const size_t smem = geo.total + 1024;
   const int64_t sb = (int64_t)p.T * p.H * D, st_ = (int64_t)p.H * D, sh = D;
-  CUtensorMap mq, mk, mv, mo;
+  CUtensorMap mq, mk, mv, mk16, mv16, mo;
   if (!make_map(&mq, p.q, p.dtype, p.B, p.T, p.H, SH::BM, sb, st_, sh, true) ||
       !make_map(&mk, p.k, p.dtype, p.B, p.T, p.H, KT, sb, st_, sh, true) ||
       !make_map(&mv, p.v, p.dtype, p.B, p.T, p.H, KT, sb, st_, sh, true) ||
+      !make_map(&mk16, p.k, p.dtype, p.B, p.T, p.H, 16, sb, st_, sh, true) ||
+      !make_map(&mv16, p.v, p.dtype, p.B, p.T, p.H, 16, sb, st_, sh, true) ||
       !make_map(&mo, p.out, p.dtype, p.B, p.T, p.H, SH::BM, p.out_sb, p.out_st, p.out_sh, false))
     return cudaErrorInvalidValue;
   TcParams tp;
@@ -734,7 +823,7 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((p.T + SH::BM - 1) / SH::BM, p.B * p.G);
-  kern<<<grid, 32 * (NCW + 2), smem, st>>>(mq, mk, mv, mo, tp);
+  kern<<<grid, 32 * (NCW + 4), smem, st>>>(mq, mk, mv, mk16, mv16, mo, tp);
   return cudaGetLastError();
 }
 
