@@ -242,6 +242,26 @@ static bool make_map(CUtensorMap *m, const void *base, int dtype, int B, int T, 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The same [B, T, H, D] tensor as a 5-D map (64 d, T, d half, H, B) whose box
+// (64 x rows x 2 x heads x 1) lands in shared memory as [head][d half][rows][64 d]:
+// one TMA operation fills both 128-byte-swizzled d halves of `heads` heads.
+// (One thread's TMA operations are processed one after another; fewer, larger
+// boxes and several issuing lanes are what raise the per-SM load rate.)
+static bool make_map5(CUtensorMap *m, const void *base, int dtype, int B, int T, int H, int rows, int heads,
+                      int64_t sb, int64_t st, int64_t sh) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[5] = {64, (cuuint64_t)T, 2, (cuuint64_t)H, (cuuint64_t)B};
+  const cuuint64_t strides[4] = {(cuuint64_t)st * 2, 128, (cuuint64_t)sh * 2, (cuuint64_t)sb * 2};
+  const cuuint32_t box[5] = {64, (cuuint32_t)rows, 2, (cuuint32_t)heads, 1};
+  const cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  const CUtensorMapDataType dt =
+      dtype == DC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(m, dt, 5, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) ==
+         CUDA_SUCCESS;
+}
+
 // key span of a query block: BM + window - 1 keys
 static int num_key_tiles(int HPG, int window) {
   const int BM = NQ / HPG;

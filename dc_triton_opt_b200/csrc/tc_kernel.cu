@@ -616,55 +616,64 @@ __global__ void __launch_bounds__(32 * NW, 1)
 
   if (role == ROLE_TMA) {
     // ================================================= TMA producer
+    // The warp runs the job loop together and each lane issues one box of a
+    // job: a single thread issuing TMA one instruction at a time caps at about
+    // 20 B/clk per SM, several lanes per instruction do not.
     if (lane == 0) {
       ptx::tma_prefetch_desc(&tm_q);
       ptx::tma_prefetch_desc(&tm_k);
       ptx::tma_prefetch_desc(&tm_v);
-      int job = 0;
-      bool ok = true;
-      auto load_kv = [&](bool isv, int q0, int b, int g, int jj) {
-        const int slot = job % nslot, use = job / nslot;
-        if (use > 0 && !ptx::mbar_wait(bar_free + slot, (use - 1) & 1, WAIT)) {
-          ok = false;
-          record_err(p, ERR_TIMEOUT_FREE);
-          return;
-        }
-        const Job jb = job_of(jj);
-        const bool last = jb.kt == nkt - 1;
-        const CUtensorMap *m = isv ? (last ? &tm_vl : &tm_v) : (last ? &tm_kl : &tm_k);
-        const int kb = q0 - p.window + 1;
-        ptx::mbar_expect_tx(bar_full + slot, jb.nh * jb.rows * 256);
-        unsigned char *dst = smem + geo.ring_off + slot * TILE_BYTES;
-        for (int u = 0; u < jb.nh; ++u)
-          for (int c = 0; c < 2; ++c)
-            ptx::tma_load_4d(dst + u * 2 * jb.half + c * jb.half, m, bar_full + slot, c * 64, g * HPG + jb.h0 + u,
-                             kb + jb.kt * KT_ROWS, b);
-        ++job;
-      };
-      int pq0 = 0, pb = 0, pg = 0;
-      int it = 0;
-      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
-        int q0, b, g;
-        tile_coords(tile, q0, b, g);
-        const int buf = it & 1;
-        if (it >= 2 && !ptx::mbar_wait(bar_Qfree + buf, ((it - 2) >> 1) & 1, WAIT)) {
-          record_err(p, ERR_TIMEOUT_Q);
-          break;
-        }
-        ptx::mbar_expect_tx(bar_q + buf, NQ * 256);
-        for (int h = 0; h < HPG; ++h)
-          for (int c = 0; c < 2; ++c)
-            ptx::tma_load_4d(smem + geo.q_off + buf * NQ * 256 + h * BM * 256 + c * BM * 128, &tm_q, bar_q + buf,
-                             c * 64, g * HPG + h, q0, b);
-        for (int jj = 0; jj < nK && ok; ++jj) load_kv(false, q0, b, g, jj);
-        if (it >= 1)
-          for (int jj = 0; jj < nK && ok; ++jj) load_kv(true, pq0, pb, pg, jj);
-        pq0 = q0; pb = b; pg = g;
+    }
+    int job = 0;
+    bool ok = true;
+    auto wait_all = [&](uint64_t *bar, int parity, int code) {
+      const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait(bar, parity, WAIT));
+      if (ok && !got) {
+        ok = false;
+        if (lane == 0) record_err(p, code);
       }
+      return ok;
+    };
+    auto load_kv = [&](bool isv, int q0, int b, int g, int jj) {
+      const int slot = job % nslot, use = job / nslot;
+      if (use > 0 && !wait_all(bar_free + slot, (use - 1) & 1, ERR_TIMEOUT_FREE)) return;
+      const Job jb = job_of(jj);
+      const bool last = jb.kt == nkt - 1;
+      const CUtensorMap *m = isv ? (last ? &tm_vl : &tm_v) : (last ? &tm_kl : &tm_k);
+      const int kb = q0 - p.window + 1;
+      if (lane == 0) ptx::mbar_expect_tx(bar_full + slot, jb.nh * jb.rows * 256);
+      __syncwarp();
+      unsigned char *dst = smem + geo.ring_off + slot * TILE_BYTES;
+      if (lane < 2 * jb.nh) {
+        const int u = lane >> 1, c = lane & 1;
+        ptx::tma_load_4d(dst + u * 2 * jb.half + c * jb.half, m, bar_full + slot, c * 64, g * HPG + jb.h0 + u,
+                         kb + jb.kt * KT_ROWS, b);
+      }
+      __syncwarp();
+      ++job;
+    };
+    int pq0 = 0, pb = 0, pg = 0;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, ++it) {
+      int q0, b, g;
+      tile_coords(tile, q0, b, g);
+      const int buf = it & 1;
+      if (it >= 2 && !wait_all(bar_Qfree + buf, ((it - 2) >> 1) & 1, ERR_TIMEOUT_Q)) break;
+      if (lane == 0) ptx::mbar_expect_tx(bar_q + buf, NQ * 256);
+      __syncwarp();
+      if (lane < 2 * HPG) {
+        const int h = lane >> 1, c = lane & 1;
+        ptx::tma_load_4d(smem + geo.q_off + buf * NQ * 256 + h * BM * 256 + c * BM * 128, &tm_q, bar_q + buf,
+                         c * 64, g * HPG + h, q0, b);
+      }
+      __syncwarp();
+      for (int jj = 0; jj < nK && ok; ++jj) load_kv(false, q0, b, g, jj);
       if (it >= 1)
         for (int jj = 0; jj < nK && ok; ++jj) load_kv(true, pq0, pb, pg, jj);
+      pq0 = q0; pb = b; pg = g;
     }
-    __syncwarp();
+    if (it >= 1)
+      for (int jj = 0; jj < nK && ok; ++jj) load_kv(true, pq0, pb, pg, jj);
   } else if (role == ROLE_MMA) {
     // ================================================= MMA issuer
     // Whole warp runs the loops; one elected lane issues each tcgen05 op, with

@@ -39,23 +39,21 @@ using namespace tc;
 constexpr int KT = 64;             // keys per tile
 constexpr int KJOB = KT * 256;     // one ring job: one head, 64 keys x 128 d
 constexpr int NCW = 8;             // compose warps (2 per lane quarter)
-#ifndef TCM_NSK
-#define TCM_NSK 3
-#endif
-#ifndef TCM_NSV
-#define TCM_NSV 2
-#endif
-// Separate K and V rings (16 KB slots), each with one producer warp and one
-// MMA warp consuming it in order: an mbarrier parity wait is only unambiguous
-// for a consumer at most one phase behind, so a ring never has two consumers.
-constexpr int NSK = TCM_NSK, NSV = TCM_NSV;
-// Pass A streams K alone and P' is idle until pass B, so the pass-A K ring
-// also uses the P' buffer as two more slots.
-constexpr int NKA = NSK + 2;
+// K/V staging.  The K, V and P' buffers share one shared-memory pool; a K job
+// carries one head's 64-key K tile plus that head's Q rows (the QK^T B
+// operand), so no Q copy stays resident.  Separate K and V rings, each with
+// one producer lane and one MMA warp consuming it in order (an mbarrier parity
+// wait is only unambiguous for a consumer at most one phase behind, so a ring
+// never has two consumers).  Pass A streams K alone, so its ring spans the
+// whole pool; pass B has NSK K slots, NSV V slots and P'.
+constexpr int NSK = 5, NSV = 3;
+constexpr int NLK = 4, NLV = 3;  // issuing lanes of the K and V producers (<= slots)
+static_assert(NLK <= NSK && NLV <= NSV, "a producer round may not wrap its ring");
 // Heads whose MMAs are interleaved: the K steps of one head accumulate into one
 // TMEM tile and serialise, so independent heads are issued K step by K step.
 constexpr int HJ = 1;
 static_assert(NSK >= HJ && NSV >= HJ, "an interleaved group needs its jobs resident");
+constexpr int NKA_MAX = 10;
 constexpr uint32_t S_COL = 0, D_COL = 128, O_COL = 256;
 // Pass A double-buffers S in the O columns (idle until pass B): S tile n of
 // pass A uses buffer n & 1; pass B uses buffer 0 only.
@@ -71,27 +69,31 @@ struct Shape {
   static constexpr int ATILE = KT * HPG * 2;  // bytes of one query's mix operand
   static constexpr int PHEAD = KT * BM * 2;   // bytes of one head's P' tile
   static constexpr int NCOL = HPG * BM;       // (head, query) columns
+  static constexpr int KQJOB = KJOB + BM * 256;              // K tile + Q rows of one head
+  static constexpr int VOFF = NSK * KQJOB;                   // V ring in the pool
+  static constexpr int POFF = VOFF + NSV * KJOB;             // P' in the pool
+  static constexpr int POOL = POFF + HPG * PHEAD;
+  static constexpr int NKA = POOL / KQJOB;                   // pass-A K slots
+  static_assert(KQJOB % 1024 == 0 && VOFF % 1024 == 0 && POFF % 1024 == 0, "128B-swizzle atoms");
+  static_assert(NKA <= NKA_MAX, "barrier space");
 };
 
 struct GeoM {
-  int q_off, kring_off, vring_off, a_off, p_off, bm_off, rec_off, stat_off, bar_off, tmem_off, total, recf;
+  int p_off, a_off, bm_off, rec_off, stat_off, bar_off, tmem_off, total, recf;
 };
 
 template <int HPG, int R>
 __host__ __device__ inline GeoM make_geo_m() {
   using SH = Shape<HPG>;
   GeoM g{};
-  g.q_off = 0;                                  // Q: HPG x BM x 256 B (64 KB); output staging at the end
-  g.kring_off = HPG * SH::BM * 256;
-  g.vring_off = g.kring_off + NSK * KJOB;
-  g.a_off = g.vring_off + NSV * KJOB;           // mix operands, BM x 64 keys x HPG fp16 (32 KB)
-  g.p_off = g.a_off + SH::BM * SH::ATILE;       // P': HPG x 64 keys x BM (32 KB); pass-A stats exchange
-  g.bm_off = g.p_off + HPG * SH::PHEAD;         // mix B operands: 2 sets x HPG x HPG fp16
+  g.p_off = SH::POFF;                           // P': HPG x 64 keys x BM (32 KB); pass-A stats exchange
+  g.a_off = SH::POOL;                           // mix operands, BM x 64 keys x HPG fp16 (32 KB)
+  g.bm_off = g.a_off + SH::BM * SH::ATILE;      // mix B operands: 2 sets x HPG x HPG fp16
   int o = g.bm_off + 2 * HPG * HPG * 2;
   g.recf = round_up(HPG * (2 * R + 1), 4);
   g.rec_off = round_up(o, 16); o = g.rec_off + 2 * SH::BM * g.recf * 4;
   g.stat_off = o; o += 2 * SH::NCOL * 4;
-  g.bar_off = round_up(o, 8); o = g.bar_off + (2 * (NKA + NSK + NSV) + 16) * 8;
+  g.bar_off = round_up(o, 8); o = g.bar_off + (2 * (NKA_MAX + NSK + NSV) + 16) * 8;
   g.tmem_off = o; o += 16;
   g.total = o;
   return g;
@@ -146,8 +148,7 @@ __device__ __forceinline__ uint32_t pack_e2(float lo, float hi) {
 template <typename E, int HPG, int R>
 __global__ void __launch_bounds__(32 * (NCW + 4), 1)
     dc_tcm_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
-                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_k16,
-                  const __grid_constant__ CUtensorMap tm_v16, const __grid_constant__ CUtensorMap tm_o,
+                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                   const TcParams p) {
   using SH = Shape<HPG>;
   constexpr int BM = SH::BM, HH = SH::HH, NQG = SH::NQG, NSG = SH::NSG, KB = SH::KB;
@@ -163,9 +164,12 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
   float *redm = reinterpret_cast<float *>(smem + geo.p_off), *reds = redm + 4 * NCOL;
   float *mval = reinterpret_cast<float *>(smem + geo.stat_off), *linv = mval + NCOL;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + geo.bar_off);
+  constexpr int NKA = SH::NKA, KQJOB = SH::KQJOB;
   uint64_t *bar_afull = bars + 0, *bar_afree = bar_afull + NKA;        // pass-A K ring
   uint64_t *bar_kfull = bar_afree + NKA, *bar_kfree = bar_kfull + NSK;  // pass-B K ring
-  uint64_t *bar_vfull = bar_kfree + NSK, *bar_vfree = bar_vfull + NSV, *bar_q = bar_vfree + NSV;
+  // bar_vgo: the pass-A ring is drained, the V ring may start (one phase)
+  uint64_t *bar_vfull = bar_kfree + NSK, *bar_vfree = bar_vfull + NSV, *bar_vgo = bar_vfree + NSV;
+  uint64_t *bar_q = bar_vgo;  // base of the remaining barriers
   uint64_t *bar_S = bar_q + 1, *bar_Sfree = bar_q + 3;  // two S buffers each
   uint64_t *bar_P = bar_q + 5, *bar_Pfree = bar_q + 6, *bar_O = bar_q + 7;
   uint64_t *bar_A = bar_q + 8, *bar_D = bar_q + 12;  // per compose sub-group (4 each)
@@ -178,9 +182,8 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
   // K/V rows at any moment instead of hitting the same lines.
   const int hrot = (blockIdx.x * 7) % HPG;
   // byte offset of K slot `slot` of the pass-A (ring_a) or pass-B ring
-  auto kslot_off = [&](bool ring_a, int slot) {
-    return ring_a && slot >= NSK ? geo.p_off + (slot - NSK) * KJOB : geo.kring_off + slot * KJOB;
-  };
+  // (both K rings start at the pool base with the same slot size)
+  auto kslot_off = [&](bool, int slot) { return slot * KQJOB; };
   const int nqb = (p.T + BM - 1) / BM;
   const int qb = nqb - 1 - static_cast<int>(blockIdx.x);  // longest spans first
   const int b = blockIdx.y / p.G, g = blockIdx.y % p.G;
@@ -205,7 +208,7 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
       ptx::mbar_init(bar_vfull + i, 1);
       ptx::mbar_init(bar_vfree + i, 1);
     }
-    ptx::mbar_init(bar_q, 1);
+    ptx::mbar_init(bar_vgo, 1);
     for (int i = 0; i < 2; ++i) {
       ptx::mbar_init(bar_S + i, 1);
       ptx::mbar_init(bar_Sfree + i, NCW);
@@ -227,64 +230,81 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
 
   if (warp == tma_warp) {
     // ============================================================ TMA producers
-    // Lane 0 fills the K ring: pass A K(0..nkt-1), then pass B K(0..nkt-1);
-    // lane 1 the V ring: V(0..nkt-1).  The last key tile loads only the rows
-    // the span needs (16-row boxes); the MMAs never read past them except for
-    // masked keys.
-    if (lane < 2) {
-      const bool isv = lane == 1;
-      if (!isv) {
-        ptx::tma_prefetch_desc(&tm_q);
-        ptx::tma_prefetch_desc(&tm_k);
-        ptx::mbar_expect_tx(bar_q, HPG * BM * 256);
-        for (int h = 0; h < HPG; ++h)
-          for (int c = 0; c < 2; ++c)
-            ptx::tma_load_4d(smem + geo.q_off + h * BM * 256 + c * BM * 128, &tm_q, bar_q, c * 64, hbase + h, q0,
-                             b);
-      } else {
-        ptx::tma_prefetch_desc(&tm_v);
+    // Lanes 0-3 fill the K ring (pass A K(0..nkt-1), then pass B K(0..nkt-1)),
+    // lanes 16-18 the V ring (V(0..nkt-1)).  A job is one head: a single 5-D
+    // box for K (both d halves) plus one for that head's Q rows, or one box
+    // for V.  A thread's TMA operations are processed one after another, so
+    // consecutive jobs go to different lanes; the lanes of a group advance
+    // together, one job each per round, and a group never has more lanes
+    // than its ring has slots, so the job a slot waits for was issued in an
+    // earlier round.
+    const bool isv = lane >= 16;
+    const int gl = lane & 15;
+    const int L = isv ? NLV : NLK;
+    const uint32_t gmask = isv ? (((1u << NLV) - 1) << 16) : ((1u << NLK) - 1);
+    if (gl < L) {
+      if (gl == 0) {
+        if (!isv) {
+          ptx::tma_prefetch_desc(&tm_q);
+          ptx::tma_prefetch_desc(&tm_k);
+        } else {
+          ptx::tma_prefetch_desc(&tm_v);
+        }
       }
       bool ok = true;
-      // one key tile (all heads) into a ring; job counts that ring's jobs
-      auto load_tile = [&](int kt, int &job, uint64_t *full, uint64_t *freeb, int nslot, bool ring_a) {
-        const int rows = kt == nkt - 1 ? rlast : KT;
-        const CUtensorMap *m = isv ? (rows == KT ? &tm_v : &tm_v16) : (rows == KT ? &tm_k : &tm_k16);
-        const int nbox = rows == KT ? 1 : rows / 16;
-        for (int hi = 0; hi < HPG && ok; ++hi, ++job) {
-          const int h = (hi + hrot) % HPG;
-          const int slot = job % nslot, use = job / nslot;
-          if (use > 0 && !ptx::mbar_wait(freeb + slot, (use - 1) & 1, WAIT)) {
-            ok = false;
-            record_err(p, ERR_TIMEOUT_FREE);
-            return;
+      // jobs [0, njobs) of one ring; job i = head i % HPG of key tile i / HPG
+      auto run_ring = [&](int njobs, uint64_t *full, uint64_t *freeb, int nslot, bool ring_a) {
+        for (int j0 = 0; j0 < njobs; j0 += L) {
+          const int job = j0 + gl;
+          bool good = ok;
+          if (job < njobs && good) {
+            const int kt = job / HPG, h = (job % HPG + hrot) % HPG;
+            const int slot = job % nslot, use = job / nslot;
+            if (use > 0 && !ptx::mbar_wait(freeb + slot, (use - 1) & 1, WAIT)) good = false;
+            if (good) {
+              ptx::mbar_expect_tx(full + slot, KJOB + (isv ? 0 : BM * 256));
+              if (!isv && ring_a) TL_JOB(0, job);
+              unsigned char *dst = smem + (isv ? SH::VOFF + slot * KJOB : kslot_off(ring_a, slot));
+              ptx::tma_load_5d(dst, isv ? &tm_v : &tm_k, full + slot, 0, k_lo + kt * KT, 0, hbase + h, b);
+              if (!isv) ptx::tma_load_5d(dst + KJOB, &tm_q, full + slot, 0, q0, 0, hbase + h, b);
+            }
           }
-          ptx::mbar_expect_tx(full + slot, rows * 256);
-          if (!isv && ring_a) TL_JOB(0, job);
-          unsigned char *dst = smem + (isv ? geo.vring_off + slot * KJOB : kslot_off(ring_a, slot));
-          for (int x = 0; x < nbox; ++x)
-            for (int c = 0; c < 2; ++c)
-              ptx::tma_load_4d(dst + c * (KJOB / 2) + x * 2048, m, full + slot, c * 64, hbase + h,
-                               k_lo + kt * KT + x * 16, b);
+          const bool all = __all_sync(gmask, good);
+          if (ok && !all) {
+            ok = false;
+            if (gl == 0) record_err(p, ERR_TIMEOUT_FREE);
+          }
         }
       };
       if (isv) {
-        int job = 0;
-        for (int kt = 0; kt < nkt; ++kt) load_tile(kt, job, bar_vfull, bar_vfree, NSV, false);
+        // the V ring overlaps pass-A slots: start once the K group has seen
+        // them drained (a one-phase barrier, so the wait is unambiguous)
+        const bool got = __all_sync(gmask, ptx::mbar_wait(bar_vgo, 0, WAIT));
+        if (!got) {
+          ok = false;
+          if (gl == 0) record_err(p, ERR_TIMEOUT_FREE);
+        }
+        if (ok) run_ring(nkt * HPG, bar_vfull, bar_vfree, NSV, false);
       } else {
-        int job = 0;
-        for (int kt = 0; kt < nkt; ++kt) load_tile(kt, job, bar_afull, bar_afree, NKA, true);
-        // the pass-B ring reuses the K slots: wait for their last pass-A use
-        const int na = job;
-        for (int sl = 0; sl < NSK && ok; ++sl)
+        const int na = nkt * HPG;
+        run_ring(na, bar_afull, bar_afree, NKA, true);
+        // The pass-B K slots and the V ring overlap pass-A slots: wait for the
+        // last use of every pass-A slot.  Every job of the ring has been issued
+        // (rounds are lockstep) and each issue waited for the slot's previous
+        // release, so the last phase cannot be more than one ahead: its
+        // parity is unambiguous.
+        for (int sl = gl; sl < NKA && ok; sl += L)
           if (sl < na) {
             const int j = sl + ((na - 1 - sl) / NKA) * NKA;
-            if (!ptx::mbar_wait(bar_afree + sl, (j / NKA) & 1, WAIT)) {
-              ok = false;
-              record_err(p, ERR_TIMEOUT_FREE);
-            }
+            if (!ptx::mbar_wait(bar_afree + sl, (j / NKA) & 1, WAIT)) ok = false;
           }
-        job = 0;
-        for (int kt = 0; kt < nkt; ++kt) load_tile(kt, job, bar_kfull, bar_kfree, NSK, false);
+        const bool all = __all_sync(gmask, ok);
+        if (!all) {
+          ok = false;
+          if (gl == 0) record_err(p, ERR_TIMEOUT_FREE);
+        }
+        if (gl == 0) ptx::mbar_arrive(bar_vgo);
+        if (ok) run_ring(na, bar_kfull, bar_kfree, NSK, false);
       }
     }
     __syncwarp();
@@ -299,9 +319,8 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
     const uint32_t idesc_qk = ptx::idesc_f16(ab_fmt, 0, 0, 64, BM);
     const uint32_t idesc_pv = ptx::idesc_f16(ab_fmt, 1, 1, 64, BM);
     const uint32_t idesc_mix = ptx::idesc_f16(0, 0, 0, 64, HH);  // fp16 x fp16
-    const uint64_t dq0 = ptx::smem_desc(ptx::smem_u32(smem + geo.q_off), 16, 1024, 2);      // Q: K-major SW128
     const uint64_t dsm = ptx::smem_desc(ptx::smem_u32(smem), 16, 1024, 2);  // K: K-major SW128, + slot offset
-    const uint64_t dv0 = ptx::smem_desc(ptx::smem_u32(smem + geo.vring_off), KJOB / 2, 1024, 2);  // V: MN-major
+    const uint64_t dv0 = ptx::smem_desc(ptx::smem_u32(smem + SH::VOFF), KJOB / 2, 1024, 2);  // V: MN-major
     const uint64_t dp0 = ptx::smem_desc(ptx::smem_u32(smem + geo.p_off), BM * 16, 128, 0);  // P': MN-major
     const uint64_t da0 = ptx::smem_desc(ptx::smem_u32(smem + geo.a_off), 128, KB * 128, 0); // mix A: K-major
     const uint64_t db0 = ptx::smem_desc(ptx::smem_u32(smem + geo.bm_off), 128, KB * 128, 0);
@@ -353,8 +372,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
         }
     };
     if (warp == mma_warp) {
-      wait_u(bar_q, 0, ERR_TIMEOUT_Q, w_other);
-      ptx::tc_fence_after();
       int scnt[2] = {0, 0}, sidx = 0;
       // S^T = K Q^T of one key tile into S buffer buf, K jobs from job0 of
       // the pass-A (ring_a) or pass-B ring
@@ -376,7 +393,7 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
           for (int hh = 0; hh < HJ; ++hh) {
             const int h = (h0 + hh + hrot) % HPG;
             ka[hh] = ptx::desc_add(dsm, kslot_off(ring_a, (job + hh) % nslot));
-            qa[hh] = ptx::desc_add(dq0, h * BM * 256);
+            qa[hh] = ptx::desc_add(ka[hh], KJOB);  // Q rows of head h follow its K tile
             dd[hh] = tbase + (static_cast<uint32_t>(16 * (h / HH)) << 16) + s_col(buf) + (h % HH) * BM;
           }
 #pragma unroll
@@ -762,7 +779,7 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
     // ============================== epilogue: O^T -> SMEM [head][d half][query][64 d] -> TMA store
     wait_or_fail(bar_O, 0, ERR_TIMEOUT_O);
     ptx::tc_fence_after();
-    unsigned char *stage = smem + geo.q_off;
+    unsigned char *stage = smem;  // pool base: every MMA has completed
     const int d = 64 * u + 16 * qtr + r16;
     if (ok) {
 #pragma unroll 1
@@ -802,12 +819,10 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   const GeoM geo = make_geo_m<HPG, R>();
   const size_t smem = geo.total + 1024;
   const int64_t sb = (int64_t)p.T * p.H * D, st_ = (int64_t)p.H * D, sh = D;
-  CUtensorMap mq, mk, mv, mk16, mv16, mo;
-  if (!make_map(&mq, p.q, p.dtype, p.B, p.T, p.H, SH::BM, sb, st_, sh, true) ||
-      !make_map(&mk, p.k, p.dtype, p.B, p.T, p.H, KT, sb, st_, sh, true) ||
-      !make_map(&mv, p.v, p.dtype, p.B, p.T, p.H, KT, sb, st_, sh, true) ||
-      !make_map(&mk16, p.k, p.dtype, p.B, p.T, p.H, 16, sb, st_, sh, true) ||
-      !make_map(&mv16, p.v, p.dtype, p.B, p.T, p.H, 16, sb, st_, sh, true) ||
+  CUtensorMap mq, mk, mv, mo;
+  if (!make_map5(&mq, p.q, p.dtype, p.B, p.T, p.H, SH::BM, 1, sb, st_, sh) ||
+      !make_map5(&mk, p.k, p.dtype, p.B, p.T, p.H, KT, 1, sb, st_, sh) ||
+      !make_map5(&mv, p.v, p.dtype, p.B, p.T, p.H, KT, 1, sb, st_, sh) ||
       !make_map(&mo, p.out, p.dtype, p.B, p.T, p.H, SH::BM, p.out_sb, p.out_st, p.out_sh, false))
     return cudaErrorInvalidValue;
   TcParams tp;
@@ -823,7 +838,7 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((p.T + SH::BM - 1) / SH::BM, p.B * p.G);
-  kern<<<grid, 32 * (NCW + 4), smem, st>>>(mq, mk, mv, mk16, mv16, mo, tp);
+  kern<<<grid, 32 * (NCW + 4), smem, st>>>(mq, mk, mv, mo, tp);
   return cudaGetLastError();
 }
 
