@@ -20,8 +20,6 @@ bool tc_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tc(const dc_attn_params &p, cudaStream_t st);
 bool tcs_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tcs(const dc_attn_params &p, cudaStream_t st);
-bool tcs32_supports(const dc_attn_params &p, std::string *why);
-cudaError_t launch_tcs32(const dc_attn_params &p, cudaStream_t st);
 bool tcm_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tcm(const dc_attn_params &p, cudaStream_t st);
 }  // namespace dcattn
@@ -86,9 +84,7 @@ int select_kernel(const dc_attn_params &p) {
     return DC_KERNEL_TC;
   }
   std::string why_s;
-  // 32 heads per group: the M = 64 streaming variant (tcs32_kernel.cu)
-  const bool tcs_ok = (p.G > 0 && p.H / p.G == 32) ? dcattn::tcs32_supports(p, &why_s)
-                                                   : dcattn::tcs_supports(p, &why_s);
+  const bool tcs_ok = dcattn::tcs_supports(p, &why_s);
   if (p.kernel == DC_KERNEL_TCS) {
     if (!tcs_ok)
       return fail(DC_ERR_UNSUPPORTED, "streaming tensor-core kernel does not support this call: %s", why_s.c_str());
@@ -145,7 +141,7 @@ int dc_attn_fwd(const dc_attn_params *pp, void *stream) {
   } else if (which == DC_KERNEL_TCM) {
     e = dcattn::launch_tcm(p, st);
   } else if (which == DC_KERNEL_TCS) {
-    e = (p.H / p.G == 32) ? dcattn::launch_tcs32(p, st) : dcattn::launch_tcs(p, st);
+    e = dcattn::launch_tcs(p, st);
   } else {
     e = dcattn::launch_simt(dcattn::to_dev(p), p.dtype, st);
   }

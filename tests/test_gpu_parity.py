@@ -280,24 +280,6 @@ def test_tcs_matches_tc_on_windowed_layer():
 
 @pytest.mark.parametrize("H,G,R,window,T,B,seq_lens,dtype", [
     (32, 1, 1, 128, 200, 1, None, "bf16"),          # config-0 layer shape, ragged T
-    (32, 1, 2, None, 300, 1, None, "bf16"),         # full causal, three key tiles at the end
-    (32, 1, 1, 64, 150, 2, [150, 77], "fp16"),      # seq_lens, fp16
-    (64, 2, 1, 100, 130, 1, None, "bf16"),          # two groups of 32 (head offset of the key weights)
-    (32, 1, 2, 1, 40, 1, None, "bf16"),             # window 1
-])
-def test_tcs32_kernel_vs_oracle(H, G, R, window, T, B, seq_lens, dtype):
-    """M = 64 streaming tensor-core kernel for 32 heads per group, every term."""
-    dt = TORCH_DT[dtype]
-    q, k, v, pre, post = O.make_inputs(B, T, H, 128, G, R, seed=H + G * 5 + R + T)
-    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
-    pre, post = round_terms(pre, dt), round_terms(post, dt)
-    ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens)
-    got = run_general(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens, dtype, "tcs")
-    assert_close(got, ref, f"tcs32 H{H} G{G} R{R} W{window} T{T}")
-
-
-@pytest.mark.parametrize("H,G,R,window,T,B,seq_lens,dtype", [
-    (32, 1, 1, 128, 200, 1, None, "bf16"),          # config-0 layer shape, ragged T
     (32, 1, 2, None, 300, 1, None, "bf16"),         # full causal, five key tiles at the end
     (32, 1, 1, 64, 150, 2, [150, 77], "fp16"),      # seq_lens, fp16
     (64, 2, 1, 100, 130, 1, None, "bf16"),          # two groups of 32 (head offset of the key weights)
