@@ -519,8 +519,9 @@ __host__ __device__ inline GeoP make_geo_p(int HPG, int R, int rlast, int nslot)
   const int ring_end = g.ring_off + nslot * TILE_BYTES;
   int o = ring_end;
   g.rec_floats = round_up(HPG * (2 * R + 1), 4);
-  g.wz_off = o;  o += 2 * HPG * HPG * 4;
-  g.rec_off = round_up(o, 16); o = g.rec_off + 2 * BM * g.rec_floats * 4;
+  g.wz_off = o;  o += 2 * HPG * HPG * 4 + 2 * HPG * 4;  // + identity/diagonal table [2][HPG]
+  // per-query records, double-buffered: tile n+1's are fetched during tile n
+  g.rec_off = round_up(o, 16); o = g.rec_off + 2 * (2 * BM * g.rec_floats * 4);
   g.red_off = o; o += 2 * 8 * NQ * 4;
   g.bar_off = round_up(o, 8); o = g.bar_off + 32 * 8;
   g.tmem_off = o; o += 16;
@@ -815,6 +816,40 @@ __global__ void __launch_bounds__(32 * NW, 1)
     auto col_of = [&](int L, int i0) { return (L / GI) * BM + i0 + (L % GI); };
     WSrc<HPG> Wreg;
     float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
+    // per-query records of one tile: [set][query][dq | qw1 (h, r) | qw2 (r, h)],
+    // dq = identity + w[h,h] (the table `wdiag`, one per group) + qdd[t,h].
+    // A record is at most one 16-bit element of a per-token weight plus that
+    // constant, so the next tile's records are prefetched as raw 16-bit
+    // values (no conversion stalls on arrival) and converted when stored.
+    const int nrec = 2 * BM * geo.rec_floats;
+    float *wdiag = Wz + 2 * HPG * HPG;
+    auto rec_src = [&](int idx, int q0, int b, int g) -> const unsigned short * {
+      const int set = idx / (BM * geo.rec_floats), rem = idx % (BM * geo.rec_floats);
+      const int i = rem / geo.rec_floats, j = rem % geo.rec_floats;
+      const TermPtrs &tm = set ? p.post : p.pre;
+      const int t = q0 + i, hbase = g * HPG;
+      if (t >= T) return nullptr;
+      const int64_t tok = (int64_t)b * T + t;
+      const void *base = nullptr;
+      int64_t e = 0;
+      if (j < HPG) {
+        base = tm.qdd; e = tok * H + hbase + j;
+      } else if (j < HPG + HPG * R) {
+        const int h = (j - HPG) / R, r = (j - HPG) % R;
+        base = tm.qw1; e = (tok * H + hbase + h) * R + r;
+      } else if (j < HPG + 2 * HPG * R) {
+        const int r = (j - HPG - HPG * R) / HPG, h = (j - HPG - HPG * R) % HPG;
+        base = tm.qw2; e = (tok * R + r) * H + hbase + h;
+      }
+      return base ? reinterpret_cast<const unsigned short *>(base) + e : nullptr;
+    };
+    auto rec_store = [&](float *dst, int idx, unsigned short raw, bool has) {
+      const int set = idx / (BM * geo.rec_floats), j = (idx % (BM * geo.rec_floats)) % geo.rec_floats;
+      float v = j < HPG ? wdiag[set * HPG + j] : 0.f;
+      if (has) v += to_f<E>(*reinterpret_cast<const E *>(&raw));
+      dst[idx] = v;
+    };
+    constexpr int MAXREC = 4;  // records per compose thread (checked by the launcher)
     int it = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       int q0, b, g;
@@ -822,37 +857,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const int buf = it & 1, hbase = g * HPG;
       const int kb = q0 - p.window + 1;
       const int slen = p.seq_lens ? min(max(p.seq_lens[b], 0), T) : T;
-      // previous tile's pass 2 is finished by every compose warp before rec / red are rewritten
-      ptx::named_bar_sync(1, ncompose);
-      if (it == 0)
-        for (int idx = ctid; idx < 2 * HPG * HPG; idx += ncompose) {
-          const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
-          const TermPtrs &tm = set ? p.post : p.pre;
-          const int h = j / HPG, hp = j % HPG;
-          Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
-        }
-      for (int idx = ctid; idx < 2 * BM * geo.rec_floats; idx += ncompose) {
-        const int set = idx / (BM * geo.rec_floats), rem = idx % (BM * geo.rec_floats);
-        const int i = rem / geo.rec_floats, j = rem % geo.rec_floats;
-        const TermPtrs &tm = set ? p.post : p.pre;
-        const int t = q0 + i;
-        float val = 0.f;
-        if (t < T) {
-          const int64_t tok = (int64_t)b * T + t;
-          if (j < HPG) {
-            const int h = j;
-            val = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)g * HPG + h) * HPG + h] : 0.f) +
-                  (tm.qdd ? ld_w<E>(tm.qdd, tok * H + hbase + h) : 0.f);
-          } else if (j < HPG + HPG * R) {
-            const int h = (j - HPG) / R, r = (j - HPG) % R;
-            val = tm.qw1 ? ld_w<E>(tm.qw1, (tok * H + hbase + h) * R + r) : 0.f;
-          } else if (j < HPG + 2 * HPG * R) {
-            const int r = (j - HPG - HPG * R) / HPG, h = (j - HPG - HPG * R) % HPG;
-            val = tm.qw2 ? ld_w<E>(tm.qw2, (tok * R + r) * H + hbase + h) : 0.f;
-          }
-        }
-        rec[idx] = val;
-      }
       const int s = kb + kt * KT_ROWS + s_local;
       const bool key_ok = s >= 0 && s < slen && s_local < rows_kt;
       const int wk0 = kb + kt * KT_ROWS + 32 * sub, wk1 = wk0 + 31;
@@ -861,10 +865,32 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const int64_t ktok = (int64_t)b * T + s;
       const uint32_t tl = tbase + (static_cast<uint32_t>(32 * sub) << 16) + buf * 256 + kt * KT_ROWS;
       auto valid = [&](int t) { return key_ok && s <= t && t - s < p.window && t < T; };
+      // issue this tile's key-weight loads first: their latency overlaps the barrier
       if (active) load_key_weights<E, HPG, R>(p.pre, ktok, H, hbase, key_ok, kw1, kw2, kdd);
-      ptx::named_bar_sync(1, ncompose);  // staged weights visible
+      // previous tile's pass 2 is finished by every compose warp before red and
+      // the record buffer of tile n+1 are rewritten
+      if (it == 0) {
+        for (int idx = ctid; idx < 2 * HPG * HPG; idx += ncompose) {
+          const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
+          const TermPtrs &tm = set ? p.post : p.pre;
+          const int h = j / HPG, hp = j % HPG;
+          Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
+        }
+        for (int idx = ctid; idx < 2 * HPG; idx += ncompose) {
+          const TermPtrs &tm = idx / HPG ? p.post : p.pre;
+          const int h = idx % HPG;
+          wdiag[idx] = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)g * HPG + h) * HPG + h] : 0.f);
+        }
+        ptx::named_bar_sync(1, ncompose);  // wdiag visible
+        for (int idx = ctid; idx < nrec; idx += ncompose) {
+          const unsigned short *src = rec_src(idx, q0, b, g);
+          rec_store(rec, idx, src ? __ldg(src) : (unsigned short)0, src != nullptr);
+        }
+      }
+      ptx::named_bar_sync(1, ncompose);  // staged weights / records visible, previous tile done
+      const float *recb = rec + (it & 1) * nrec;
       if (active) {
-Wreg.load(Wz);
+        Wreg.load(Wz);
       }
       if (threadIdx.x == 0) TLP_STAMP(it, 0);
       bool ok = ptx::mbar_wait(bar_S + 2 * buf + kt, (it >> 1) & 1, WAIT);
@@ -888,7 +914,7 @@ Wreg.load(Wz);
 #pragma unroll
             for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
 #ifndef DC_EXP_NOCOMPOSE
-            compose<HPG, R>(a, o, Wreg, rec + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+            compose<HPG, R>(a, o, Wreg, recb + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
 #else
 #pragma unroll
             for (int h = 0; h < HPG; ++h) o[h] = a[h];
@@ -965,6 +991,21 @@ Wreg.load(Wz);
 Wreg.load(Wz + HPG * HPG);
         load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
       }
+      // fetch the next tile's records now (raw 16-bit); they land during pass 2
+      unsigned short nrv[MAXREC];
+      bool nhas[MAXREC];
+      const int ntile = tile + gridDim.x;
+      if (ntile < ntiles) {
+        int nq0, nb, ng;
+        tile_coords(ntile, nq0, nb, ng);
+#pragma unroll
+        for (int k = 0; k < MAXREC; ++k) {
+          const int idx = ctid + k * ncompose;
+          const unsigned short *src = idx < nrec ? rec_src(idx, nq0, nb, ng) : nullptr;
+          nhas[k] = src != nullptr;
+          nrv[k] = src ? __ldg(src) : (unsigned short)0;
+        }
+      }
       const float *fac = redm + rw * NQ;
       unsigned char *pbase = p_tile(buf, kt) + (s_local & 7) * 16 + (s_local >> 3) * (BM * 16);
 #pragma unroll 1
@@ -980,7 +1021,7 @@ Wreg.load(Wz + HPG * HPG);
             float a[HPG], o[HPG];
 #pragma unroll
             for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * fac[h * BM + i0 + ii];
-            compose<HPG, R>(a, o, Wreg, rec + (BM + i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+            compose<HPG, R>(a, o, Wreg, recb + (BM + i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
 #pragma unroll
             for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
           }
@@ -1015,6 +1056,14 @@ Wreg.load(Wz + HPG * HPG);
               }
             }
           }
+        }
+      }
+      if (ntile < ntiles) {
+        float *nrec_buf = rec + ((it + 1) & 1) * nrec;
+#pragma unroll
+        for (int k = 0; k < MAXREC; ++k) {
+          const int idx = ctid + k * ncompose;
+          if (idx < nrec) rec_store(nrec_buf, idx, nrv[k], nhas[k]);
         }
       }
       ptx::fence_proxy_async_smem();
@@ -1102,6 +1151,9 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
   tp.pre = to_ptrs(p.pre);
   tp.post = to_ptrs(p.post);
   const WarpRoles roles = make_roles(nkt, rlast, CS);
+  // the compose threads prefetch the next tile's per-query records, at most
+  // 4 each (MAXREC in the kernel); otherwise run the per-tile kernel
+  if (2 * BM * round_up(HPG * (2 * R + 1), 4) > 4 * 32 * roles.ncw) return launch_t<E, HPG, R>(p, st);
   auto kern = roles.nwarps <= 18 ? dc_tcp_kernel<E, HPG, R, CS, 18> : dc_tcp_kernel<E, HPG, R, CS, 22>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
