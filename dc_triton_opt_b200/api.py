@@ -4,6 +4,8 @@ Entry points (each a drop-in for the reference call it names):
 
 * :func:`dc_attn_fwd` — general form: static head mix W, query- and key-wise
   rank-R weights, qdd/kdd gates, per-query matrices; window or full causal.
+* :func:`dc_attn_fwd_host` — the same for inputs and output in host memory,
+  with the batch pipelined over copy / compute streams.
 * :func:`dc_attention_window_chunked_residual_grouped` —
   ``dc_attention_torch.py:159`` (same signature, defaults, output [B,N,T,D]).
 * :func:`dc_attention_window_chunked_residual` — ``dc_attention_torch.py:88``.
@@ -155,6 +157,108 @@ def dc_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         _lib.check(lib.dc_attn_fwd(ctypes.byref(p), ctypes.c_void_p(stream)))
     # Converted temporaries in `keep` may be freed on return: the caching
     # allocator only hands their blocks to later work on this same stream.
+    return out
+
+
+_PER_TOKEN = ("qw1", "qw2", "kw1", "kw2", "qdd", "kdd", "qmat")
+_host_ws = {}  # (device, name, shape, dtype) -> device buffer reused across calls
+
+
+def _ws(device, name, shape, dtype):
+    key = (device, name, tuple(shape), dtype)
+    buf = _host_ws.get(key)
+    if buf is None:
+        buf = torch.empty(shape, device=device, dtype=dtype)
+        _host_ws[key] = buf
+    return buf
+
+
+def dc_attn_fwd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                     pre: Optional[DCTerms] = None, post: Optional[DCTerms] = None,
+                     scaling: Optional[float] = None, window: Optional[int] = None, G: int = 1,
+                     seq_lens: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                     device=None, chunks: int = 4, kernel: str = "auto") -> torch.Tensor:
+    """:func:`dc_attn_fwd` for inputs in host memory (ideally pinned).
+
+    q, k, v [B,T,H,D] and the per-token weights of ``pre``/``post`` are CPU
+    tensors; the output is written to ``out`` (a [B,T,H,D] CPU tensor; a pinned
+    one is allocated if None).  The batch is processed in ``chunks`` slices
+    whose host-to-device copies, forward and device-to-host copies run on three
+    streams, so the transfers of neighbouring slices overlap each other and the
+    compute (two device buffers per stream stage).  Asynchronous like the
+    device entry point: the caller's current stream waits for the last copy,
+    so a ``torch.cuda.synchronize()`` (or a sync of that stream) makes ``out``
+    valid.
+    """
+    _check(q.dim() == 4 and not q.is_cuda and not k.is_cuda and not v.is_cuda,
+           "q, k, v must be [B,T,H,D] host tensors")
+    _check(k.shape == q.shape and v.shape == q.shape, "k and v must match q's shape")
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    B, T, H, D = q.shape
+    dtype = q.dtype
+    if out is None:
+        out = torch.empty((B, T, H, D), dtype=dtype, pin_memory=True)
+    _check(out.shape == (B, T, H, D) and out.dtype == dtype and not out.is_cuda and out.is_contiguous(),
+           "out must be a contiguous [B,T,H,D] host tensor of q's dtype")
+    nch = max(1, min(int(chunks), B))
+    cb = -(-B // nch)
+    comp = torch.cuda.current_stream(device)
+    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    # static mixes (small) go to the device once
+    w_dev = {}
+    for side, tm in (("pre", pre), ("post", post)):
+        if tm is not None and tm.w is not None:
+            w_dev[side] = tm.w.to(device=device, dtype=torch.float32, non_blocking=True)
+    sl_dev = None
+    if seq_lens is not None:
+        sl_dev = seq_lens.to(device=device, dtype=torch.int32, non_blocking=True)
+    ev_comp = [None, None]  # per buffer slot: forward finished (inputs and output buffer in use until then)
+    ev_out = [None, None]   # per buffer slot: output copied back
+    last = None
+    with torch.cuda.device(device):
+        for c in range(nch):
+            b0, b1 = c * cb, min(B, (c + 1) * cb)
+            if b0 >= b1:
+                break
+            n, slot = b1 - b0, c % 2
+
+            def dev(name, t):
+                buf = _ws(device, f"{slot}.{name}", (cb,) + tuple(t.shape[1:]), t.dtype)[:n]
+                buf.copy_(t[b0:b1], non_blocking=True)
+                return buf
+
+            with torch.cuda.stream(s_in):
+                if ev_comp[slot] is not None:
+                    s_in.wait_event(ev_comp[slot])
+                dq, dk, dv = dev("q", q), dev("k", k), dev("v", v)
+                terms = {}
+                for side, tm in (("pre", pre), ("post", post)):
+                    if tm is None:
+                        terms[side] = None
+                        continue
+                    kw = {"identity": tm.identity, "w": w_dev.get(side)}
+                    for f in _PER_TOKEN:
+                        t = getattr(tm, f)
+                        kw[f] = None if t is None else dev(f"{side}.{f}", t)
+                    terms[side] = DCTerms(**kw)
+                ev_in = torch.cuda.Event()
+                ev_in.record(s_in)
+            comp.wait_event(ev_in)
+            if ev_out[slot] is not None:
+                comp.wait_event(ev_out[slot])
+            dout = _ws(device, f"{slot}.out", (cb, T, H, D), dtype)[:n]
+            dc_attn_fwd(dq, dk, dv, terms["pre"], terms["post"], scaling, window, G,
+                        None if sl_dev is None else sl_dev[b0:b1], out=dout, kernel=kernel)
+            ev_comp[slot] = torch.cuda.Event()
+            ev_comp[slot].record(comp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_comp[slot])
+                out[b0:b1].copy_(dout, non_blocking=True)
+                ev_out[slot] = torch.cuda.Event()
+                ev_out[slot].record(s_out)
+                last = ev_out[slot]
+        if last is not None:
+            comp.wait_event(last)
     return out
 
 

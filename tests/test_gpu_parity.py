@@ -297,3 +297,24 @@ def test_tcm_kernel_vs_oracle(H, G, R, window, T, B, seq_lens, dtype):
     ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens)
     got = run_general(q, k, v, pre, post, 128 ** -0.5, window, G, seq_lens, dtype, "tcm")
     assert_close(got, ref, f"tcm H{H} G{G} R{R} W{window} T{T}")
+
+
+@pytest.mark.parametrize("G,B,seq_lens,chunks", [(8, 5, [64, 30, 64, 1, 50], 4), (1, 3, None, 2), (8, 1, None, 4)])
+def test_host_entry_point_matches_device(G, B, seq_lens, chunks):
+    """dc_attn_fwd_host (host tensors, batch pipelined over streams) equals the
+    device entry point bit for bit, ragged last chunk and seq_lens included."""
+    dt = torch.bfloat16
+    q, k, v, pre, post = O.make_inputs(B, 64, 32, 128, G, 1, seed=G + B)
+    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    sl = None if seq_lens is None else torch.tensor(seq_lens, dtype=torch.int32)
+    qd, kd, vd = (T_(x, dt) for x in (q, k, v))
+    pre_d, post_d = to_dcterms(pre, dt), to_dcterms(post, dt)
+    ref = dc.dc_attn_fwd(qd, kd, vd, pre_d, post_d, 128 ** -0.5, 48, G, None if sl is None else sl.to(DEV))
+    host = lambda tm: dc.DCTerms(identity=tm.identity, w=tm.w, **{f: (None if getattr(tm, f) is None else
+                                 getattr(tm, f).cpu().pin_memory()) for f in ("qw1", "qw2", "kw1", "kw2",
+                                                                             "qdd", "kdd")})
+    got = dc.dc_attn_fwd_host(qd.cpu().pin_memory(), kd.cpu().pin_memory(), vd.cpu().pin_memory(),
+                              host(pre_d), host(post_d), 128 ** -0.5, 48, G, sl, chunks=chunks)
+    torch.cuda.synchronize()
+    assert torch.equal(got, ref.cpu())
