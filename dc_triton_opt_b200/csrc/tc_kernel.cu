@@ -502,7 +502,7 @@ struct GeoP {
   int nslot, q_off, p1_off, ring_off, wz_off, rec_off, red_off, bar_off, tmem_off, total, rec_floats, p1_bytes;
 };
 
-__host__ __device__ inline GeoP make_geo_p(int HPG, int R, int rlast, int nslot) {
+__host__ __device__ inline GeoP make_geo_p(int HPG, int R, int rlast, int nslot, int G) {
   GeoP g{};
   const int BM = NQ / HPG;
   g.nslot = nslot;
@@ -519,7 +519,9 @@ __host__ __device__ inline GeoP make_geo_p(int HPG, int R, int rlast, int nslot)
   const int ring_end = g.ring_off + nslot * TILE_BYTES;
   int o = ring_end;
   g.rec_floats = round_up(HPG * (2 * R + 1), 4);
-  g.wz_off = o;  o += 2 * HPG * HPG * 4 + 2 * HPG * 4;  // + identity/diagonal table [2][HPG]
+  // static mixes of every group [2][G][HPG*HPG] and the identity + diagonal
+  // table [2][G][HPG]: a persistent CTA's tiles belong to different groups
+  g.wz_off = o;  o += 2 * G * HPG * HPG * 4 + 2 * G * HPG * 4;
   // per-query records, double-buffered: tile n+1's are fetched during tile n
   g.rec_off = round_up(o, 16); o = g.rec_off + 2 * (2 * BM * g.rec_floats * 4);
   g.red_off = o; o += 2 * 8 * NQ * 4;
@@ -543,7 +545,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                           ~static_cast<uintptr_t>(1023));
-  const GeoP geo = make_geo_p(HPG, R, rlast, nslot);
+  const GeoP geo = make_geo_p(HPG, R, rlast, nslot, p.G);
   float *Wz = reinterpret_cast<float *>(smem + geo.wz_off);
   float *rec = reinterpret_cast<float *>(smem + geo.rec_off);
   float *red = reinterpret_cast<float *>(smem + geo.red_off);
@@ -817,12 +819,13 @@ __global__ void __launch_bounds__(32 * NW, 1)
     WSrc<HPG> Wreg;
     float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
     // per-query records of one tile: [set][query][dq | qw1 (h, r) | qw2 (r, h)],
-    // dq = identity + w[h,h] (the table `wdiag`, one per group) + qdd[t,h].
+    // dq = identity + w[h,h] (the table `wdiag`, per group) + qdd[t,h].
     // A record is at most one 16-bit element of a per-token weight plus that
     // constant, so the next tile's records are prefetched as raw 16-bit
     // values (no conversion stalls on arrival) and converted when stored.
     const int nrec = 2 * BM * geo.rec_floats;
-    float *wdiag = Wz + 2 * HPG * HPG;
+    const int G = p.G;
+    float *wdiag = Wz + 2 * G * HPG * HPG;  // [set][group][HPG]
     auto rec_src = [&](int idx, int q0, int b, int g) -> const unsigned short * {
       const int set = idx / (BM * geo.rec_floats), rem = idx % (BM * geo.rec_floats);
       const int i = rem / geo.rec_floats, j = rem % geo.rec_floats;
@@ -843,9 +846,9 @@ __global__ void __launch_bounds__(32 * NW, 1)
       }
       return base ? reinterpret_cast<const unsigned short *>(base) + e : nullptr;
     };
-    auto rec_store = [&](float *dst, int idx, unsigned short raw, bool has) {
+    auto rec_store = [&](float *dst, int idx, unsigned short raw, bool has, int gg) {
       const int set = idx / (BM * geo.rec_floats), j = (idx % (BM * geo.rec_floats)) % geo.rec_floats;
-      float v = j < HPG ? wdiag[set * HPG + j] : 0.f;
+      float v = j < HPG ? wdiag[(set * G + gg) * HPG + j] : 0.f;
       if (has) v += to_f<E>(*reinterpret_cast<const E *>(&raw));
       dst[idx] = v;
     };
@@ -870,27 +873,27 @@ __global__ void __launch_bounds__(32 * NW, 1)
       // previous tile's pass 2 is finished by every compose warp before red and
       // the record buffer of tile n+1 are rewritten
       if (it == 0) {
-        for (int idx = ctid; idx < 2 * HPG * HPG; idx += ncompose) {
-          const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
+        for (int idx = ctid; idx < 2 * G * HPG * HPG; idx += ncompose) {
+          const int set = idx / (G * HPG * HPG), gg = (idx / (HPG * HPG)) % G, j = idx % (HPG * HPG);
           const TermPtrs &tm = set ? p.post : p.pre;
           const int h = j / HPG, hp = j % HPG;
-          Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
+          Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)gg * HPG + hp) * HPG + h];
         }
-        for (int idx = ctid; idx < 2 * HPG; idx += ncompose) {
-          const TermPtrs &tm = idx / HPG ? p.post : p.pre;
-          const int h = idx % HPG;
-          wdiag[idx] = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)g * HPG + h) * HPG + h] : 0.f);
+        for (int idx = ctid; idx < 2 * G * HPG; idx += ncompose) {
+          const int set = idx / (G * HPG), gg = (idx / HPG) % G, h = idx % HPG;
+          const TermPtrs &tm = set ? p.post : p.pre;
+          wdiag[idx] = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)gg * HPG + h) * HPG + h] : 0.f);
         }
         ptx::named_bar_sync(1, ncompose);  // wdiag visible
         for (int idx = ctid; idx < nrec; idx += ncompose) {
           const unsigned short *src = rec_src(idx, q0, b, g);
-          rec_store(rec, idx, src ? __ldg(src) : (unsigned short)0, src != nullptr);
+          rec_store(rec, idx, src ? __ldg(src) : (unsigned short)0, src != nullptr, g);
         }
       }
       ptx::named_bar_sync(1, ncompose);  // staged weights / records visible, previous tile done
       const float *recb = rec + (it & 1) * nrec;
       if (active) {
-        Wreg.load(Wz);
+        Wreg.load(Wz + g * HPG * HPG);
       }
       if (threadIdx.x == 0) TLP_STAMP(it, 0);
       bool ok = ptx::mbar_wait(bar_S + 2 * buf + kt, (it >> 1) & 1, WAIT);
@@ -988,15 +991,15 @@ __global__ void __launch_bounds__(32 * NW, 1)
 
       // ---- pass 2: normalise, post-composition, P' -> SMEM
       if (active && ok) {
-Wreg.load(Wz + HPG * HPG);
+Wreg.load(Wz + (G + g) * HPG * HPG);
         load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
       }
       // fetch the next tile's records now (raw 16-bit); they land during pass 2
       unsigned short nrv[MAXREC];
       bool nhas[MAXREC];
       const int ntile = tile + gridDim.x;
+      int nq0 = 0, nb = 0, ng = 0;
       if (ntile < ntiles) {
-        int nq0, nb, ng;
         tile_coords(ntile, nq0, nb, ng);
 #pragma unroll
         for (int k = 0; k < MAXREC; ++k) {
@@ -1063,7 +1066,7 @@ Wreg.load(Wz + HPG * HPG);
 #pragma unroll
         for (int k = 0; k < MAXREC; ++k) {
           const int idx = ctid + k * ncompose;
-          if (idx < nrec) rec_store(nrec_buf, idx, nrv[k], nhas[k]);
+          if (idx < nrec) rec_store(nrec_buf, idx, nrv[k], nhas[k], ng);
         }
       }
       ptx::fence_proxy_async_smem();
@@ -1130,8 +1133,8 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
   // deepest K/V ring that fits, at most 3 slots: a 4th slot (SMEM ~226 KB)
   // measured slower, the smaller L1 then serves spills and weight loads worse
   int nslot = 3;
-  while (nslot > 2 && make_geo_p(HPG, R, rlast, nslot).total + 1024 > 227 * 1024) --nslot;
-  const size_t smem = make_geo_p(HPG, R, rlast, nslot).total + 1024;
+  while (nslot > 2 && make_geo_p(HPG, R, rlast, nslot, p.G).total + 1024 > 227 * 1024) --nslot;
+  const size_t smem = make_geo_p(HPG, R, rlast, nslot, p.G).total + 1024;
   const int64_t sb = (int64_t)p.T * p.H * D, st_ = (int64_t)p.H * D, sh = D;
   CUtensorMap mq, mk, mv, mkl, mvl, mo;
   if (!make_map(&mq, p.q, p.dtype, p.B, p.T, p.H, BM, sb, st_, sh, true) ||

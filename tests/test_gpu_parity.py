@@ -318,3 +318,18 @@ def test_host_entry_point_matches_device(G, B, seq_lens, chunks):
                               host(pre_d), host(post_d), 128 ** -0.5, 48, G, sl, chunks=chunks)
     torch.cuda.synchronize()
     assert torch.equal(got, ref.cpu())
+
+
+@pytest.mark.parametrize("G", [8, 32, 4])
+def test_persistent_kernel_many_tiles_per_cta(G):
+    """More tiles than SMs, so each persistent CTA walks tiles of several batches
+    and head groups (each group with its own static mix): every tile must use
+    its own group's weights."""
+    dt = torch.bfloat16
+    B, T = 8, 640
+    q, k, v, pre, post = O.make_inputs(B, T, 32, 128, G, 1, seed=500 + G, mix_std=0.05)
+    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, 128, G, None)
+    got = run_general(q, k, v, pre, post, 128 ** -0.5, 128, G, None, "bf16", "tc")
+    assert_close(got, ref, f"persistent G{G} B{B} T{T}")
