@@ -66,12 +66,12 @@ def _oracle_rows(q, k, v, pre, post, b, a, t0, t1, window, G):
     return ref[0, t0 - a:]
 
 
-@pytest.mark.parametrize("G", [8, 1])
+@pytest.mark.parametrize("G", [8, 1, 2, 4, 16, 32])
 def test_config1_full_size_window_locality(G):
-    """config1 (B16 T4096 H32 D128 W128 R1, every term) at G=8 (persistent TC
-    kernel) and G=1 (tensor-core-mix kernel): rows at the sequence start, in
-    the middle and at the end of the last batch against the oracle on their
-    key windows."""
+    """config1 (B16 T4096 H32 D128 W128 R1, every term) over the G sweep
+    (persistent TC kernel for G >= 4, tensor-core-mix kernel for G <= 2):
+    rows at the sequence start, in the middle and at the end of the last
+    batch against the oracle on their key windows."""
     B, T, H, D, R, W = 16, 4096, 32, 128, 1, 128
     q, k, v, pre, post = _inputs(B, T, H, D, G, R, seed=100 + G)
     out = dc.dc_attn_fwd(q, k, v, pre, post, D ** -0.5, W, G)
@@ -82,16 +82,18 @@ def test_config1_full_size_window_locality(G):
         assert_close(_np(out[b, t0:t1]), ref, f"config1 G{G} b{b} rows [{t0},{t1})")
 
 
-def test_config2_g1_full_size_window_locality():
-    """config2 at G=1 (W256 R2): 3-key-tile spans through the tensor-core-mix kernel."""
-    B, T, H, D, G, R, W = 16, 4096, 32, 128, 1, 2, 256
-    q, k, v, pre, post = _inputs(B, T, H, D, G, R, seed=201)
+@pytest.mark.parametrize("G", [1, 4, 32])
+def test_config2_full_size_window_locality(G):
+    """config2 (W256 R2) at its G values: 3-key-tile spans (single-pass TC
+    kernel for G 4 and 32, tensor-core-mix kernel for G 1)."""
+    B, T, H, D, R, W = 16, 4096, 32, 128, 2, 256
+    q, k, v, pre, post = _inputs(B, T, H, D, G, R, seed=200 + G)
     out = dc.dc_attn_fwd(q, k, v, pre, post, D ** -0.5, W, G)
     torch.cuda.synchronize()
     for b, t0, t1 in ((3, 100, 164), (15, 4040, 4096)):
         a = max(0, t0 - W + 1)
         ref = _oracle_rows(q, k, v, pre, post, b, a, t0, t1, W, G)
-        assert_close(_np(out[b, t0:t1]), ref, f"config2 G1 b{b} rows [{t0},{t1})")
+        assert_close(_np(out[b, t0:t1]), ref, f"config2 G{G} b{b} rows [{t0},{t1})")
 
 
 def test_config3_full_size_causal_prefix():

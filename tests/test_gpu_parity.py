@@ -320,7 +320,7 @@ def test_host_entry_point_matches_device(G, B, seq_lens, chunks):
     assert torch.equal(got, ref.cpu())
 
 
-@pytest.mark.parametrize("G", [8, 32, 4])
+@pytest.mark.parametrize("G", [8, 32, 4, 16])
 def test_persistent_kernel_many_tiles_per_cta(G):
     """More tiles than SMs, so each persistent CTA walks tiles of several batches
     and head groups (each group with its own static mix): every tile must use
