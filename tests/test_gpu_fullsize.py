@@ -123,3 +123,24 @@ def test_config1_full_size_batch_shards_are_exact(G):
         part = dc.dc_attn_fwd(q[b0:b1], k[b0:b1], v[b0:b1], half(pre, b0, b1), half(post, b0, b1), D ** -0.5, W, G)
         torch.cuda.synchronize()
         assert torch.equal(part, full[b0:b1]), f"G{G} batch slice [{b0},{b1}) differs"
+
+
+def test_config4_full_size_window_locality_and_shard():
+    """config4 (B64 T8192 W256 G1 R2, the multi-GPU scaling layer) on one GPU:
+    rows at both ends of the sequence against the oracle on their windows, and
+    the rank-3-of-8 batch shard equal to the same rows of the full batch."""
+    B, T, H, D, G, R, W = 64, 8192, 32, 128, 1, 2, 256
+    q, k, v, pre, post = _inputs(B, T, H, D, G, R, seed=501)
+    out = dc.dc_attn_fwd(q, k, v, pre, post, D ** -0.5, W, G)
+    torch.cuda.synchronize()
+    for b, t0, t1 in ((0, 0, 32), (63, 8160, 8192)):
+        a = max(0, t0 - W + 1)
+        ref = _oracle_rows(q, k, v, pre, post, b, a, t0, t1, W, G)
+        assert_close(_np(out[b, t0:t1]), ref, f"config4 b{b} rows [{t0},{t1})")
+    b0, b1 = 24, 32
+    part = dc.dc_attn_fwd(q[b0:b1], k[b0:b1], v[b0:b1],
+                          dc.DCTerms(identity=pre.identity, w=pre.w, **{f: getattr(pre, f)[b0:b1] for f in PER_TOKEN}),
+                          dc.DCTerms(identity=post.identity, w=post.w, **{f: getattr(post, f)[b0:b1] for f in PER_TOKEN}),
+                          D ** -0.5, W, G)
+    torch.cuda.synchronize()
+    assert torch.equal(part, out[b0:b1])
