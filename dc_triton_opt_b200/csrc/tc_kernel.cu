@@ -449,9 +449,6 @@ Wreg.load(Wz + HPG * HPG);
 // Q(n) K(n) V(n-1), i.e. QK(n) is issued before PV(n-1) so the compose warps
 // can start tile n while tile n-1 drains.
 
-// development switch: force the one-tile-per-CTA kernel
-bool g_disable_persistent = false;
-
 // Warp-role table of the persistent kernel, built on the host.  Compose warps
 // exist only for the TMEM lane quarters that hold keys of their key tile (the
 // last key tile is usually short), and a compose warp must sit at an index
@@ -916,12 +913,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
             float a[HPG], o[HPG];
 #pragma unroll
             for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
-#ifndef DC_EXP_NOCOMPOSE
             compose<HPG, R>(a, o, Wreg, recb + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
-#else
-#pragma unroll
-            for (int h = 0; h < HPG; ++h) o[h] = a[h];
-#endif
             const bool vl = valid(q0 + i0 + ii);
 #pragma unroll
             for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : -INFINITY;
@@ -930,17 +922,9 @@ __global__ void __launch_bounds__(32 * NW, 1)
           for (int h = 0; h < HPG; ++h)
 #pragma unroll
             for (int ii = 0; ii < GI; ++ii) {
-#ifndef DC_EXP_NOREDUX
               const float mw = ptx::warp_max(v[h][ii]);
-#else
-              const float mw = 0.f;
-#endif
               if (lane == h * GI + ii) mine_m = mw;
-#ifndef DC_EXP_NOEXP
               v[h][ii] = exp2f((v[h][ii] - (mw == -INFINITY ? 0.f : mw)) * sl2e);
-#else
-              v[h][ii] = (v[h][ii] - (mw == -INFINITY ? 0.f : mw)) * sl2e;
-#endif
             }
 #pragma unroll
           for (int h = 0; h < HPG; ++h) ptx::tmem_st<GI>(tl + h * BM + i0, v[h]);
@@ -949,7 +933,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
           for (int h = 0; h < HPG; ++h)
 #pragma unroll
             for (int ii = 0; ii < GI; ++ii) x[h * GI + ii] = v[h][ii];
-#ifndef DC_EXP_NOSUM
 #pragma unroll
           for (int off = 16, cnt = 32; off >= 1; off >>= 1, cnt >>= 1) {
             const bool upper = (lane & off) != 0;
@@ -960,7 +943,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
               x[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
             }
           }
-#endif
           mine_s = x[0];
         }
         redm[rw * NQ + col_of(lane, i0)] = mine_m;
@@ -1169,7 +1151,7 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
 
 template <typename E, int HPG>
 static cudaError_t launch_r(const dc_attn_params &p, cudaStream_t st) {
-  if (num_key_tiles(HPG, p.window) <= 2 && !g_disable_persistent)
+  if (num_key_tiles(HPG, p.window) <= 2)
     return p.R <= 1 ? launch_p<E, HPG, 1>(p, st) : launch_p<E, HPG, 2>(p, st);
   return p.R <= 1 ? launch_t<E, HPG, 1>(p, st) : launch_t<E, HPG, 2>(p, st);
 }
