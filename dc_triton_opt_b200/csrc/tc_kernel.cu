@@ -460,15 +460,28 @@ struct WarpRoles {
   int nwarps, ncw, nslots, epi_leader;
 };
 
-static WarpRoles make_roles(int nkt, int rlast, int CS) {
+// A second key tile of at most 32 rows would put all its keys in TMEM lane
+// quarter 0 and so all its compose warps on one SM sub-partition (a warp reads
+// only the lane quarter of its index mod 4), doubling that sub-partition's
+// share of the composition.  Instead its K rows are loaded four times (rows
+// 0, 32, 64, 96 of the MMA operand): every lane quarter then holds all its
+// keys, and one warp per quarter composes one quarter of the columns.
+// (At 8 heads per group the extra K loads cost more than the balance gains.)
+__host__ __device__ inline bool replicated_last(int nkt, int rlast, int hpg) {
+  return nkt == 2 && rlast <= 32 && hpg <= 4;
+}
+
+static WarpRoles make_roles(int nkt, int rlast, int CS, int hpg) {
   WarpRoles r;
   for (int i = 0; i < 32; ++i) r.role[i] = ROLE_IDLE;
   bool used[32] = {false};
+  const bool rep = replicated_last(nkt, rlast, hpg);
   const int nq_last = (rlast + 31) / 32;
   r.ncw = 0;
   for (int kt = 0; kt < nkt; ++kt) {
-    const int nq = kt < nkt - 1 ? 4 : nq_last;
-    for (int cs = 0; cs < CS; ++cs)
+    const bool rk = rep && kt == nkt - 1;  // one warp per quarter, one column group each
+    const int nq = kt < nkt - 1 || rk ? 4 : nq_last;
+    for (int cs = 0; cs < (rk ? 1 : CS); ++cs)
       for (int sub = 0; sub < nq; ++sub) {
         int w = sub;
         while (used[w]) w += 4;
@@ -568,7 +581,8 @@ __global__ void __launch_bounds__(32 * NW, 1)
   const int rows_of[2] = {nkt == 1 ? rlast : KT_ROWS, rlast};
   // K/V jobs of one tile: one per (key tile, head), except that the short last
   // key tile of all heads is packed into a single job when it fits one slot
-  const bool packed_last = HPG > 1 && HPG * rlast * 256 <= TILE_BYTES;
+  const bool rep_last = replicated_last(nkt, rlast, HPG);
+  const bool packed_last = !rep_last && HPG > 1 && HPG * rlast * 256 <= TILE_BYTES;
   const int nK = HPG * (nkt - 1) + (packed_last ? 1 : HPG);
   struct Job { int kt, h0, nh, rows, half; };  // half: byte distance of the d-halves
   auto job_of = [&](int jj) {
@@ -641,13 +655,14 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const bool last = jb.kt == nkt - 1;
       const CUtensorMap *m = isv ? (last ? &tm_vl : &tm_v) : (last ? &tm_kl : &tm_k);
       const int kb = q0 - p.window + 1;
-      if (lane == 0) ptx::mbar_expect_tx(bar_full + slot, jb.nh * jb.rows * 256);
+      const int ncopy = (!isv && last && rep_last) ? 4 : 1;  // K rows at 0, 32, 64, 96 (see replicated_last)
+      if (lane == 0) ptx::mbar_expect_tx(bar_full + slot, ncopy * jb.nh * jb.rows * 256);
       __syncwarp();
       unsigned char *dst = smem + geo.ring_off + slot * TILE_BYTES;
-      if (lane < 2 * jb.nh) {
-        const int u = lane >> 1, c = lane & 1;
-        ptx::tma_load_4d(dst + u * 2 * jb.half + c * jb.half, m, bar_full + slot, c * 64, g * HPG + jb.h0 + u,
-                         kb + jb.kt * KT_ROWS, b);
+      if (lane < 2 * jb.nh * ncopy) {
+        const int c = lane & 1, u = (lane >> 1) % jb.nh, r = (lane >> 1) / jb.nh;
+        ptx::tma_load_4d(dst + u * 2 * jb.half + c * jb.half + r * 32 * 128, m, bar_full + slot, c * 64,
+                         g * HPG + jb.h0 + u, kb + jb.kt * KT_ROWS, b);
       }
       __syncwarp();
       ++job;
@@ -803,12 +818,16 @@ __global__ void __launch_bounds__(32 * NW, 1)
   } else if (role != ROLE_IDLE) {
     // ================================================= compose warps
     const int sub = role & 3, kt = role >> 3, cs = (role >> 2) & 1;
-    const int rw = kt * 4 + sub;
+    // a warp of the replicated last key tile: its quarter holds keys 0..31 of
+    // the tile, it composes column group `sub` (one reduction slot, disjoint columns)
+    const bool rk = rep_last && kt == nkt - 1;
+    const int rw = kt * 4 + (rk ? 0 : sub);
     int cord = 0;  // ordinal of this compose warp among the compose warps
     for (int w = 0; w < warp; ++w) cord += roles.role[w] < 0x40;
     const int ctid = cord * 32 + lane;  // compose-local thread index
-    const int g_begin = cs * (NG / CS), g_end = g_begin + NG / CS;
-    const int s_local = 32 * sub + lane;
+    const int g_begin = rk ? sub : cs * (NG / CS), g_end = rk ? sub + 1 : g_begin + NG / CS;
+    const int srow0 = rk ? 0 : 32 * sub;  // first key row of this warp's lanes
+    const int s_local = srow0 + lane;
     const int rows_kt = rows_of[kt];
     const float sl2e = p.scale * kLog2e;
     float *redm = red, *reds = red + 4 * nkt * NQ;
@@ -859,9 +878,9 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const int slen = p.seq_lens ? min(max(p.seq_lens[b], 0), T) : T;
       const int s = kb + kt * KT_ROWS + s_local;
       const bool key_ok = s >= 0 && s < slen && s_local < rows_kt;
-      const int wk0 = kb + kt * KT_ROWS + 32 * sub, wk1 = wk0 + 31;
+      const int wk0 = kb + kt * KT_ROWS + srow0, wk1 = wk0 + 31;
       const int khi = min(q0 + BM - 1, slen - 1);
-      const bool active = wk1 >= max(0, kb) && wk0 <= khi && 32 * sub < rows_kt;
+      const bool active = wk1 >= max(0, kb) && wk0 <= khi && srow0 < rows_kt;
       const int64_t ktok = (int64_t)b * T + s;
       const uint32_t tl = tbase + (static_cast<uint32_t>(32 * sub) << 16) + buf * 256 + kt * KT_ROWS;
       auto valid = [&](int t) { return key_ok && s <= t && t - s < p.window && t < T; };
@@ -1135,7 +1154,7 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
   tp.err_flag = p.err_flag;
   tp.pre = to_ptrs(p.pre);
   tp.post = to_ptrs(p.post);
-  const WarpRoles roles = make_roles(nkt, rlast, CS);
+  const WarpRoles roles = make_roles(nkt, rlast, CS, HPG);
   // the compose threads prefetch the next tile's per-query records, at most
   // 4 each (MAXREC in the kernel); otherwise run the per-tile kernel
   if (2 * BM * round_up(HPG * (2 * R + 1), 4) > 4 * 32 * roles.ncw) return launch_t<E, HPG, R>(p, st);
