@@ -463,9 +463,10 @@ struct WarpRoles {
 // A second key tile of at most 32 rows would put all its keys in TMEM lane
 // quarter 0 and so all its compose warps on one SM sub-partition (a warp reads
 // only the lane quarter of its index mod 4), doubling that sub-partition's
-// share of the composition.  Instead its K rows are loaded four times (rows
-// 0, 32, 64, 96 of the MMA operand): every lane quarter then holds all its
-// keys, and one warp per quarter composes one quarter of the columns.
+// share of the composition.  Instead its K rows are loaded to rows 64 and 96
+// of the MMA operand: lane quarters 2 and 3 hold its keys, and one warp in
+// each composes half of its columns.  Quarters 0 and 1 are left out because
+// their sub-partitions also run the TMA and MMA warps.
 // (At 8 heads per group the extra K loads cost more than the balance gains.)
 __host__ __device__ inline bool replicated_last(int nkt, int rlast, int hpg) {
   return nkt == 2 && rlast <= 32 && hpg <= 4;
@@ -479,10 +480,10 @@ static WarpRoles make_roles(int nkt, int rlast, int CS, int hpg) {
   const int nq_last = (rlast + 31) / 32;
   r.ncw = 0;
   for (int kt = 0; kt < nkt; ++kt) {
-    const bool rk = rep && kt == nkt - 1;  // one warp per quarter, one column group each
+    const bool rk = rep && kt == nkt - 1;  // one warp in quarters 2 and 3, two column groups each
     const int nq = kt < nkt - 1 || rk ? 4 : nq_last;
     for (int cs = 0; cs < (rk ? 1 : CS); ++cs)
-      for (int sub = 0; sub < nq; ++sub) {
+      for (int sub = rk ? 2 : 0; sub < nq; ++sub) {
         int w = sub;
         while (used[w]) w += 4;
         used[w] = true;
@@ -655,13 +656,14 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const bool last = jb.kt == nkt - 1;
       const CUtensorMap *m = isv ? (last ? &tm_vl : &tm_v) : (last ? &tm_kl : &tm_k);
       const int kb = q0 - p.window + 1;
-      const int ncopy = (!isv && last && rep_last) ? 4 : 1;  // K rows at 0, 32, 64, 96 (see replicated_last)
+      const int ncopy = (!isv && last && rep_last) ? 2 : 1;  // K rows at 64 and 96 (see replicated_last)
       if (lane == 0) ptx::mbar_expect_tx(bar_full + slot, ncopy * jb.nh * jb.rows * 256);
       __syncwarp();
       unsigned char *dst = smem + geo.ring_off + slot * TILE_BYTES;
       if (lane < 2 * jb.nh * ncopy) {
         const int c = lane & 1, u = (lane >> 1) % jb.nh, r = (lane >> 1) / jb.nh;
-        ptx::tma_load_4d(dst + u * 2 * jb.half + c * jb.half + r * 32 * 128, m, bar_full + slot, c * 64,
+        ptx::tma_load_4d(dst + u * 2 * jb.half + c * jb.half + (ncopy > 1 ? (r + 2) * 32 * 128 : 0), m,
+                         bar_full + slot, c * 64,
                          g * HPG + jb.h0 + u, kb + jb.kt * KT_ROWS, b);
       }
       __syncwarp();
@@ -818,14 +820,15 @@ __global__ void __launch_bounds__(32 * NW, 1)
   } else if (role != ROLE_IDLE) {
     // ================================================= compose warps
     const int sub = role & 3, kt = role >> 3, cs = (role >> 2) & 1;
-    // a warp of the replicated last key tile: its quarter holds keys 0..31 of
-    // the tile, it composes column group `sub` (one reduction slot, disjoint columns)
+    // a warp of the replicated last key tile: its quarter (2 or 3) holds keys
+    // 0..31 of the tile, it composes column groups 2 (sub - 2) and the next
+    // (one reduction slot, disjoint columns)
     const bool rk = rep_last && kt == nkt - 1;
     const int rw = kt * 4 + (rk ? 0 : sub);
     int cord = 0;  // ordinal of this compose warp among the compose warps
     for (int w = 0; w < warp; ++w) cord += roles.role[w] < 0x40;
     const int ctid = cord * 32 + lane;  // compose-local thread index
-    const int g_begin = rk ? sub : cs * (NG / CS), g_end = rk ? sub + 1 : g_begin + NG / CS;
+    const int g_begin = rk ? 2 * (sub - 2) : cs * (NG / CS), g_end = g_begin + (rk ? 2 : NG / CS);
     const int srow0 = rk ? 0 : 32 * sub;  // first key row of this warp's lanes
     const int s_local = srow0 + lane;
     const int rows_kt = rows_of[kt];
@@ -1158,7 +1161,9 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
   // the compose threads prefetch the next tile's per-query records, at most
   // 4 each (MAXREC in the kernel); otherwise run the per-tile kernel
   if (2 * BM * round_up(HPG * (2 * R + 1), 4) > 4 * 32 * roles.ncw) return launch_t<E, HPG, R>(p, st);
-  auto kern = roles.nwarps <= 18 ? dc_tcp_kernel<E, HPG, R, CS, 18> : dc_tcp_kernel<E, HPG, R, CS, 22>;
+  auto kern = roles.nwarps <= 16   ? dc_tcp_kernel<E, HPG, R, CS, 16>
+              : roles.nwarps <= 18 ? dc_tcp_kernel<E, HPG, R, CS, 18>
+                                   : dc_tcp_kernel<E, HPG, R, CS, 22>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   const int ntiles = (p.T + BM - 1) / BM * p.B * p.G;
