@@ -311,6 +311,12 @@ Wreg.load(Wz);
       redm[rw * NQ + col_of(lane, i0)] = mine_m;
       reds[rw * NQ + col_of(lane, i0)] = mine_s;
     }
+    // the post-set weights replace the pre-set ones (dead after pass 1); issued
+    // here, their latency overlaps the column reduction and its two barriers
+    if (active) {
+      Wreg.load(Wz + HPG * HPG);
+      load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
+    }
     ptx::tmem_wait_st();
     ptx::named_bar_sync(1, ncompose);
     // combine the warps of each column: m = max_w m_w, l = sum_w s_w 2^((m_w - m) sl2e);
@@ -333,10 +339,6 @@ Wreg.load(Wz);
     if (threadIdx.x == 0) TL_STAMP(5);
 
     // ---- pass 2: normalise, post-composition, P' -> SMEM (PV B operand)
-    if (active && ok) {
-Wreg.load(Wz + HPG * HPG);
-      load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
-    }
     const float *fac = redm + rw * NQ;
     unsigned char *prow = smem + geo.p_off + (s_local & 7) * 16 + (s_local >> 3) * (BM * 16);
 #pragma unroll 1
@@ -970,6 +972,12 @@ __global__ void __launch_bounds__(32 * NW, 1)
         redm[rw * NQ + col_of(lane, i0)] = mine_m;
         reds[rw * NQ + col_of(lane, i0)] = mine_s;
       }
+      // post-set weights into the registers of the pre-set ones (dead after
+      // pass 1); their latency overlaps the column reduction and its barriers
+      if (active) {
+        Wreg.load(Wz + (G + g) * HPG * HPG);
+        load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
+      }
       ptx::tmem_wait_st();
       ptx::named_bar_sync(1, ncompose);
       for (int j = ctid; j < NQ; j += ncompose) {
@@ -994,10 +1002,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
       }
 
       // ---- pass 2: normalise, post-composition, P' -> SMEM
-      if (active && ok) {
-Wreg.load(Wz + (G + g) * HPG * HPG);
-        load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
-      }
       // fetch the next tile's records now (raw 16-bit); they land during pass 2
       unsigned short nrv[MAXREC];
       bool nhas[MAXREC];
