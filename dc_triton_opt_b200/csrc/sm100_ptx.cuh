@@ -238,6 +238,43 @@ template <> __device__ __forceinline__ void tmem_st<32>(uint32_t a, const float 
 }
 #undef DC_U
 
+// ---------------------------------------------------------------- paired fp32
+// Blackwell executes two fp32 lanes per instruction with the .f32x2 forms of
+// add / mul / fma (each half rounds exactly like the scalar instruction).  A
+// pair lives in one 64-bit register: x in the low word, y in the high word.
+typedef unsigned long long f2_t;
+__device__ __forceinline__ f2_t f2_pack(float x, float y) {
+  f2_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(x), "f"(y));
+  return r;
+}
+__device__ __forceinline__ f2_t f2_dup(float x) { return f2_pack(x, x); }
+__device__ __forceinline__ float f2_lo(f2_t a) {
+  float x, y;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(a));
+  return x;
+}
+__device__ __forceinline__ float f2_hi(f2_t a) {
+  float x, y;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(a));
+  return y;
+}
+__device__ __forceinline__ f2_t f2_fma(f2_t a, f2_t b, f2_t c) {
+  f2_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ f2_t f2_mul(f2_t a, f2_t b) {
+  f2_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ f2_t f2_add(f2_t a, f2_t b) {
+  f2_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
   float r;
   asm volatile("redux.sync.max.f32 %0, %1, 0xffffffff;" : "=f"(r) : "f"(v));

@@ -188,6 +188,66 @@ __device__ __forceinline__ void compose(const float (&a)[HPG], float (&o)[HPG], 
   }
 }
 
+// Paired form of compose for two queries (pair half x: query i, y: query
+// i + 1) against the thread's key, on .f32x2 instructions.  Every half
+// performs the same operations in the same order as compose, so the results
+// are bit-identical.  rec2 is the pair-interleaved record of the two queries:
+// rec2[2 j + q] = element j of query q's record.  The per-key weights and the
+// static mix are held as duplicated pairs.  The pairs need about twice the
+// registers of the scalar form: at 2 or more heads per group the persistent
+// kernel then spills and runs slower, so only the 1-head groups use it.
+template <int HPG, int R>
+struct KeyW2 {
+  ptx::f2_t kw1[HPG * R], kw2[R * HPG], kdd[HPG];
+  __device__ __forceinline__ void set(const float (&a)[HPG * R], const float (&b)[R * HPG], const float (&c)[HPG]) {
+#pragma unroll
+    for (int j = 0; j < HPG * R; ++j) { kw1[j] = ptx::f2_dup(a[j]); kw2[j] = ptx::f2_dup(b[j]); }
+#pragma unroll
+    for (int j = 0; j < HPG; ++j) kdd[j] = ptx::f2_dup(c[j]);
+  }
+};
+template <int HPG>
+struct WSrc2 {
+  const float *p;
+  __device__ __forceinline__ void load(const float *smem_wt) { p = smem_wt; }
+  __device__ __forceinline__ ptx::f2_t get(int h, int hp) const { return ptx::f2_dup(p[h * HPG + hp]); }
+};
+
+template <int HPG, int R>
+__device__ __forceinline__ void compose2(const ptx::f2_t (&a)[HPG], ptx::f2_t (&o)[HPG], const WSrc2<HPG> &W,
+                                         const float *rec2, const KeyW2<HPG, R> &K) {
+  constexpr int RF = round_up(HPG * (2 * R + 1), 4);
+  ptx::f2_t r2[RF];
+#pragma unroll
+  for (int j = 0; j < RF; j += 2) {
+    const float4 x = *reinterpret_cast<const float4 *>(rec2 + 2 * j);
+    r2[j] = ptx::f2_pack(x.x, x.y);
+    r2[j + 1] = ptx::f2_pack(x.z, x.w);
+  }
+  const ptx::f2_t *dq = r2, *qa = r2 + HPG, *qb = r2 + HPG + HPG * R;
+  ptx::f2_t aq[R], ak[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) { aq[r] = 0ull; ak[r] = 0ull; }
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) {
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      aq[r] = ptx::f2_fma(qa[h * R + r], a[h], aq[r]);
+      ak[r] = ptx::f2_fma(K.kw1[h * R + r], a[h], ak[r]);
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) {
+    ptx::f2_t x = ptx::f2_mul(ptx::f2_add(dq[h], K.kdd[h]), a[h]);
+#pragma unroll
+    for (int hp = 0; hp < HPG; ++hp)
+      if (hp != h) x = ptx::f2_fma(W.get(h, hp), a[hp], x);
+#pragma unroll
+    for (int r = 0; r < R; ++r) x = ptx::f2_fma(qb[r * HPG + h], aq[r], ptx::f2_fma(K.kw2[r * HPG + h], ak[r], x));
+    o[h] = x;
+  }
+}
+
 template <typename E>
 __device__ __forceinline__ float ld_w(const void *base, int64_t idx) {
   return to_f<E>(reinterpret_cast<const E *>(base)[idx]);

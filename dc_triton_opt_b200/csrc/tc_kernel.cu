@@ -837,9 +837,15 @@ __global__ void __launch_bounds__(32 * NW, 1)
     const float sl2e = p.scale * kLog2e;
     float *redm = red, *reds = red + 4 * nkt * NQ;
     auto col_of = [&](int L, int i0) { return (L / GI) * BM + i0 + (L % GI); };
+    // one head per group: the composition runs on paired fp32 (compose2)
+    constexpr bool PAIR = HPG == 1;
     WSrc<HPG> Wreg;
+    WSrc2<HPG> Wreg2;
+    KeyW2<HPG, R> K2;
     float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
     // per-query records of one tile: [set][query][dq | qw1 (h, r) | qw2 (r, h)],
+    // for compose2 stored pair-interleaved (queries 2p and 2p + 1 alternate
+    // element by element: [set][query / 2][element][query % 2]),
     // dq = identity + w[h,h] (the table `wdiag`, per group) + qdd[t,h].
     // A record is at most one 16-bit element of a per-token weight plus that
     // constant, so the next tile's records are prefetched as raw 16-bit
@@ -871,7 +877,12 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const int set = idx / (BM * geo.rec_floats), j = (idx % (BM * geo.rec_floats)) % geo.rec_floats;
       float v = j < HPG ? wdiag[(set * G + gg) * HPG + j] : 0.f;
       if (has) v += to_f<E>(*reinterpret_cast<const E *>(&raw));
-      dst[idx] = v;
+      if (PAIR) {
+        const int rem = idx % (BM * geo.rec_floats), i = rem / geo.rec_floats;
+        dst[idx - rem + (i >> 1) * 2 * geo.rec_floats + 2 * j + (i & 1)] = v;
+      } else {
+        dst[idx] = v;
+      }
     };
     constexpr int MAXREC = 4;  // records per compose thread (checked by the launcher)
     int it = 0;
@@ -914,13 +925,15 @@ __global__ void __launch_bounds__(32 * NW, 1)
       ptx::named_bar_sync(1, ncompose);  // staged weights / records visible, previous tile done
       const float *recb = rec + (it & 1) * nrec;
       if (active) {
-        Wreg.load(Wz + g * HPG * HPG);
+        if constexpr (PAIR) Wreg2.load(Wz + g * HPG * HPG);
+        else Wreg.load(Wz + g * HPG * HPG);
       }
       if (threadIdx.x == 0) TLP_STAMP(it, 0);
       bool ok = ptx::mbar_wait(bar_S + 2 * buf + kt, (it >> 1) & 1, WAIT);
       if (threadIdx.x == 0) TLP_STAMP(it, 1);
       if (!ok) record_err(p, ERR_TIMEOUT_S);
       ptx::tc_fence_after();
+      if (PAIR && active) K2.set(kw1, kw2, kdd);
 
       // ---- pass 1 (see dc_tc_kernel)
 #pragma unroll 1
@@ -932,15 +945,31 @@ __global__ void __launch_bounds__(32 * NW, 1)
 #pragma unroll
           for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
           ptx::tmem_wait_ld();
+          if constexpr (PAIR) {
 #pragma unroll
-          for (int ii = 0; ii < GI; ++ii) {
-            float a[HPG], o[HPG];
+            for (int ii = 0; ii < GI; ii += 2) {
+              ptx::f2_t a[HPG], o[HPG];
 #pragma unroll
-            for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
-            compose<HPG, R>(a, o, Wreg, recb + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
-            const bool vl = valid(q0 + i0 + ii);
+              for (int h = 0; h < HPG; ++h) a[h] = ptx::f2_pack(v[h][ii], v[h][ii + 1]);
+              compose2<HPG, R>(a, o, Wreg2, recb + (i0 + ii) * geo.rec_floats, K2);
+              const bool vl0 = valid(q0 + i0 + ii), vl1 = valid(q0 + i0 + ii + 1);
 #pragma unroll
-            for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : -INFINITY;
+              for (int h = 0; h < HPG; ++h) {
+                v[h][ii] = vl0 ? ptx::f2_lo(o[h]) : -INFINITY;
+                v[h][ii + 1] = vl1 ? ptx::f2_hi(o[h]) : -INFINITY;
+              }
+            }
+          } else {
+#pragma unroll
+            for (int ii = 0; ii < GI; ++ii) {
+              float a[HPG], o[HPG];
+#pragma unroll
+              for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
+              compose<HPG, R>(a, o, Wreg, recb + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+              const bool vl = valid(q0 + i0 + ii);
+#pragma unroll
+              for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : -INFINITY;
+            }
           }
 #pragma unroll
           for (int h = 0; h < HPG; ++h)
@@ -975,7 +1004,8 @@ __global__ void __launch_bounds__(32 * NW, 1)
       // post-set weights into the registers of the pre-set ones (dead after
       // pass 1); their latency overlaps the column reduction and its barriers
       if (active) {
-        Wreg.load(Wz + (G + g) * HPG * HPG);
+        if constexpr (PAIR) Wreg2.load(Wz + (G + g) * HPG * HPG);
+        else Wreg.load(Wz + (G + g) * HPG * HPG);
         load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
       }
       ptx::tmem_wait_st();
@@ -1002,6 +1032,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
       }
 
       // ---- pass 2: normalise, post-composition, P' -> SMEM
+      if (PAIR && active) K2.set(kw1, kw2, kdd);
       // fetch the next tile's records now (raw 16-bit); they land during pass 2
       unsigned short nrv[MAXREC];
       bool nhas[MAXREC];
@@ -1027,14 +1058,32 @@ __global__ void __launch_bounds__(32 * NW, 1)
 #pragma unroll
           for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
           ptx::tmem_wait_ld();
+          if constexpr (PAIR) {
 #pragma unroll
-          for (int ii = 0; ii < GI; ++ii) {
-            float a[HPG], o[HPG];
+            for (int ii = 0; ii < GI; ii += 2) {
+              ptx::f2_t a[HPG], o[HPG];
 #pragma unroll
-            for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * fac[h * BM + i0 + ii];
-            compose<HPG, R>(a, o, Wreg, recb + (BM + i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+              for (int h = 0; h < HPG; ++h) {
+                const float2 f = *reinterpret_cast<const float2 *>(fac + h * BM + i0 + ii);
+                a[h] = ptx::f2_mul(ptx::f2_pack(v[h][ii], v[h][ii + 1]), ptx::f2_pack(f.x, f.y));
+              }
+              compose2<HPG, R>(a, o, Wreg2, recb + (BM + i0 + ii) * geo.rec_floats, K2);
 #pragma unroll
-            for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
+              for (int h = 0; h < HPG; ++h) {
+                v[h][ii] = ptx::f2_lo(o[h]);
+                v[h][ii + 1] = ptx::f2_hi(o[h]);
+              }
+            }
+          } else {
+#pragma unroll
+            for (int ii = 0; ii < GI; ++ii) {
+              float a[HPG], o[HPG];
+#pragma unroll
+              for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * fac[h * BM + i0 + ii];
+              compose<HPG, R>(a, o, Wreg, recb + (BM + i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+#pragma unroll
+              for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
+            }
           }
         } else {
 #pragma unroll
