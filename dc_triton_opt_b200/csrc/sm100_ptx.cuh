@@ -249,16 +249,13 @@ __device__ __forceinline__ f2_t f2_pack(float x, float y) {
   return r;
 }
 __device__ __forceinline__ f2_t f2_dup(float x) { return f2_pack(x, x); }
-__device__ __forceinline__ float f2_lo(f2_t a) {
-  float x, y;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(a));
-  return x;
+__device__ __forceinline__ float2 f2_unpack(f2_t a) {
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(a));
+  return r;
 }
-__device__ __forceinline__ float f2_hi(f2_t a) {
-  float x, y;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(x), "=f"(y) : "l"(a));
-  return y;
-}
+__device__ __forceinline__ float f2_lo(f2_t a) { return f2_unpack(a).x; }
+__device__ __forceinline__ float f2_hi(f2_t a) { return f2_unpack(a).y; }
 __device__ __forceinline__ f2_t f2_fma(f2_t a, f2_t b, f2_t c) {
   f2_t d;
   asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));

@@ -478,6 +478,15 @@ static WarpRoles make_roles(int nkt, int rlast, int CS, int hpg) {
   WarpRoles r;
   for (int i = 0; i < 32; ++i) r.role[i] = ROLE_IDLE;
   bool used[32] = {false};
+  bool fits = true;  // every role found a warp index below 32
+  // first free index at start, start + step, ...; -1 when none is left
+  auto free_from = [&](int start, int step) {
+    int w = start;
+    while (w < 32 && used[w]) w += step;
+    if (w >= 32) { fits = false; return -1; }
+    used[w] = true;
+    return w;
+  };
   const bool rep = replicated_last(nkt, rlast, hpg);
   const int nq_last = (rlast + 31) / 32;
   r.ncw = 0;
@@ -486,19 +495,16 @@ static WarpRoles make_roles(int nkt, int rlast, int CS, int hpg) {
     const int nq = kt < nkt - 1 || rk ? 4 : nq_last;
     for (int cs = 0; cs < (rk ? 1 : CS); ++cs)
       for (int sub = rk ? 2 : 0; sub < nq; ++sub) {
-        int w = sub;
-        while (used[w]) w += 4;
-        used[w] = true;
+        const int w = free_from(sub, 4);
+        if (w < 0) continue;
         r.role[w] = static_cast<uint8_t>(kt << 3 | cs << 2 | sub);
         ++r.ncw;
       }
   }
   r.nslots = 4 * (nkt - 1) + nq_last;
   auto take = [&](uint8_t role, int quarter) {
-    int w = quarter < 0 ? 0 : quarter;
-    while (used[w]) w += quarter < 0 ? 1 : 4;
-    used[w] = true;
-    r.role[w] = role;
+    const int w = quarter < 0 ? free_from(0, 1) : free_from(quarter, 4);
+    if (w >= 0) r.role[w] = role;
     return w;
   };
   take(ROLE_TMA, -1);
@@ -508,6 +514,7 @@ static WarpRoles make_roles(int nkt, int rlast, int CS, int hpg) {
   r.nwarps = 0;
   for (int i = 0; i < 32; ++i)
     if (used[i]) r.nwarps = i + 1;
+  if (!fits) r.nwarps = 0;  // no valid table: the launcher runs the per-tile kernel
   return r;
 }
 
@@ -1213,7 +1220,8 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
   const WarpRoles roles = make_roles(nkt, rlast, CS, HPG);
   // the compose threads prefetch the next tile's per-query records, at most
   // 4 each (MAXREC in the kernel); otherwise run the per-tile kernel
-  if (2 * BM * round_up(HPG * (2 * R + 1), 4) > 4 * 32 * roles.ncw) return launch_t<E, HPG, R>(p, st);
+  if (roles.nwarps == 0 || roles.nwarps > 22 || 2 * BM * round_up(HPG * (2 * R + 1), 4) > 4 * 32 * roles.ncw)
+    return launch_t<E, HPG, R>(p, st);
   auto kern = roles.nwarps <= 16   ? dc_tcp_kernel<E, HPG, R, CS, 16>
               : roles.nwarps <= 18 ? dc_tcp_kernel<E, HPG, R, CS, 18>
                                    : dc_tcp_kernel<E, HPG, R, CS, 22>;
