@@ -307,6 +307,12 @@ def run_ours(args, cfg, world, rank, local):
     by = algo_bytes(B, T, H, D, R)
     achieved = by / (ms_step * 1e-3) / 1e9
     tflops_rank = fl_rank / (ms_step * 1e-3) / 1e12
+    strong = subset = None
+    if not args.no_extra:
+        del qh, kh, vh, host_sets, out_host
+        strong = strong_scaling_config4(world, rank, local)
+        if rank == 0:
+            subset = reference_subset(local)
     if rank != 0:
         return
     cpu = None
@@ -332,7 +338,90 @@ def run_ours(args, cfg, world, rank, local):
         "clocks": clk.summary(),
         "cpu_baseline": cpu,
     }
+    if not args.no_extra:
+        line["strong_scaling"] = strong
+        line["reference_subset"] = subset
     print(json.dumps(line), flush=True)
+
+
+def time_calls(call, steps, warmup, stream, world):
+    """Device time per call (CUDA events on `stream`, max over ranks), after warm-up."""
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(steps):
+        call()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    return max_over_ranks(ev0.elapsed_time(ev1) / steps, stream.device)
+
+
+def strong_scaling_config4(world, rank, local, steps=5, warmup=3):
+    """BASELINE config 4 (B64 T8192 W256 G1 R2) with its batch split over the
+    ranks (shard_work: contiguous batch slices, no collective): per-GPU and
+    whole-box ms and TFLOP/s, time = max over ranks."""
+    import dc_triton_opt_b200 as dc
+    from dc_triton_opt_b200.shard import shard_work
+    cfg = dict(WORKLOADS["config4"])
+    b0, b1, g0, g1 = shard_work(cfg["B"], cfg["G"], world, rank)
+    device = torch.device("cuda", local)
+    rcfg = dict(cfg, B=max(1, b1 - b0))
+    q, k, v, pre, post = make_inputs(rcfg, device, seed=4321 + rank)
+    D, W, G = cfg["D"], cfg["window"], cfg["G"]
+    out = torch.empty_like(q)
+    call = lambda: dc.dc_attn_fwd(q, k, v, pre, post, D ** -0.5, W, G, out=out)
+    ms = time_calls(call, steps, warmup, torch.cuda.current_stream(device), world)
+    fl = flops(cfg["B"], cfg["H"], D, G, cfg["R"], pairs(cfg["T"], W))
+    del q, k, v, pre, post, out
+    torch.cuda.empty_cache()
+    return {"workload": "config4", "B": cfg["B"], "T": cfg["T"], "window": W, "G": G, "R": cfg["R"],
+            "n_gpus": world, "batch_per_gpu": b1 - b0, "ms_per_step": ms,
+            "tflops_whole_box": fl / (ms * 1e-3) / 1e12, "tflops_per_gpu": fl / world / (ms * 1e-3) / 1e12,
+            "steps": steps, "warmup": warmup, "timing": "CUDA events, max over ranks"}
+
+
+# Published forward times of the reference's best kernels (H100, fp16, rank-1
+# query-wise residual terms, no static mix, no key-wise terms): BASELINE.md §1.
+PUBLISHED_H100 = {
+    "w112": {"kernel": "V4HCM (TritonDCOneKernelMixedProbs), BM16 W112, G8", "B": 8, "us": 958.0,
+             "source": "onekernel_opt_summary.md:766 (B not stated, about 8)"},
+    "w240": {"kernel": "V4HCM256 (TritonDCOneKernelMixedProbs256), BM16 W240, G8", "B": 16, "us": 4403.0,
+             "source": "fa3_dc_hopper_plan.md:294"},
+}
+
+
+def reference_subset(local, steps=10, warmup=3):
+    """This library on the exact work the reference's best kernels do (fp16,
+    B16 T4096 N32 D128, G8, the residual rank-1 weights only, windows 112 and
+    240), for comparison with their published H100 times.  The reference's
+    Triton kernels themselves cannot run on this box (see `reference_kernels`)."""
+    import dc_triton_opt_b200 as dc
+    device = torch.device("cuda", local)
+    g = torch.Generator(device=device).manual_seed(7)
+    B, T, N, D = 16, 4096, 32, 128
+    rn = lambda *sh: torch.randn(*sh, generator=g, device=device, dtype=torch.float32).to(torch.float16)
+    q, k, v = rn(B, T, N, D), rn(B, T, N, D), rn(B, T, N, D)
+    ws = [0.1 * rn(B, T, N) for _ in range(6)]
+    res = {}
+    for key, W in (("w112", 112), ("w240", 240)):
+        out = torch.empty((B, N, T, D), device=device, dtype=torch.float16)
+        call = lambda: dc.dc_attention_window_chunked_residual_grouped(q, k, v, ws, D ** -0.5, W, G=8)
+        ms = time_calls(call, steps, warmup, torch.cuda.current_stream(device), 1)
+        pub = PUBLISHED_H100[key]
+        res[key] = {"window": W, "B": B, "us_per_call": ms * 1e3,
+                    "qk_pv_tflops": 4 * D * N * B * pairs(T, W) / (ms * 1e-3) / 1e12,
+                    "published_h100": pub,
+                    "published_h100_us_scaled_to_B16": pub["us"] * B / pub["B"]}
+        del out
+    res["dtype"] = "fp16"
+    res["reference_kernels"] = (
+        "unavailable on the GPU box: the reference tree is not an installable package (no setup.py or "
+        "pyproject at its root), and its sources may not be copied into this repository")
+    return res
 
 
 def main():
@@ -348,6 +437,8 @@ def main():
     ap.add_argument("--T", type=int, default=None)
     ap.add_argument("--kernel", default="auto", choices=["auto", "simt", "tc", "tcs", "tcm"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-extra", action="store_true",
+                    help="skip the config-4 strong-scaling and reference-subset blocks")
     args = ap.parse_args()
     cfg = dict(WORKLOADS[args.workload])
     for k in ("G", "window", "B", "T"):

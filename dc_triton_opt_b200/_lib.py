@@ -12,15 +12,19 @@ import threading
 
 PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(PKG, "libdcattn.so")
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 DC_DTYPE_BF16, DC_DTYPE_FP16 = 0, 1
 DC_KERNEL_AUTO, DC_KERNEL_SIMT, DC_KERNEL_TC, DC_KERNEL_TCS, DC_KERNEL_TCM = 0, 1, 2, 3, 4
 KERNELS = {"auto": DC_KERNEL_AUTO, "simt": DC_KERNEL_SIMT, "tc": DC_KERNEL_TC, "tcs": DC_KERNEL_TCS, "tcm": DC_KERNEL_TCM}
 STATUS = {0: "DC_OK", -1: "DC_ERR_NULL", -2: "DC_ERR_SHAPE", -3: "DC_ERR_DTYPE",
           -4: "DC_ERR_UNSUPPORTED", -5: "DC_ERR_ALIGN", -6: "DC_ERR_LAUNCH", -7: "DC_ERR_DEVICE"}
-EXPORTS = ("dc_attn_fwd", "dc_attn_fwd_residual", "dc_attn_select_kernel",
-           "dc_attn_last_error", "dc_attn_abi_version", "dc_attn_params_size")
+DC_TEST_SKIP_LOADS = 1
+DEV_ERRORS = {0: "DC_DEV_OK", 1: "DC_DEV_ERR_TIMEOUT_Q", 2: "DC_DEV_ERR_TIMEOUT_FULL",
+              3: "DC_DEV_ERR_TIMEOUT_FREE", 4: "DC_DEV_ERR_TIMEOUT_S", 5: "DC_DEV_ERR_TIMEOUT_P",
+              6: "DC_DEV_ERR_TIMEOUT_O"}
+EXPORTS = ("dc_attn_fwd", "dc_attn_fwd_residual", "dc_attn_select_kernel", "dc_attn_read_error",
+           "dc_attn_last_kernel", "dc_attn_last_error", "dc_attn_abi_version", "dc_attn_params_size")
 
 
 class DcTerms(ctypes.Structure):
@@ -39,7 +43,8 @@ class DcAttnParams(ctypes.Structure):
                 ("q", ctypes.c_void_p), ("k", ctypes.c_void_p), ("v", ctypes.c_void_p),
                 ("out", ctypes.c_void_p), ("out_sb", ctypes.c_int64), ("out_st", ctypes.c_int64),
                 ("out_sh", ctypes.c_int64), ("seq_lens", ctypes.c_void_p),
-                ("err_flag", ctypes.c_void_p), ("pre", DcTerms), ("post", DcTerms)]
+                ("err_flag", ctypes.c_void_p), ("pre", DcTerms), ("post", DcTerms),
+                ("wait_us", ctypes.c_uint32), ("test_flags", ctypes.c_int32)]
 
 
 _lib = None
@@ -63,6 +68,10 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.dc_attn_select_kernel.restype = ctypes.c_int
         lib.dc_attn_last_error.argtypes = []
         lib.dc_attn_last_error.restype = ctypes.c_char_p
+        lib.dc_attn_read_error.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p]
+        lib.dc_attn_read_error.restype = ctypes.c_int
+        lib.dc_attn_last_kernel.argtypes = []
+        lib.dc_attn_last_kernel.restype = ctypes.c_int
         lib.dc_attn_abi_version.restype = ctypes.c_int
         lib.dc_attn_params_size.restype = ctypes.c_int
         vp, i64, i32 = ctypes.c_void_p, ctypes.c_int64, ctypes.c_int32

@@ -20,6 +20,7 @@ raises through ``TORCH_CHECK``, which surfaces as ``RuntimeError`` too).
 from __future__ import annotations
 
 import ctypes
+import warnings
 from dataclasses import dataclass, fields
 from typing import Optional, Sequence
 
@@ -107,7 +108,8 @@ def dc_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                 pre: Optional[DCTerms] = None, post: Optional[DCTerms] = None,
                 scaling: Optional[float] = None, window: Optional[int] = None, G: int = 1,
                 seq_lens: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                kernel: str = "auto") -> torch.Tensor:
+                kernel: str = "auto", check: bool = False, wait_us: int = 0,
+                test_flags: int = 0) -> torch.Tensor:
     """General DC-attention forward.  q,k,v [B,T,H,D] (bf16 or fp16) -> [B,T,H,D].
 
     ``window=None`` is full causal; otherwise key s is visible from query t iff
@@ -115,6 +117,12 @@ def dc_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     attention).  ``out`` may be any tensor whose last dim is contiguous and whose
     [b,t,h] strides are positive (e.g. a [B,N,T,D] tensor permuted to
     [B,T,N,D]); it is written in place and returned.
+
+    Every wait inside the kernels is bounded (``wait_us``, default 2 s); a wait
+    that runs out makes the kernel skip the rest of its work and write a code
+    to the device error word.  ``check=True`` synchronises with the stream and
+    raises ``RuntimeError`` if that happened (otherwise read it later with
+    :func:`device_error`).  ``test_flags`` is for tests only.
     """
     _check(q.dim() == 4, f"q must be [B,T,H,D] (got {list(q.shape)})")
     _check(k.shape == q.shape and v.shape == q.shape, "k and v must match q's shape")
@@ -151,26 +159,104 @@ def dc_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         p.seq_lens = seq_lens.data_ptr()
     p.pre = _terms_struct(pre, "pre", B, T, H, G, R, dtype, device, keep)
     p.post = _terms_struct(post, "post", B, T, H, G, R, dtype, device, keep)
+    _check(0 <= int(wait_us) < 2 ** 32, "wait_us must be in [0, 2^32)")
+    p.wait_us = int(wait_us)
+    p.test_flags = int(test_flags)
     lib = _lib.load()
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
         _lib.check(lib.dc_attn_fwd(ctypes.byref(p), ctypes.c_void_p(stream)))
+        if kernel == "auto" and lib.dc_attn_last_kernel() == _lib.DC_KERNEL_SIMT:
+            _warn_simt(T, H, D, G, R, window, pre, post)
+        if check:
+            _raise_device_error(lib, stream)
     # Converted temporaries in `keep` may be freed on return: the caching
     # allocator only hands their blocks to later work on this same stream.
     return out
 
 
+_SIMT_WARNED = set()
+
+
+def _warn_simt(T, H, D, G, R, window, pre, post):
+    """One warning per distinct request shape that AUTO had to run on the
+    CUDA-core kernel (two orders of magnitude slower than the tensor-core ones)."""
+    has_qmat = any(tm is not None and tm.qmat is not None for tm in (pre, post))
+    key = (T, H, D, G, R, window, has_qmat)
+    if key in _SIMT_WARNED:
+        return
+    _SIMT_WARNED.add(key)
+    why = ("per-query mixing matrices (qmat)" if has_qmat else
+           f"D={D}, heads per group={H // G}, R={R}, window={window}")
+    warnings.warn(f"dc_attn_fwd: no tensor-core kernel supports this call ({why}); "
+                  "it runs on the CUDA-core kernel, which is much slower", RuntimeWarning, stacklevel=3)
+
+
+def _raise_device_error(lib, stream):
+    code = lib.dc_attn_read_error(None, 1, ctypes.c_void_p(stream))
+    if code < 0:
+        _lib.check(code, "dc_attn_read_error")
+    if code > 0:
+        raise RuntimeError(f"dc_attn_fwd: device error {_lib.DEV_ERRORS.get(code, code)} "
+                           "(a wait inside the kernel ran out; the output is not valid)")
+
+
+def device_error(device=None, clear: bool = True) -> int:
+    """Code in the library's device error word of ``device`` (0 = none) after
+    the work queued so far on its current stream (this synchronises with that
+    stream).  Non-zero means a kernel's bounded wait ran out and that launch's
+    output is not valid; ``clear`` resets the word."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device).cuda_stream
+        code = lib.dc_attn_read_error(None, 1 if clear else 0, ctypes.c_void_p(stream))
+    if code < 0:
+        _lib.check(code, "dc_attn_read_error")
+    return code
+
+
 _PER_TOKEN = ("qw1", "qw2", "kw1", "kw2", "qdd", "kdd", "qmat")
-_host_ws = {}  # (device, name, shape, dtype) -> device buffer reused across calls
 
 
-def _ws(device, name, shape, dtype):
-    key = (device, name, tuple(shape), dtype)
-    buf = _host_ws.get(key)
-    if buf is None:
-        buf = torch.empty(shape, device=device, dtype=dtype)
-        _host_ws[key] = buf
-    return buf
+class _HostWorkspace:
+    """Device staging buffers of :func:`dc_attn_fwd_host` for one device: two
+    slots of inputs and output, the copy streams, and per slot the events of
+    its last use.  The events are kept across calls, so a call never
+    overwrites a slot that an earlier call's forward or copy-back still uses.
+    One buffer set per device is retained (two batch slices of q, k, v, out and
+    the per-token weights); a call with other slice shapes first waits for the
+    old buffers' last use, then replaces them."""
+
+    def __init__(self, device):
+        self.device = device
+        self.key = None
+        self.bufs = {}
+        self.ev_comp = [None, None]  # slot's inputs / output buffer in use by a forward until then
+        self.ev_out = [None, None]   # slot's output copied back to the host
+        self.slot = 0
+        self.s_in = torch.cuda.Stream(device)
+        self.s_out = torch.cuda.Stream(device)
+
+    def reset(self, key):
+        if key == self.key:
+            return
+        for ev in self.ev_comp + self.ev_out:
+            if ev is not None:
+                ev.synchronize()
+        self.bufs.clear()
+        self.ev_comp, self.ev_out = [None, None], [None, None]
+        self.key = key
+
+    def buf(self, slot, name, shape, dtype):
+        b = self.bufs.get((slot, name))
+        if b is None:
+            b = torch.empty(shape, device=self.device, dtype=dtype)
+            self.bufs[(slot, name)] = b
+        return b
+
+
+_host_ws = {}  # device -> _HostWorkspace
 
 
 def dc_attn_fwd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
@@ -203,8 +289,15 @@ def dc_attn_fwd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     nch = max(1, min(int(chunks), B))
     cb = -(-B // nch)
     comp = torch.cuda.current_stream(device)
-    s_in, s_out = torch.cuda.Stream(device), torch.cuda.Stream(device)
-    # static mixes (small) go to the device once
+    ws = _host_ws.get(device)
+    if ws is None:
+        ws = _host_ws[device] = _HostWorkspace(device)
+    tok_shapes = tuple((side, f, tuple(getattr(tm, f).shape[1:]), getattr(tm, f).dtype)
+                       for side, tm in (("pre", pre), ("post", post)) if tm is not None
+                       for f in _PER_TOKEN if getattr(tm, f) is not None)
+    ws.reset((cb, T, H, D, dtype, tok_shapes))
+    s_in, s_out = ws.s_in, ws.s_out
+    # static mixes (small) go to the device once per call
     w_dev = {}
     for side, tm in (("pre", pre), ("post", post)):
         if tm is not None and tm.w is not None:
@@ -212,24 +305,24 @@ def dc_attn_fwd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     sl_dev = None
     if seq_lens is not None:
         sl_dev = seq_lens.to(device=device, dtype=torch.int32, non_blocking=True)
-    ev_comp = [None, None]  # per buffer slot: forward finished (inputs and output buffer in use until then)
-    ev_out = [None, None]   # per buffer slot: output copied back
     last = None
     with torch.cuda.device(device):
         for c in range(nch):
             b0, b1 = c * cb, min(B, (c + 1) * cb)
             if b0 >= b1:
                 break
-            n, slot = b1 - b0, c % 2
+            n, slot = b1 - b0, ws.slot
+            ws.slot ^= 1
 
             def dev(name, t):
-                buf = _ws(device, f"{slot}.{name}", (cb,) + tuple(t.shape[1:]), t.dtype)[:n]
+                buf = ws.buf(slot, name, (cb,) + tuple(t.shape[1:]), t.dtype)[:n]
                 buf.copy_(t[b0:b1], non_blocking=True)
                 return buf
 
             with torch.cuda.stream(s_in):
-                if ev_comp[slot] is not None:
-                    s_in.wait_event(ev_comp[slot])
+                # the slot's previous forward (of this call or an earlier one) has read its inputs
+                if ws.ev_comp[slot] is not None:
+                    s_in.wait_event(ws.ev_comp[slot])
                 dq, dk, dv = dev("q", q), dev("k", k), dev("v", v)
                 terms = {}
                 for side, tm in (("pre", pre), ("post", post)):
@@ -244,19 +337,20 @@ def dc_attn_fwd_host(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                 ev_in = torch.cuda.Event()
                 ev_in.record(s_in)
             comp.wait_event(ev_in)
-            if ev_out[slot] is not None:
-                comp.wait_event(ev_out[slot])
-            dout = _ws(device, f"{slot}.out", (cb, T, H, D), dtype)[:n]
+            if ws.ev_out[slot] is not None:
+                comp.wait_event(ws.ev_out[slot])  # the slot's previous output has been copied back
+            dout = ws.buf(slot, "out", (cb, T, H, D), dtype)[:n]
             dc_attn_fwd(dq, dk, dv, terms["pre"], terms["post"], scaling, window, G,
                         None if sl_dev is None else sl_dev[b0:b1], out=dout, kernel=kernel)
-            ev_comp[slot] = torch.cuda.Event()
-            ev_comp[slot].record(comp)
+            ev = torch.cuda.Event()
+            ev.record(comp)
+            ws.ev_comp[slot] = ev
             with torch.cuda.stream(s_out):
-                s_out.wait_event(ev_comp[slot])
+                s_out.wait_event(ev)
                 out[b0:b1].copy_(dout, non_blocking=True)
-                ev_out[slot] = torch.cuda.Event()
-                ev_out[slot].record(s_out)
-                last = ev_out[slot]
+                ev_o = torch.cuda.Event()
+                ev_o.record(s_out)
+                ws.ev_out[slot] = last = ev_o
         if last is not None:
             comp.wait_event(last)
     return out

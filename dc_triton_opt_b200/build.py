@@ -9,6 +9,7 @@ git-ignored but travel with the source tree to the GPU host).
 
 from __future__ import annotations
 
+import concurrent.futures
 import os
 import subprocess
 import sys
@@ -49,16 +50,20 @@ def build(force: bool = False, verbose: bool = False) -> str:
     os.makedirs(objdir, exist_ok=True)
     headers = [os.path.join(CSRC, f) for f in os.listdir(CSRC) if f.endswith((".cuh", ".h"))]
     headers.append(os.path.join(ROOT, "include", "dc_attn.h"))
-    objs = []
+    objs, cmds = [], []
     for src in SOURCES:
         s = os.path.join(CSRC, src)
         o = os.path.join(objdir, src.replace(".cu", ".o"))
         objs.append(o)
         if force or _stale(o, [s] + headers):
-            cmd = [NVCC, *nvcc_flags(), "-c", s, "-o", o]
+            cmds.append([NVCC, *nvcc_flags(), "-c", s, "-o", o])
+    # the translation units are independent: compile them concurrently
+    with concurrent.futures.ThreadPoolExecutor(max_workers=max(1, min(len(cmds), os.cpu_count() or 1))) as ex:
+        for cmd in cmds:
             if verbose:
                 print(" ".join(cmd), flush=True)
-            subprocess.run(cmd, check=True)
+        for f in [ex.submit(subprocess.run, cmd, check=True) for cmd in cmds]:
+            f.result()
     if force or _stale(LIB, objs):
         cmd = [NVCC, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", *objs, "-o", LIB,
                "-lcuda", "-Xcompiler", "-fPIC"]

@@ -24,9 +24,29 @@ bool tcm_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tcm(const dc_attn_params &p, cudaStream_t st);
 }  // namespace dcattn
 
+// The library's own device error word, used when a caller passes no
+// err_flag: one int32 per device that loads the library (static device
+// memory, no allocation).  Host code must not take its address directly; the
+// device address comes from cudaGetSymbolAddress on the current device.
+static __device__ int32_t g_err_word;
+
 namespace {
 
 thread_local std::string g_last_error;
+thread_local int g_last_kernel = 0;
+
+// Device address of g_err_word on the current device (looked up once per device).
+int32_t *default_err_word() {
+  static int32_t *addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  if (!addr[dev]) {
+    void *p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_err_word) != cudaSuccess) return nullptr;
+    addr[dev] = static_cast<int32_t *>(p);
+  }
+  return addr[dev];
+}
 
 int fail(int code, const char *fmt, ...) __attribute__((format(printf, 2, 3)));
 int fail(int code, const char *fmt, ...) {
@@ -130,10 +150,13 @@ int dc_attn_select_kernel(const dc_attn_params *p) {
 int dc_attn_fwd(const dc_attn_params *pp, void *stream) {
   int rc = validate(pp);
   if (rc != DC_OK) return rc;
-  const dc_attn_params &p = *pp;
+  dc_attn_params p = *pp;
   const int which = select_kernel(p);
   if (which < 0) return which;
   if ((rc = check_device()) != DC_OK) return rc;
+  if (!p.err_flag && !(p.err_flag = default_err_word()))
+    return fail(DC_ERR_DEVICE, "cannot resolve the library's device error word");
+  if (p.wait_us == 0) p.wait_us = 2000000u;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e;
   if (which == DC_KERNEL_TC) {
@@ -148,7 +171,25 @@ int dc_attn_fwd(const dc_attn_params *pp, void *stream) {
   if (e != cudaSuccess)
     return fail(DC_ERR_LAUNCH, "kernel launch failed: %s", cudaGetErrorString(e));
   g_last_error.clear();
+  g_last_kernel = which;
   return DC_OK;
+}
+
+int dc_attn_last_kernel(void) { return g_last_kernel; }
+
+int dc_attn_read_error(int32_t *err_flag, int clear, void *stream) {
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int32_t *word = err_flag ? err_flag : default_err_word();
+  if (!word) return fail(DC_ERR_DEVICE, "cannot resolve the library's device error word");
+  int32_t code = 0;
+  cudaError_t e = cudaMemcpyAsync(&code, word, sizeof(code), cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && clear && code != 0) {
+    e = cudaMemsetAsync(word, 0, sizeof(int32_t), st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  }
+  if (e != cudaSuccess) return fail(DC_ERR_LAUNCH, "reading the device error word failed: %s", cudaGetErrorString(e));
+  return code;
 }
 
 int dc_attn_fwd_residual(const void *q, const void *k, const void *v, const void *pre_w1, const void *pre_w2,

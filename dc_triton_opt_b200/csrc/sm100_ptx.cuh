@@ -61,11 +61,12 @@ __device__ __forceinline__ uint64_t globaltimer_ns() {
 }
 
 // Wait for the phase with the given parity to complete.  Gives up (returns
-// false) after about `limit` / 8 microseconds of wall-clock time (default
-// ~2 s): every wait of the kernels is bounded.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit = (1u << 24)) {
+// false) after `limit_us` microseconds of wall-clock time: every wait of the
+// kernels is bounded, and the caller records an error code and skips the
+// work that depended on it.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32_t limit_us) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t deadline = globaltimer_ns() + (static_cast<uint64_t>(limit) >> 3) * 1000ull;
+  const uint64_t deadline = globaltimer_ns() + static_cast<uint64_t>(limit_us) * 1000ull;
   while (!mbar_try_wait_sleep(bar, parity, 20000)) {
     if (globaltimer_ns() > deadline) return false;
   }

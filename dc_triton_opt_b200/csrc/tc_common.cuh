@@ -66,55 +66,16 @@ struct TcParams {
   void *out;
   int64_t out_sb, out_st, out_sh;
   int32_t *err_flag;
+  uint32_t wait_us;  // limit of every mbarrier wait (microseconds)
+  int32_t skip_loads;  // testing: the TMA producer issues nothing (waits run out)
   TermPtrs pre, post;
 };
 
-static __device__ int g_default_err;
-
-#ifdef DC_TIMELINE
-// development builds only: clock64 stamps of the phases (per CTA; the
-// persistent kernel records CTA 0 per tile iteration)
-__device__ unsigned long long g_timeline[8192][40];
-#define TLP_STAMP(it, i)                                                 \
-  do {                                                                   \
-    if (blockIdx.x == 0 && (it) < 8192) g_timeline[(it)][i] = clock64(); \
-  } while (0)
-#define TL_STAMP(i)                                                                   \
-  do {                                                                                \
-    const int cta_ = blockIdx.y * gridDim.x + blockIdx.x;                             \
-    if (cta_ < 8192) g_timeline[cta_][i] = clock64();                                 \
-  } while (0)
-#define TL_VAL(i, v)                                                                  \
-  do {                                                                                \
-    const int cta_ = blockIdx.y * gridDim.x + blockIdx.x;                             \
-    if (cta_ < 8192) g_timeline[cta_][i] = (v);                                       \
-  } while (0)
-#define TL_CLK() clock64()
-// per-job times of one CTA (development builds): [0] producer issue, [1] consumer ready
-__device__ long long g_jobt[2][256];
-#define TL_JOB(k, j)                                                                      \
-  do {                                                                                    \
-    if (blockIdx.x == 5 && blockIdx.y == 0 && (j) < 256) g_jobt[k][j] = clock64();        \
-  } while (0)
-#else
-#define TL_VAL(i, v) \
-  do {               \
-  } while (0)
-#define TL_CLK() 0ll
-#define TL_JOB(k, j) \
-  do {               \
-  } while (0)
-#define TLP_STAMP(it, i) \
-  do {                   \
-  } while (0)
-#define TL_STAMP(i) \
-  do {              \
-  } while (0)
-#endif  // error sink when the caller passes no err_flag
-
+// A bounded wait that ran out writes its code here (the first code wins).
+// err_flag is never NULL in a launch: the C layer substitutes the library's
+// per-device error word when the caller passes none.
 __device__ __forceinline__ void record_err(const TcParams &p, int code) {
-  int *dst = p.err_flag ? p.err_flag : &g_default_err;
-  atomicCAS(dst, 0, code);
+  atomicCAS(p.err_flag, 0, code);
 }
 
 // Static head mix of a group, stored transposed with a zero diagonal:

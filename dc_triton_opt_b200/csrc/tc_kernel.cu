@@ -67,7 +67,6 @@ __global__ void __launch_bounds__(MAXT, 1)
   // [kb + 128 kt, kb + 128 kt + 128), the last tile only its first rlast rows
   const int kb = q0 - p.window + 1;
   const int slen = p.seq_lens ? min(max(p.seq_lens[b], 0), T) : T;
-  if (threadIdx.x == 0) TL_STAMP(0);
 
   if (threadIdx.x == 0) {
     ptx::mbar_init(bar_q, 1);
@@ -86,11 +85,10 @@ __global__ void __launch_bounds__(MAXT, 1)
   ptx::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
   const uint32_t o_col = KT_ROWS * nkt;
-  if (threadIdx.x == 0) TL_STAMP(1);
 
   if (warp == ctrl_warp) {
     // ================================================= TMA producer (one thread)
-    if (lane == 0) {
+    if (lane == 0 && !p.skip_loads) {
       const int nslot = geo.nslot;
       const int nK = HPG * nkt, total = 2 * nK;
       ptx::tma_prefetch_desc(&tm_q);
@@ -104,7 +102,7 @@ __global__ void __launch_bounds__(MAXT, 1)
       // jobs are key-tile major: job j -> key tile j / HPG, head j % HPG; K jobs then V jobs
       for (int j = 0; j < total; ++j) {
         const int slot = j % nslot, use = j / nslot;
-        if (use > 0 && !ptx::mbar_wait(bar_free + slot, (use - 1) & 1, 1u << 24)) {
+        if (use > 0 && !ptx::mbar_wait(bar_free + slot, (use - 1) & 1, p.wait_us)) {
           record_err(p, ERR_TIMEOUT_FREE);
           break;
         }
@@ -137,7 +135,7 @@ __global__ void __launch_bounds__(MAXT, 1)
     const int nK = HPG * nkt, total = 2 * nK;
     bool ok = true;
     auto wait_u = [&](uint64_t *bar, int parity, int code) {
-      const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait(bar, parity, 1u << 24));
+      const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait(bar, parity, p.wait_us));
       if (ok && !got) {
         ok = false;
         if (lane == 0) record_err(p, code);
@@ -145,12 +143,10 @@ __global__ void __launch_bounds__(MAXT, 1)
       return ok;
     };
     wait_u(bar_q, 0, ERR_TIMEOUT_Q);
-    if (lane == 0) TL_STAMP(2);
     // ---- S^T_h = K_h Q_h^T; key tile kt is signalled as soon as its heads are issued
     for (int j = 0; j < nK && ok; ++j) {
       const int slot = j % nslot;
       if (!wait_u(bar_full + slot, (j / nslot) & 1, ERR_TIMEOUT_FULL)) break;
-      if (lane == 0 && j < 12) TL_STAMP(12 + j);
       ptx::tc_fence_after();
       const int kt = j / HPG, h = j % HPG;
       const uint64_t ad = ptx::desc_add(kd0, slot * TILE_BYTES);
@@ -167,10 +163,8 @@ __global__ void __launch_bounds__(MAXT, 1)
       }
       __syncwarp();
     }
-    if (lane == 0) TL_STAMP(3);
     // ---- O^T_h = V_h^T P'^T_h, accumulated over key tiles
     if (ok) wait_u(bar_P, 0, ERR_TIMEOUT_P);
-    if (lane == 0) TL_STAMP(7);
     ptx::tc_fence_after();
     for (int j = nK; j < total && ok; ++j) {
       const int slot = j % nslot;
@@ -191,7 +185,6 @@ __global__ void __launch_bounds__(MAXT, 1)
     }
     if (ptx::elect_one()) ptx::mma_commit(bar_O);
     __syncwarp();
-    if (lane == 0) TL_STAMP(10);
   } else {
     // ================================================= compose warps
     // stage the static mix and the per-query weights (fp32) while the first loads fly
@@ -255,9 +248,8 @@ __global__ void __launch_bounds__(MAXT, 1)
     if (active) {
 Wreg.load(Wz);
     }
-    if (!ptx::mbar_wait(bar_S + kt, 0)) { ok = false; record_err(p, ERR_TIMEOUT_S); }
+    if (!ptx::mbar_wait(bar_S + kt, 0, p.wait_us)) { ok = false; record_err(p, ERR_TIMEOUT_S); }
     ptx::tc_fence_after();
-    if (threadIdx.x == 0) TL_STAMP(4);
 
     // ---- pass 1: pre-composition + mask, warp-local column max (redux), e = exp(S - m_w),
     //      warp-local column sums (shuffle transpose-reduce); e written back to TMEM
@@ -336,7 +328,6 @@ Wreg.load(Wz);
       for (int w = 0; w < 4 * nkt; ++w) redm[w * NQ + j] *= il;
     }
     ptx::named_bar_sync(1, ncompose);
-    if (threadIdx.x == 0) TL_STAMP(5);
 
     // ---- pass 2: normalise, post-composition, P' -> SMEM (PV B operand)
     const float *fac = redm + rw * NQ;
@@ -393,12 +384,10 @@ Wreg.load(Wz);
     ptx::fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(bar_P);
-    if (threadIdx.x == 0) TL_STAMP(6);
 
     // ---- epilogue: O^T (lanes = d) -> SMEM [head][d half][query][64 d] -> TMA store
-    if (!ptx::mbar_wait(bar_O, 0, 1u << 24)) { ok = false; record_err(p, ERR_TIMEOUT_O); }
+    if (!ptx::mbar_wait(bar_O, 0, p.wait_us)) { ok = false; record_err(p, ERR_TIMEOUT_O); }
     ptx::tc_fence_after();
-    if (threadIdx.x == 0) TL_STAMP(8);
     unsigned char *stage = smem + geo.q_off;  // Q is dead once every MMA has completed
     const int d = 32 * sub + lane;
     if (ok) {
@@ -428,7 +417,6 @@ Wreg.load(Wz);
 
   ptx::tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) TL_STAMP(9);
   if (warp == ctrl_warp) {
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tbase, 512);
@@ -626,7 +614,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
   __syncthreads();
   ptx::tc_fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t WAIT = 1u << 24;
+  const uint32_t WAIT = p.wait_us;
 
   // tile -> (query block, batch, group)
   auto tile_coords = [&](int tile, int &q0, int &b, int &g) {
@@ -649,7 +637,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
       ptx::tma_prefetch_desc(&tm_v);
     }
     int job = 0;
-    bool ok = true;
+    bool ok = !p.skip_loads;
     auto wait_all = [&](uint64_t *bar, int parity, int code) {
       const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait(bar, parity, WAIT));
       if (ok && !got) {
@@ -753,9 +741,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const int buf = it & 1;
       // TMEM buffer free once the epilogue of tile it-2 has read its O
       if (it >= 2 && !wait_u(bar_Ofree + buf, ((it - 2) >> 1) & 1, ERR_TIMEOUT_O)) break;
-      if (lane == 0) TLP_STAMP(it, 7);
       if (!wait_u(bar_q + buf, (it >> 1) & 1, ERR_TIMEOUT_Q)) break;
-      if (lane == 0) TLP_STAMP(it, 8);
       ptx::tc_fence_after();
       const uint64_t qd0 = ptx::smem_desc(ptx::smem_u32(smem + geo.q_off + buf * NQ * 256), 16, 1024, 2);
       for (int jj = 0; jj < nK && ok; ++jj, ++job) {
@@ -781,9 +767,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
         }
         __syncwarp();
       }
-      if (lane == 0) TLP_STAMP(it, 9);
       if (it >= 1 && ok) pv(it - 1);
-      if (lane == 0) TLP_STAMP(it, 10);
     }
     if (it >= 1 && ok) pv(it - 1);
   } else if ((role & 0xF0) == ROLE_EPI) {
@@ -794,9 +778,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
       int q0, b, g;
       tile_coords(tile, q0, b, g);
       const int buf = it & 1;
-      if (threadIdx.x == 32 * epi_warp0) TLP_STAMP(it, 4);
       if (!ptx::mbar_wait(bar_O + buf, (it >> 1) & 1, WAIT)) { record_err(p, ERR_TIMEOUT_O); break; }
-      if (threadIdx.x == 32 * epi_warp0) TLP_STAMP(it, 5);
       ptx::tc_fence_after();
       unsigned char *stage = smem + geo.q_off + buf * NQ * 256;
 #pragma unroll 1
@@ -823,7 +805,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
         ptx::bulk_commit();
         ptx::bulk_wait_read0();
         ptx::mbar_arrive(bar_Qfree + buf);
-        TLP_STAMP(it, 6);
       }
     }
   } else if (role != ROLE_IDLE) {
@@ -935,9 +916,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
         if constexpr (PAIR) Wreg2.load(Wz + g * HPG * HPG);
         else Wreg.load(Wz + g * HPG * HPG);
       }
-      if (threadIdx.x == 0) TLP_STAMP(it, 0);
       bool ok = ptx::mbar_wait(bar_S + 2 * buf + kt, (it >> 1) & 1, WAIT);
-      if (threadIdx.x == 0) TLP_STAMP(it, 1);
       if (!ok) record_err(p, ERR_TIMEOUT_S);
       ptx::tc_fence_after();
       if (PAIR && active) K2.set(kw1, kw2, kdd);
@@ -1031,7 +1010,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
         for (int w = 0; w < nslots; ++w) redm[w * NQ + j] *= il;
       }
       ptx::named_bar_sync(1, ncompose);
-      if (threadIdx.x == 0) TLP_STAMP(it, 2);
       // P' of key tile 0 overwrites Q: every QK product of this tile must be complete
       if (ok && kt == 0 && nkt > 1) {
         ok = ptx::mbar_wait(bar_S + 2 * buf + nkt - 1, (it >> 1) & 1, WAIT);
@@ -1137,7 +1115,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_P + buf);
-      if (threadIdx.x == 0) TLP_STAMP(it, 3);
     }
   }
 
@@ -1174,6 +1151,8 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   tp.out = p.out;
   tp.out_sb = p.out_sb; tp.out_st = p.out_st; tp.out_sh = p.out_sh;
   tp.err_flag = p.err_flag;
+  tp.wait_us = p.wait_us;
+  tp.skip_loads = (p.test_flags & DC_TEST_SKIP_LOADS) != 0;
   tp.pre = to_ptrs(p.pre);
   tp.post = to_ptrs(p.post);
   // short windows (<= 2 key tiles): two warps per TMEM lane quarter and key tile
@@ -1215,6 +1194,8 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
   tp.out = p.out;
   tp.out_sb = p.out_sb; tp.out_st = p.out_st; tp.out_sh = p.out_sh;
   tp.err_flag = p.err_flag;
+  tp.wait_us = p.wait_us;
+  tp.skip_loads = (p.test_flags & DC_TEST_SKIP_LOADS) != 0;
   tp.pre = to_ptrs(p.pre);
   tp.post = to_ptrs(p.post);
   const WarpRoles roles = make_roles(nkt, rlast, CS, HPG);

@@ -193,7 +193,7 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
   const int nkt = (span + KT - 1) / KT;
   const int rlast = ((span - KT * (nkt - 1)) + 15) / 16 * 16;
   const int slen = p.seq_lens ? min(max(p.seq_lens[b], 0), T) : T;
-  const uint32_t WAIT = 1u << 24;
+  const uint32_t WAIT = p.wait_us;
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < NKA; ++i) {
@@ -242,7 +242,7 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
     const int gl = lane & 15;
     const int L = isv ? NLV : NLK;
     const uint32_t gmask = isv ? (((1u << NLV) - 1) << 16) : ((1u << NLK) - 1);
-    if (gl < L) {
+    if (gl < L && !p.skip_loads) {
       if (gl == 0) {
         if (!isv) {
           ptx::tma_prefetch_desc(&tm_q);
@@ -263,7 +263,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
             if (use > 0 && !ptx::mbar_wait(freeb + slot, (use - 1) & 1, WAIT)) good = false;
             if (good) {
               ptx::mbar_expect_tx(full + slot, KJOB + (isv ? 0 : BM * 256));
-              if (!isv && ring_a) TL_JOB(0, job);
               unsigned char *dst = smem + (isv ? SH::VOFF + slot * KJOB : kslot_off(ring_a, slot));
               ptx::tma_load_5d(dst, isv ? &tm_v : &tm_k, full + slot, 0, k_lo + kt * KT, 0, hbase + h, b);
               if (!isv) ptx::tma_load_5d(dst + KJOB, &tm_q, full + slot, 0, q0, 0, hbase + h, b);
@@ -324,21 +323,18 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
     const uint64_t dp0 = ptx::smem_desc(ptx::smem_u32(smem + geo.p_off), BM * 16, 128, 0);  // P': MN-major
     const uint64_t da0 = ptx::smem_desc(ptx::smem_u32(smem + geo.a_off), 128, KB * 128, 0); // mix A: K-major
     const uint64_t db0 = ptx::smem_desc(ptx::smem_u32(smem + geo.bm_off), 128, KB * 128, 0);
-    long long w_ring = 0, w_a = 0, w_other = 0;  // timeline: cycles waited (development builds)
     bool ok = true;
-    auto wait_u = [&](uint64_t *bar, int parity, int code, long long &acc) {
-      const long long t0 = TL_CLK();
+    auto wait_u = [&](uint64_t *bar, int parity, int code) {
       const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait(bar, parity, WAIT));
       if (ok && !got) {
         ok = false;
         if (lane == 0) record_err(p, code);
       }
-      acc += TL_CLK() - t0;
     };
     // ring jobs are consumed in order: wait for a job's data, release its slot
     auto wait_jobs = [&](int job, uint64_t *full, int nslot) {
       for (int hh = 0; hh < HJ; ++hh)
-        wait_u(full + ((job + hh) % nslot), ((job + hh) / nslot) & 1, ERR_TIMEOUT_FULL, w_ring);
+        wait_u(full + ((job + hh) % nslot), ((job + hh) / nslot) & 1, ERR_TIMEOUT_FULL);
       ptx::tc_fence_after();
     };
     auto free_jobs = [&](int job, uint64_t *freeb, int nslot) {
@@ -351,7 +347,7 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
       for (int sgl = 0; sgl < NSG; ++sgl)
         for (int cs = 0; cs < 2; ++cs) {
           const int sg = cs * NSG + sgl;
-          wait_u(bar_A + sg, round & 1, ERR_TIMEOUT_P, w_a);
+          wait_u(bar_A + sg, round & 1, ERR_TIMEOUT_P);
           if (!ok) return;
           ptx::tc_fence_after();
           const uint64_t aq = ptx::desc_add(da0, sg * NQG * ATILE);
@@ -378,7 +374,7 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
       auto qk = [&](int buf, int job0, bool ring_a) {
         uint64_t *full = ring_a ? bar_afull : bar_kfull, *freeb = ring_a ? bar_afree : bar_kfree;
         const int nslot = ring_a ? NKA : NSK;
-        if (scnt[buf] >= 1) wait_u(bar_Sfree + buf, (scnt[buf] - 1) & 1, ERR_TIMEOUT_S, w_other);
+        if (scnt[buf] >= 1) wait_u(bar_Sfree + buf, (scnt[buf] - 1) & 1, ERR_TIMEOUT_S);
         ++scnt[buf];
         ++sidx;
         if (!ok) return;
@@ -386,7 +382,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
         for (int h0 = 0, job = job0; h0 < HPG; h0 += HJ, job += HJ) {
           wait_jobs(job, full, nslot);
           if (!ok) return;
-          if (lane == 0 && ring_a) TL_JOB(1, job);
           uint64_t ka[HJ], qa[HJ];
           uint32_t dd[HJ];
 #pragma unroll
@@ -407,7 +402,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
         }
         if (ptx::elect_one()) ptx::mma_commit(bar_S + buf);
         __syncwarp();
-        if (lane == 0 && sidx <= 6) TL_STAMP(28 + sidx);
       };
       // pass A: S tiles alternate between the two buffers; pass B: buffer 0
       for (int kt = 0; kt < nkt && ok; ++kt) qk(kt & 1, kt * HPG, true);
@@ -421,7 +415,7 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
     } else {
       // O^T += V^T P'^T per key tile of pass B
       for (int kt = 0; kt < nkt && ok; ++kt) {
-        wait_u(bar_P, kt & 1, ERR_TIMEOUT_P, w_other);
+        wait_u(bar_P, kt & 1, ERR_TIMEOUT_P);
         if (!ok) break;
         ptx::tc_fence_after();
         const int nks = (kt == nkt - 1 ? rlast : KT) / 16;
@@ -459,11 +453,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
       if (ptx::elect_one()) ptx::mma_commit(bar_O);
       __syncwarp();
     }
-    if (lane == 0 && warp == mma_warp) {
-      TL_VAL(35, w_ring);
-      TL_VAL(37, w_other);
-    }
-    if (lane == 0 && warp == mix_warp) TL_VAL(36, w_a);
   } else {
     // ============================================================ compose warps
     const int qtr = warp & 3, cs = warp >> 2;
@@ -511,14 +500,11 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
     ptx::named_bar_sync(1, 32 * NCW);
 
     bool ok = true;
-    long long w_comp = 0;  // timeline: cycles waited (development builds)
     auto wait_or_fail = [&](uint64_t *bar, int parity, int code) {
-      const long long t0 = TL_CLK();
       if (ok && !ptx::mbar_wait(bar, parity, WAIT)) {
         ok = false;
         record_err(p, code);
       }
-      w_comp += TL_CLK() - t0;
     };
     auto arrive = [&](uint64_t *bar) {
       ptx::fence_proxy_async_smem();
@@ -604,8 +590,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
 #pragma unroll
     for (int k = 0; k < NSG; ++k) { m_run[k][0] = m_run[k][1] = -INFINITY; l_run[k][0] = l_run[k][1] = 0.f; }
 
-    const bool tlw = warp == 0 && lane == 0;  // timeline stamps (development builds)
-    if (tlw) TL_STAMP(0);
     // ============================== pass A: statistics of the composed logits
     for (int kt = 0; kt < nkt; ++kt) {
       const int s = k_lo + kt * KT + key_local;
@@ -616,7 +600,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
       const int sbuf = kt & 1;
       wait_or_fail(bar_S + sbuf, scnt[sbuf] & 1, ERR_TIMEOUT_S);
       ptx::tc_fence_after();
-      if (tlw && kt < 3) TL_STAMP(1 + 4 * kt);
       float aq[NSG][NQG][R], ak[NSG][NQG][R];
 #pragma unroll
       for (int sgl = 0; sgl < NSG; ++sgl) {
@@ -627,7 +610,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
         reduce_and_stage(kwp, 0, i0, a, aq[sgl], ak[sgl]);
         arrive(bar_A + cs * NSG + sgl);
       }
-      if (tlw && kt < 3) TL_STAMP(2 + 4 * kt);
 #pragma unroll
       for (int sgl = 0; sgl < NSG; ++sgl) {
         const int sg = cs * NSG + sgl, i0 = sg * NQG;
@@ -669,7 +651,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
             m_run[sgl][k] = mn;
           }
       }
-      if (tlw && kt < 3) TL_STAMP(3 + 4 * kt);
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_Sfree + sbuf);
@@ -698,7 +679,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
       linv[jc] = l > 0.f ? 1.f / l : 0.f;
     }
     ptx::named_bar_sync(1, 32 * NCW);
-    if (tlw) TL_STAMP(12);
 
     // ============================== pass B: probabilities, post mix, P'V
     for (int kt = 0; kt < nkt; ++kt) {
@@ -711,7 +691,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
       const int sbuf = 0;
       wait_or_fail(bar_S + sbuf, scnt[sbuf] & 1, ERR_TIMEOUT_S);
       ptx::tc_fence_after();
-      if (tlw && kt < 3) TL_STAMP(13 + 5 * kt);
       float aq[NSG][NQG][R], ak[NSG][NQG][R];
 #pragma unroll
       for (int sgl = 0; sgl < NSG; ++sgl) {
@@ -722,7 +701,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
         reduce_and_stage(kwp, 0, i0, a, aq[sgl], ak[sgl]);
         arrive(bar_A + cs * NSG + sgl);
       }
-      if (tlw && kt < 3) TL_STAMP(14 + 5 * kt);
       load_keyw<E, HH, R>(kwq, p.post, tok, H, hbase + HH * u, key_ok);
       float pr[NSG][HH][NQG], pq[NSG][NQG][R], pk[NSG][NQG][R];
 #pragma unroll
@@ -746,13 +724,11 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
         reduce_and_stage(kwq, 1, i0, pr[sgl], pq[sgl], pk[sgl]);
         arrive(bar_A + sg);
       }
-      if (tlw && kt < 3) TL_STAMP(15 + 5 * kt);
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_Sfree + sbuf);
       ++scnt[sbuf];
       if (kt >= 1) wait_or_fail(bar_Pfree, (kt - 1) & 1, ERR_TIMEOUT_P);
-      if (tlw && kt < 3) TL_STAMP(16 + 5 * kt);
 #pragma unroll
       for (int sgl = 0; sgl < NSG; ++sgl) {
         const int sg = cs * NSG + sgl, i0 = sg * NQG;
@@ -773,7 +749,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
           }
       }
       arrive(bar_P);
-      if (tlw && kt < 3) TL_STAMP(17 + 5 * kt);
     }
 
     // ============================== epilogue: O^T -> SMEM [head][d half][query][64 d] -> TMA store
@@ -801,8 +776,6 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
       ptx::bulk_commit();
       ptx::bulk_wait_read0();
     }
-    if (tlw) TL_STAMP(28);
-    if (tlw) TL_VAL(38, w_comp);
   }
 
   ptx::tc_fence_before();
@@ -832,6 +805,8 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   tp.out = p.out;
   tp.out_sb = p.out_sb; tp.out_st = p.out_st; tp.out_sh = p.out_sh;
   tp.err_flag = p.err_flag;
+  tp.wait_us = p.wait_us;
+  tp.skip_loads = (p.test_flags & DC_TEST_SKIP_LOADS) != 0;
   tp.pre = to_ptrs(p.pre);
   tp.post = to_ptrs(p.post);
   auto kern = dc_tcm_kernel<E, HPG, R>;

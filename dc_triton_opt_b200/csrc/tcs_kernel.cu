@@ -104,7 +104,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
   const int nkt = (span + KT_ROWS - 1) / KT_ROWS;
   const int rlast = ((span - KT_ROWS * (nkt - 1)) + 15) / 16 * 16;
   const int slen = p.seq_lens ? min(max(p.seq_lens[b], 0), T) : T;
-  const uint32_t WAIT = 1u << 24;
+  const uint32_t WAIT = p.wait_us;
   const uint32_t o_col = NSB * NQT;
 
   if (threadIdx.x == 0) {
@@ -131,7 +131,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
   if (warp == tma_warp) {
     // ================================================= TMA producer
     // ring jobs: pass A K(kt, h); pass B K(0, h); then K(kt, h), V(kt-1, h); last V(nkt-1, h)
-    if (lane == 0) {
+    if (lane == 0 && !p.skip_loads) {
       ptx::tma_prefetch_desc(&tm_q);
       ptx::tma_prefetch_desc(&tm_k);
       ptx::tma_prefetch_desc(&tm_v);
@@ -518,6 +518,8 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   tp.out = p.out;
   tp.out_sb = p.out_sb; tp.out_st = p.out_st; tp.out_sh = p.out_sh;
   tp.err_flag = p.err_flag;
+  tp.wait_us = p.wait_us;
+  tp.skip_loads = (p.test_flags & DC_TEST_SKIP_LOADS) != 0;
   tp.pre = to_ptrs(p.pre);
   tp.post = to_ptrs(p.post);
   auto kern = dc_tcs_kernel<E, HPG, R>;

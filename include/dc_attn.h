@@ -32,7 +32,12 @@
  *     legacy default stream) and is asynchronous;
  *   - the return value is 0 on success or a negative DC_ERR_* code; the
  *     message of the last error on the calling thread is returned by
- *     dc_attn_last_error().
+ *     dc_attn_last_error();
+ *   - errors found on the device after a launch (a bounded wait inside a
+ *     kernel that ran out: the kernel then skips the rest of its work and the
+ *     output is not valid) are written to an error word, the caller's
+ *     err_flag or the library's own per-device word, and read back with
+ *     dc_attn_read_error().
  */
 #ifndef DC_ATTN_H_
 #define DC_ATTN_H_
@@ -43,7 +48,7 @@
 extern "C" {
 #endif
 
-#define DC_ATTN_ABI_VERSION 1
+#define DC_ATTN_ABI_VERSION 2
 
 #if defined(_WIN32)
 #define DC_API __declspec(dllexport)
@@ -103,10 +108,30 @@ typedef struct dc_attn_params {
   void *out;               /* out[b*out_sb + t*out_st + h*out_sh + d]             */
   int64_t out_sb, out_st, out_sh; /* element strides; d is contiguous             */
   const int32_t *seq_lens; /* [B] keys s >= seq_lens[b] are masked; NULL = T      */
-  int32_t *err_flag;       /* optional device int; kernels that wait on barriers
-                              write a non-zero code here instead of hanging       */
+  int32_t *err_flag;       /* optional device int32; a kernel whose bounded wait runs
+                              out writes its DC_DEV_ERR_* code here (first code
+                              wins).  NULL = the library's per-device error word  */
   dc_terms pre, post;
+  uint32_t wait_us;        /* limit of every wait inside a kernel, microseconds;
+                              0 = 2 s                                             */
+  int32_t test_flags;      /* testing only, 0 in normal use (DC_TEST_*)           */
 } dc_attn_params;
+
+/* dc_attn_params.test_flags: the loading warp issues no loads, so every wait
+ * of the launch runs out after wait_us and the kernel reports a timeout.  It
+ * lets a test exercise the device-error path without a fault. */
+#define DC_TEST_SKIP_LOADS 1
+
+/* Device error codes (written to the error word, read by dc_attn_read_error). */
+enum dc_dev_error {
+  DC_DEV_OK = 0,
+  DC_DEV_ERR_TIMEOUT_Q = 1,    /* query tile never arrived            */
+  DC_DEV_ERR_TIMEOUT_FULL = 2, /* key / value tile never arrived      */
+  DC_DEV_ERR_TIMEOUT_FREE = 3, /* ring slot never released            */
+  DC_DEV_ERR_TIMEOUT_S = 4,    /* logits never completed              */
+  DC_DEV_ERR_TIMEOUT_P = 5,    /* probabilities never written         */
+  DC_DEV_ERR_TIMEOUT_O = 6     /* output accumulator never completed  */
+};
 
 /* General forward.  Returns DC_OK or a DC_ERR_* code. */
 DC_API int dc_attn_fwd(const dc_attn_params *p, void *stream);
@@ -122,6 +147,18 @@ DC_API int dc_attn_fwd_residual(const void *q, const void *k, const void *v,
                          const int32_t *seq_lens, int32_t B, int32_t T, int32_t N,
                          int32_t D, int32_t G, float scaling, int32_t window,
                          int32_t chunk_size, int32_t dtype, void *stream);
+
+/* Read the device error word `err_flag` (NULL = the library's word on the
+ * current device) after the work queued on `stream` so far: the call enqueues
+ * a copy on `stream` and synchronises with it.  Returns the DC_DEV_* code
+ * (0 = no error) or a negative DC_ERR_* code if the copy failed.  With
+ * clear != 0 the word is reset to 0 afterwards.  No counterpart in the
+ * reference, whose kernels never wait on a barrier that can stay open. */
+DC_API int dc_attn_read_error(int32_t *err_flag, int clear, void *stream);
+
+/* The kernel (enum dc_kernel) the last successful dc_attn_fwd call on the
+ * calling thread launched, 0 if none yet. */
+DC_API int dc_attn_last_kernel(void);
 
 /* Which kernel DC_KERNEL_AUTO would pick for *p (enum dc_kernel), or a
  * negative DC_ERR_* code if no kernel supports the request. */

@@ -78,3 +78,59 @@ def test_two_gloo_ranks_shard_and_gather(tmp_path):
     err, t = np.load(tmp_path / "err.npy")
     assert err == 0.0
     assert t == 20.0
+
+
+@pytest.mark.parametrize("B,G,world", [(1, 8, 8), (2, 8, 8), (3, 8, 8), (1, 4, 8), (64, 1, 8), (2, 1, 8),
+                                       (2, 4, 3)])
+def test_work_shards_cover_pairs_exactly_once(B, G, world):
+    from dc_triton_opt_b200.shard import shard_work
+    seen = []
+    for r in range(world):
+        b0, b1, g0, g1 = shard_work(B, G, world, r)
+        assert 0 <= b0 <= b1 <= B and 0 <= g0 <= g1 <= G
+        seen.extend((b, g) for b in range(b0, b1) for g in range(g0, g1))
+    assert sorted(seen) == [(b, g) for b in range(B) for g in range(G)]
+
+
+def _group_worker(rank, world, port, out_dir):
+    """B=1 < world: the ranks split the head groups of the single batch."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    from oracle import dc_oracle as O
+    from dc_triton_opt_b200.shard import shard_inputs, shard_work
+    B, T, H, D, G, R, W = 1, 40, 8, 16, 4, 1, 12
+    q, k, v, pre, post = O.make_inputs(B, T, H, D, G, R, seed=33, mix_std=0.1)
+    t = lambda a: None if a is None else torch.from_numpy(np.ascontiguousarray(a))
+    from dc_triton_opt_b200 import DCTerms
+    dct = lambda tm: DCTerms(identity=tm.identity, w=t(tm.w), qw1=t(tm.qw1), qw2=t(tm.qw2), kw1=t(tm.kw1),
+                             kw2=t(tm.kw2), qdd=t(tm.qdd), kdd=t(tm.kdd))
+    shard = shard_work(B, G, world, rank)
+    sq, sk, sv, spre, spost, sg = shard_inputs(t(q), t(k), t(v), dct(pre), dct(post), G, shard)
+    n = lambda a: None if a is None else a.numpy()
+    ot = lambda tm: O.Terms(identity=tm.identity, w=n(tm.w), qw1=n(tm.qw1), qw2=n(tm.qw2), kw1=n(tm.kw1),
+                            kw2=n(tm.kw2), qdd=n(tm.qdd), kdd=n(tm.kdd))
+    out = O.dc_attn_oracle(n(sq), n(sk), n(sv), ot(spre), ot(spost), 0.25, W, sg)
+    b0, b1, g0, g1 = shard
+    hpg = H // G
+    full = np.zeros((B, T, H, D))
+    full[b0:b1, :, g0 * hpg:g1 * hpg] = out
+    mask = np.zeros((B, T, H, D))
+    mask[b0:b1, :, g0 * hpg:g1 * hpg] = 1.0
+    acc, cnt = torch.from_numpy(full), torch.from_numpy(mask)
+    dist.all_reduce(acc)
+    dist.all_reduce(cnt)
+    if rank == 0:
+        ref = O.dc_attn_oracle(q, k, v, pre, post, 0.25, W, G)
+        np.save(os.path.join(out_dir, "gerr.npy"), np.array([np.abs(acc.numpy() - ref).max(),
+                                                              np.abs(cnt.numpy() - 1).max()]))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+def test_two_gloo_ranks_shard_head_groups(tmp_path):
+    world = 2
+    mp.spawn(_group_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    err, cover = np.load(tmp_path / "gerr.npy")
+    assert cover == 0.0
+    assert err < 1e-12
