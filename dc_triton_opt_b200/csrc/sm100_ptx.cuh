@@ -123,6 +123,8 @@ __device__ __forceinline__ void tma_store_4d(const CUtensorMap *m, const void *s
 __device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
 // Wait until the shared-memory sources of all committed bulk stores were read.
 __device__ __forceinline__ void bulk_wait_read0() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Wait until all committed bulk stores are complete (writes visible).
+__device__ __forceinline__ void bulk_wait_all0() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
 
 // ---------------------------------------------------------------- TMEM
 // Warp-wide: allocate `ncols` TMEM columns, address written to *dst (smem).
@@ -271,6 +273,20 @@ __device__ __forceinline__ f2_t f2_add(f2_t a, f2_t b) {
   f2_t d;
   asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
   return d;
+}
+
+// Sum of a 32-bit unsigned value over the warp (every lane gets it), modulo 2^32.
+__device__ __forceinline__ uint32_t warp_sum_u32(uint32_t v) {
+  uint32_t r;
+  asm volatile("redux.sync.add.u32 %0, %1, 0xffffffff;" : "=r"(r) : "r"(v));
+  return r;
+}
+
+// 2^x on the special-function unit (approximate; subnormal results flush to 0).
+__device__ __forceinline__ float ex2(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
 }
 
 __device__ __forceinline__ float warp_max(float v) {

@@ -209,9 +209,134 @@ __device__ __forceinline__ void compose2(const ptx::f2_t (&a)[HPG], ptx::f2_t (&
   }
 }
 
+// Logit given to masked (query, key) pairs: finite, so that max / exp need no
+// infinity checks; 2^(kMaskedLogit - m) is 0 for any real maximum m.
+constexpr float kMaskedLogit = -1e30f;
+
+// HPG consecutive floats of shared memory (16-byte aligned when HPG % 4 == 0).
+template <int HPG>
+__device__ __forceinline__ void ld_row(const float *p, float (&r)[HPG]) {
+  if constexpr (HPG % 4 == 0) {
+#pragma unroll
+    for (int j = 0; j < HPG; j += 4) {
+      const float4 x = *reinterpret_cast<const float4 *>(p + j);
+      r[j] = x.x; r[j + 1] = x.y; r[j + 2] = x.z; r[j + 3] = x.w;
+    }
+  } else if constexpr (HPG == 2) {
+    const float2 x = *reinterpret_cast<const float2 *>(p);
+    r[0] = x.x; r[1] = x.y;
+  } else {
+    r[0] = p[0];
+  }
+}
+
+// Composition of one (query, key) pair with the query's mixing matrix M
+// (shared memory, [h'][h]: the coefficient of a[h'] in o[h]) and the key's
+// weights in registers:
+//   o[h] = sum_h' M[h'][h] a[h'] + kdd[h] a[h] + sum_r kw2[r][h] sum_h' kw1[h'][r] a[h'].
+template <int HPG, int R>
+__device__ __forceinline__ void compose_m(const float (&a)[HPG], float (&o)[HPG], const float *M,
+                                          const float (&kw1)[HPG * R], const float (&kw2)[R * HPG],
+                                          const float (&kdd)[HPG]) {
+  float ak[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    ak[r] = 0.f;
+#pragma unroll
+    for (int h = 0; h < HPG; ++h) ak[r] = fmaf(kw1[h * R + r], a[h], ak[r]);
+  }
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) o[h] = kdd[h] * a[h];
+#pragma unroll
+  for (int h1 = 0; h1 < HPG; ++h1) {
+    float mr[HPG];
+    ld_row<HPG>(M + h1 * HPG, mr);
+#pragma unroll
+    for (int h = 0; h < HPG; ++h) o[h] = fmaf(mr[h], a[h1], o[h]);
+  }
+#pragma unroll
+  for (int h = 0; h < HPG; ++h)
+#pragma unroll
+    for (int r = 0; r < R; ++r) o[h] = fmaf(kw2[r * HPG + h], ak[r], o[h]);
+}
+
+// Two floats rounded to E (bf16 / fp16) and packed low | high << 16.
+template <typename E>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  const E a = from_f<E>(lo), b = from_f<E>(hi);
+  return static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&a)) |
+         (static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&b)) << 16);
+}
+
 template <typename E>
 __device__ __forceinline__ float ld_w(const void *base, int64_t idx) {
   return to_f<E>(reinterpret_cast<const E *>(base)[idx]);
+}
+
+// N consecutive 16-bit elements (N * 2 bytes, aligned to that size), raw.
+template <int N>
+struct Raw16 {
+  uint32_t w[(N + 1) / 2];
+};
+template <int N>
+__device__ __forceinline__ Raw16<N> ld_raw16(const void *p) {
+  Raw16<N> r;
+  if constexpr (N == 1) {
+    r.w[0] = __ldg(reinterpret_cast<const unsigned short *>(p));
+  } else if constexpr (N == 2) {
+    r.w[0] = __ldg(reinterpret_cast<const unsigned int *>(p));
+  } else if constexpr (N == 4) {
+    const uint2 x = __ldg(reinterpret_cast<const uint2 *>(p));
+    r.w[0] = x.x; r.w[1] = x.y;
+  } else {
+    static_assert(N % 8 == 0, "16-bit vector of 1, 2, 4 or a multiple of 8 elements");
+#pragma unroll
+    for (int k = 0; k < N / 8; ++k) {
+      const uint4 x = __ldg(reinterpret_cast<const uint4 *>(p) + k);
+      r.w[4 * k] = x.x; r.w[4 * k + 1] = x.y; r.w[4 * k + 2] = x.z; r.w[4 * k + 3] = x.w;
+    }
+  }
+  return r;
+}
+template <int N>
+__device__ __forceinline__ Raw16<N> raw16_zero() {
+  Raw16<N> r;
+#pragma unroll
+  for (int k = 0; k < (N + 1) / 2; ++k) r.w[k] = 0u;
+  return r;
+}
+// element i of a raw vector as float (the bit pattern 0 converts to 0.0)
+template <typename E, int N>
+__device__ __forceinline__ float raw16_get(const Raw16<N> &r, int i) {
+  const unsigned short b = static_cast<unsigned short>(r.w[i >> 1] >> (16 * (i & 1)));
+  return to_f<E>(*reinterpret_cast<const E *>(&b));
+}
+template <typename E>
+__device__ __forceinline__ const E *elem(const void *base, int64_t i) {
+  return reinterpret_cast<const E *>(base) + i;
+}
+
+// The per-key weights of key token `tok` for heads [hbase, hbase + HPG): kw1
+// [h][r], kw2 [r][h], kdd [h], each a run of contiguous elements loaded as one
+// vector (zero when the key is outside the sequence or the term is absent).
+template <typename E, int HPG, int R>
+__device__ __forceinline__ void load_key_weights_vec(const TermPtrs &tm, int64_t tok, int H, int hbase, bool ok,
+                                                     float (&kw1)[HPG * R], float (&kw2)[R * HPG],
+                                                     float (&kdd)[HPG]) {
+  const Raw16<HPG * R> a = (ok && tm.kw1) ? ld_raw16<HPG * R>(elem<E>(tm.kw1, (tok * H + hbase) * R))
+                                          : raw16_zero<HPG * R>();
+  const Raw16<HPG> c = (ok && tm.kdd) ? ld_raw16<HPG>(elem<E>(tm.kdd, tok * H + hbase)) : raw16_zero<HPG>();
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const Raw16<HPG> bq = (ok && tm.kw2) ? ld_raw16<HPG>(elem<E>(tm.kw2, (tok * R + r) * H + hbase))
+                                         : raw16_zero<HPG>();
+#pragma unroll
+    for (int h = 0; h < HPG; ++h) kw2[r * HPG + h] = raw16_get<E, HPG>(bq, h);
+  }
+#pragma unroll
+  for (int j = 0; j < HPG * R; ++j) kw1[j] = raw16_get<E, HPG * R>(a, j);
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) kdd[h] = raw16_get<E, HPG>(c, h);
 }
 
 template <typename E, int HPG, int R>

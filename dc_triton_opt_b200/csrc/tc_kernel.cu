@@ -507,7 +507,8 @@ static WarpRoles make_roles(int nkt, int rlast, int CS, int hpg) {
 }
 
 struct GeoP {
-  int nslot, q_off, p1_off, ring_off, wz_off, rec_off, red_off, bar_off, tmem_off, total, rec_floats, p1_bytes;
+  int nslot, q_off, p1_off, ring_off, wz_off, raw_off, mrec_off, red_off, fac_off, bar_off, tmem_off, stage_off,
+      total, raw_floats, p1_bytes;
 };
 
 __host__ __device__ inline GeoP make_geo_p(int HPG, int R, int rlast, int nslot, int G) {
@@ -526,15 +527,20 @@ __host__ __device__ inline GeoP make_geo_p(int HPG, int R, int rlast, int nslot,
   if (HPG > 1 && HPG * rlast * 256 <= TILE_BYTES) pad = (2 * HPG - 1) * rlast * 128 + TILE_BYTES / 2 - TILE_BYTES;
   const int ring_end = g.ring_off + nslot * TILE_BYTES;
   int o = ring_end;
-  g.rec_floats = round_up(HPG * (2 * R + 1), 4);
-  // static mixes of every group [2][G][HPG*HPG] and the identity + diagonal
-  // table [2][G][HPG]: a persistent CTA's tiles belong to different groups
-  g.wz_off = o;  o += 2 * G * HPG * HPG * 4 + 2 * G * HPG * 4;
-  // per-query records, double-buffered: tile n+1's are fetched during tile n
-  g.rec_off = round_up(o, 16); o = g.rec_off + 2 * (2 * BM * g.rec_floats * 4);
-  g.red_off = o; o += 2 * 8 * NQ * 4;
+  g.raw_floats = HPG * (2 * R + 1);
+  // static mix of every group with the identity on its diagonal [set][G][h'][h]:
+  // a persistent CTA's tiles belong to different groups
+  g.wz_off = o;  o += 2 * G * HPG * HPG * 4;
+  // per-query weights as loaded (qdd[h] | qw1[h][r] | qw2[r][h]) [parity][set][BM]:
+  // tile n+1's are fetched during tile n
+  g.raw_off = round_up(o, 16); o = g.raw_off + 2 * 2 * BM * g.raw_floats * 4;
+  // per-query mixing matrices [parity][set][BM][h'][h]: tile n+1's are built during tile n
+  g.mrec_off = round_up(o, 16); o = g.mrec_off + 2 * 2 * BM * HPG * HPG * 4;
+  g.red_off = round_up(o, 16); o = g.red_off + 2 * 8 * NQ * 4;   // column maxima | column sums
+  g.fac_off = o; o += 8 * NQ * 4;                                 // probability factors [slot][BM][HPG]
   g.bar_off = round_up(o, 8); o = g.bar_off + 32 * 8;
   g.tmem_off = o; o += 16;
+  g.stage_off = round_up(o, 1024); o = g.stage_off + 8192;  // epilogue staging (32 columns)
   g.total = o > ring_end + pad ? o : ring_end + pad;
   return g;
 }
@@ -554,9 +560,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                           ~static_cast<uintptr_t>(1023));
   const GeoP geo = make_geo_p(HPG, R, rlast, nslot, p.G);
-  float *Wz = reinterpret_cast<float *>(smem + geo.wz_off);
-  float *rec = reinterpret_cast<float *>(smem + geo.rec_off);
-  float *red = reinterpret_cast<float *>(smem + geo.red_off);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + geo.bar_off);
   uint64_t *bar_full = bars + 0, *bar_free = bars + 22;         // ring (up to 4 slots each)
   uint64_t *bar_q = bars + 6;                                    // [2] Q landed
@@ -564,7 +567,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
   uint64_t *bar_P = bars + 12;                                   // [2] P' written (compose warps)
   uint64_t *bar_O = bars + 14;                                   // [2] O complete (PV committed)
   uint64_t *bar_Ofree = bars + 16;                               // [2] O read out of TMEM (epilogue)
-  uint64_t *bar_Qfree = bars + 18;                               // [2] staging tile stored (epilogue)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(smem + geo.tmem_off);
 
   const int ncw = roles.ncw;  // compose warps
@@ -583,7 +585,12 @@ __global__ void __launch_bounds__(32 * NW, 1)
   const bool packed_last = !rep_last && HPG > 1 && HPG * rlast * 256 <= TILE_BYTES;
   const int nK = HPG * (nkt - 1) + (packed_last ? 1 : HPG);
   struct Job { int kt, h0, nh, rows, half; };  // half: byte distance of the d-halves
-  auto job_of = [&](int jj) {
+  // K jobs visit the last key tile first: its compose warps then start with
+  // the others instead of one key-tile load later; V jobs keep key-tile order
+  // (the first PV product of a tile initialises the accumulator)
+  const int nlast = packed_last ? 1 : HPG;
+  auto job_of = [&](int jj, bool isv) {
+    if (!isv && nkt > 1) jj = jj < nlast ? HPG * (nkt - 1) + jj : jj - nlast;
     Job j;
     if (jj < HPG * (nkt - 1)) { j.kt = jj / HPG; j.h0 = jj % HPG; j.nh = 1; }
     else if (packed_last) { j.kt = nkt - 1; j.h0 = 0; j.nh = HPG; }
@@ -605,7 +612,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
       ptx::mbar_init(bar_P + i, ncw);
       ptx::mbar_init(bar_O + i, 1);
       ptx::mbar_init(bar_Ofree + i, 4);
-      ptx::mbar_init(bar_Qfree + i, 1);
     }
     ptx::fence_mbar_init();
   }
@@ -649,7 +655,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     auto load_kv = [&](bool isv, int q0, int b, int g, int jj) {
       const int slot = job % nslot, use = job / nslot;
       if (use > 0 && !wait_all(bar_free + slot, (use - 1) & 1, ERR_TIMEOUT_FREE)) return;
-      const Job jb = job_of(jj);
+      const Job jb = job_of(jj, isv);
       const bool last = jb.kt == nkt - 1;
       const CUtensorMap *m = isv ? (last ? &tm_vl : &tm_v) : (last ? &tm_kl : &tm_k);
       const int kb = q0 - p.window + 1;
@@ -672,7 +678,8 @@ __global__ void __launch_bounds__(32 * NW, 1)
       int q0, b, g;
       tile_coords(tile, q0, b, g);
       const int buf = it & 1;
-      if (it >= 2 && !wait_all(bar_Qfree + buf, ((it - 2) >> 1) & 1, ERR_TIMEOUT_Q)) break;
+      // the Q buffer holds P' of key tile 0 of tile it - 2 until its PV products are complete
+      if (it >= 2 && !wait_all(bar_O + buf, ((it - 2) >> 1) & 1, ERR_TIMEOUT_Q)) break;
       if (lane == 0) ptx::mbar_expect_tx(bar_q + buf, NQ * 256);
       __syncwarp();
       if (lane < 2 * HPG) {
@@ -714,7 +721,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
         const int slot = job % nslot;
         if (!wait_u(bar_full + slot, (job / nslot) & 1, ERR_TIMEOUT_FULL)) return;
         ptx::tc_fence_after();
-        const Job jb = job_of(jj);
+        const Job jb = job_of(jj, true);
         const int nks = jb.rows / 16;
         for (int u = 0; u < jb.nh; ++u) {
           const int h = jb.h0 + u;
@@ -748,7 +755,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
         const int slot = job % nslot;
         if (!wait_u(bar_full + slot, (job / nslot) & 1, ERR_TIMEOUT_FULL)) break;
         ptx::tc_fence_after();
-        const Job jb = job_of(jj);
+        const Job jb = job_of(jj, false);
         for (int u = 0; u < jb.nh; ++u) {
           const int h = jb.h0 + u;
           const uint64_t ad = ptx::smem_desc(ring_addr + slot * TILE_BYTES + u * 2 * jb.half, 16, 1024, 2);
@@ -772,7 +779,13 @@ __global__ void __launch_bounds__(32 * NW, 1)
     if (it >= 1 && ok) pv(it - 1);
   } else if ((role & 0xF0) == ROLE_EPI) {
     // ================================================= epilogue: O^T (lanes = d) -> SMEM -> TMA store
+    // 32 columns at a time through an 8 KB staging buffer of its own, so the Q
+    // buffer (P' of key tile 0) is free as soon as the PV products are done.
+    // Staging layout: [box][d half][RB rows][64 d], one box = RB queries of one head.
     const int quarter = warp & 3, d = 32 * quarter + lane;
+    constexpr int RB = BM < 32 ? BM : 32;
+    unsigned char *stage = smem + geo.stage_off;
+    const bool leader = warp == epi_warp0 && lane == 0;
     int it = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       int q0, b, g;
@@ -780,35 +793,48 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const int buf = it & 1;
       if (!ptx::mbar_wait(bar_O + buf, (it >> 1) & 1, WAIT)) { record_err(p, ERR_TIMEOUT_O); break; }
       ptx::tc_fence_after();
-      unsigned char *stage = smem + geo.q_off + buf * NQ * 256;
 #pragma unroll 1
-      for (int c = 0; c < NQ / 8; ++c) {
-        float v[8];
-        ptx::tmem_ld<8>(tbase + (static_cast<uint32_t>(32 * quarter) << 16) + buf * 256 + 8 * c, v);
+      for (int c = 0; c < NQ / 32; ++c) {
+        float v[32];
+        ptx::tmem_ld<32>(tbase + (static_cast<uint32_t>(32 * quarter) << 16) + buf * 256 + 32 * c, v);
         ptx::tmem_wait_ld();
+        if (c == NQ / 32 - 1) {
+          // every TMEM read of this tile is done: the buffer may take the next S
+          ptx::tc_fence_before();
+          __syncwarp();
+          if (lane == 0) ptx::mbar_arrive(bar_Ofree + buf);
+        }
+        ptx::named_bar_sync(2, 128);  // the previous chunk's stores have read the staging buffer
 #pragma unroll
-        for (int jj = 0; jj < 8; ++jj) {
-          const int col = 8 * c + jj, h = col / BM, i = col % BM;
-          *reinterpret_cast<E *>(stage + (h * 2 + (d >> 6)) * (BM * 128) + i * 128 + (d & 63) * 2) =
+        for (int jj = 0; jj < 32; ++jj)
+          *reinterpret_cast<E *>(stage + ((jj / RB) * 2 + (d >> 6)) * (RB * 128) + (jj % RB) * 128 + (d & 63) * 2) =
               from_f<E>(v[jj]);
+        ptx::fence_proxy_async_smem();
+        ptx::named_bar_sync(2, 128);
+        if (leader) {
+#pragma unroll
+          for (int box = 0; box < 32 / RB; ++box) {
+            const int col0 = 32 * c + box * RB, h = col0 / BM, i0 = col0 % BM;
+#pragma unroll
+            for (int dh = 0; dh < 2; ++dh)
+              ptx::tma_store_4d(&tm_o, stage + (box * 2 + dh) * (RB * 128), dh * 64, g * HPG + h, q0 + i0, b);
+          }
+          ptx::bulk_commit();
+          ptx::bulk_wait_read0();
         }
       }
-      ptx::tc_fence_before();
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(bar_Ofree + buf);
-      ptx::fence_proxy_async_smem();
-      ptx::named_bar_sync(2, 128);
-      if (warp == epi_warp0 && lane == 0) {
-        for (int h = 0; h < HPG; ++h)
-          for (int c = 0; c < 2; ++c)
-            ptx::tma_store_4d(&tm_o, stage + (h * 2 + c) * (BM * 128), c * 64, g * HPG + h, q0, b);
-        ptx::bulk_commit();
-        ptx::bulk_wait_read0();
-        ptx::mbar_arrive(bar_Qfree + buf);
-      }
     }
+    if (leader) ptx::bulk_wait_all0();
   } else if (role != ROLE_IDLE) {
     // ================================================= compose warps
+    //
+    // For one (query t, key s) pair and one composition set, the HPG heads of
+    // the group are mixed as
+    //   o[h] = sum_h' M_t[h'][h] a[h'] + kdd_s[h] a[h] + sum_r kw2_s[r][h] sum_h' kw1_s[h'][r] a[h']
+    // M_t = w[g] + identity + diag(qdd_t) + qw1_t qw2_t folds every
+    // query-dependent term into one HPG x HPG matrix per query, built once per
+    // tile; the key-dependent terms come from registers.  The pre set is scaled
+    // by scale * log2(e), so composed logits are in base-2 units.
     const int sub = role & 3, kt = role >> 3, cs = (role >> 2) & 1;
     // a warp of the replicated last key tile: its quarter (2 or 3) holds keys
     // 0..31 of the tile, it composes column groups 2 (sub - 2) and the next
@@ -823,56 +849,61 @@ __global__ void __launch_bounds__(32 * NW, 1)
     const int s_local = srow0 + lane;
     const int rows_kt = rows_of[kt];
     const float sl2e = p.scale * kLog2e;
-    float *redm = red, *reds = red + 4 * nkt * NQ;
-    auto col_of = [&](int L, int i0) { return (L / GI) * BM + i0 + (L % GI); };
-    // one head per group: the composition runs on paired fp32 (compose2)
-    constexpr bool PAIR = HPG == 1;
-    WSrc<HPG> Wreg;
-    WSrc2<HPG> Wreg2;
-    KeyW2<HPG, R> K2;
-    float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
-    // per-query records of one tile: [set][query][dq | qw1 (h, r) | qw2 (r, h)],
-    // for compose2 stored pair-interleaved (queries 2p and 2p + 1 alternate
-    // element by element: [set][query / 2][element][query % 2]),
-    // dq = identity + w[h,h] (the table `wdiag`, per group) + qdd[t,h].
-    // A record is at most one 16-bit element of a per-token weight plus that
-    // constant, so the next tile's records are prefetched as raw 16-bit
-    // values (no conversion stalls on arrival) and converted when stored.
-    const int nrec = 2 * BM * geo.rec_floats;
     const int G = p.G;
-    float *wdiag = Wz + 2 * G * HPG * HPG;  // [set][group][HPG]
-    auto rec_src = [&](int idx, int q0, int b, int g) -> const unsigned short * {
-      const int set = idx / (BM * geo.rec_floats), rem = idx % (BM * geo.rec_floats);
-      const int i = rem / geo.rec_floats, j = rem % geo.rec_floats;
+    constexpr int RAWF = HPG * (2 * R + 1);
+    constexpr int MF = HPG * HPG;
+    constexpr int NM = 2 * BM * MF;      // mixing-matrix entries of one tile (both sets)
+    constexpr int MAXREC = 4;            // weight chunks per compose thread (checked by the launcher)
+    float *Wt = reinterpret_cast<float *>(smem + geo.wz_off);      // [set][G][h'][h]
+    float *raw = reinterpret_cast<float *>(smem + geo.raw_off);    // [set][BM][RAWF]
+    float *mrec = reinterpret_cast<float *>(smem + geo.mrec_off);  // [parity][set][BM][h'][h]
+    float *redm = reinterpret_cast<float *>(smem + geo.red_off);   // [slot][NQ] column maxima (base 2)
+    uint32_t *reds = reinterpret_cast<uint32_t *>(redm + 8 * NQ);  // [slot][NQ] column sums (fixed point)
+    float *fac = reinterpret_cast<float *>(smem + geo.fac_off);    // [slot][BM][HPG]
+    float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
+
+    // per-query weights of a tile as chunks of HPG contiguous elements: chunk c =
+    // (set, query i, k), k = 0: qdd[h]; 1..R: qw1[h][r] (HPG * R contiguous
+    // elements cut into R chunks); R+1..2R: qw2[r][h].  Chunk k of a record
+    // lands at record floats [k * HPG, (k + 1) * HPG).
+    constexpr int NCK = 2 * R + 1;
+    constexpr int NCH = 2 * BM * NCK;
+    auto chunk_src = [&](int c, int q0, int b, int g) -> const E * {
+      const int set = c / (BM * NCK), rem = c % (BM * NCK), i = rem / NCK, k = rem % NCK;
       const TermPtrs &tm = set ? p.post : p.pre;
       const int t = q0 + i, hbase = g * HPG;
       if (t >= T) return nullptr;
       const int64_t tok = (int64_t)b * T + t;
-      const void *base = nullptr;
-      int64_t e = 0;
-      if (j < HPG) {
-        base = tm.qdd; e = tok * H + hbase + j;
-      } else if (j < HPG + HPG * R) {
-        const int h = (j - HPG) / R, r = (j - HPG) % R;
-        base = tm.qw1; e = (tok * H + hbase + h) * R + r;
-      } else if (j < HPG + 2 * HPG * R) {
-        const int r = (j - HPG - HPG * R) / HPG, h = (j - HPG - HPG * R) % HPG;
-        base = tm.qw2; e = (tok * R + r) * H + hbase + h;
-      }
-      return base ? reinterpret_cast<const unsigned short *>(base) + e : nullptr;
+      if (k == 0) return tm.qdd ? elem<E>(tm.qdd, tok * H + hbase) : nullptr;
+      if (k <= R) return tm.qw1 ? elem<E>(tm.qw1, (tok * H + hbase) * R + (k - 1) * HPG) : nullptr;
+      return tm.qw2 ? elem<E>(tm.qw2, (tok * R + (k - 1 - R)) * H + hbase) : nullptr;
     };
-    auto rec_store = [&](float *dst, int idx, unsigned short raw, bool has, int gg) {
-      const int set = idx / (BM * geo.rec_floats), j = (idx % (BM * geo.rec_floats)) % geo.rec_floats;
-      float v = j < HPG ? wdiag[(set * G + gg) * HPG + j] : 0.f;
-      if (has) v += to_f<E>(*reinterpret_cast<const E *>(&raw));
-      if (PAIR) {
-        const int rem = idx % (BM * geo.rec_floats), i = rem / geo.rec_floats;
-        dst[idx - rem + (i >> 1) * 2 * geo.rec_floats + 2 * j + (i & 1)] = v;
-      } else {
-        dst[idx] = v;
+    auto chunk_store = [&](int c, const Raw16<HPG> &v) {
+      const int set = c / (BM * NCK), rem = c % (BM * NCK), i = rem / NCK, k = rem % NCK;
+      float *dst = raw + (set * BM + i) * RAWF + k * HPG;
+#pragma unroll
+      for (int h = 0; h < HPG; ++h) dst[h] = raw16_get<E, HPG>(v, h);
+    };
+    // per-query matrices of a tile (group g) from the raw values -> mrec[par]
+    auto build_m = [&](int par, int g) {
+      float *dst = mrec + par * NM;
+      for (int idx = ctid; idx < NM; idx += ncompose) {
+        const int set = idx / (BM * MF), i = (idx / MF) % BM, h1 = (idx % MF) / HPG, h = idx % HPG;
+        const float *rr = raw + (set * BM + i) * RAWF;
+        float m = Wt[((set * G + g) * HPG + h1) * HPG + h] + (h1 == h ? rr[h] : 0.f);
+#pragma unroll
+        for (int r = 0; r < R; ++r) m = fmaf(rr[HPG + h1 * R + r], rr[HPG + HPG * R + r * HPG + h], m);
+        dst[idx] = set ? m : m * sl2e;
       }
     };
-    constexpr int MAXREC = 4;  // records per compose thread (checked by the launcher)
+    auto load_key = [&](const TermPtrs &tm, float f, int64_t ktok, int hbase, bool key_ok) {
+      load_key_weights_vec<E, HPG, R>(tm, ktok, H, hbase, key_ok, kw1, kw2, kdd);
+#pragma unroll
+      for (int j = 0; j < R * HPG; ++j) kw2[j] *= f;
+#pragma unroll
+      for (int j = 0; j < HPG; ++j) kdd[j] *= f;
+    };
+
     int it = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
       int q0, b, g;
@@ -882,68 +913,77 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const int slen = p.seq_lens ? min(max(p.seq_lens[b], 0), T) : T;
       const int s = kb + kt * KT_ROWS + s_local;
       const bool key_ok = s >= 0 && s < slen && s_local < rows_kt;
-      const int wk0 = kb + kt * KT_ROWS + srow0, wk1 = wk0 + 31;
+      const int wk0 = kb + kt * KT_ROWS + srow0;
       const int khi = min(q0 + BM - 1, slen - 1);
-      const bool active = wk1 >= max(0, kb) && wk0 <= khi && srow0 < rows_kt;
+      const bool active = wk0 + 31 >= max(0, kb) && wk0 <= khi && srow0 < rows_kt;
       const int64_t ktok = (int64_t)b * T + s;
       const uint32_t tl = tbase + (static_cast<uint32_t>(32 * sub) << 16) + buf * 256 + kt * KT_ROWS;
+      // every (query, key) pair of this warp's keys and the GI queries from t0 is unmasked
+      const bool keys_in = wk0 >= 0 && wk0 + 31 < slen && srow0 + 31 < rows_kt;
+      auto all_valid = [&](int t0) {
+        return keys_in && wk0 + 31 <= t0 && t0 + GI - 1 - wk0 < p.window && t0 + GI - 1 < T;
+      };
       auto valid = [&](int t) { return key_ok && s <= t && t - s < p.window && t < T; };
       // issue this tile's key-weight loads first: their latency overlaps the barrier
-      if (active) load_key_weights<E, HPG, R>(p.pre, ktok, H, hbase, key_ok, kw1, kw2, kdd);
-      // previous tile's pass 2 is finished by every compose warp before red and
-      // the record buffer of tile n+1 are rewritten
+      if (active) load_key(p.pre, sl2e, ktok, hbase, key_ok);
       if (it == 0) {
-        for (int idx = ctid; idx < 2 * G * HPG * HPG; idx += ncompose) {
-          const int set = idx / (G * HPG * HPG), gg = (idx / (HPG * HPG)) % G, j = idx % (HPG * HPG);
+        for (int idx = ctid; idx < 2 * G * MF; idx += ncompose) {
+          const int set = idx / (G * MF), gg = (idx / MF) % G, h1 = (idx % MF) / HPG, h = idx % HPG;
           const TermPtrs &tm = set ? p.post : p.pre;
-          const int h = j / HPG, hp = j % HPG;
-          Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)gg * HPG + hp) * HPG + h];
+          Wt[idx] = (tm.w ? tm.w[((int64_t)gg * HPG + h1) * HPG + h] : 0.f) + (h1 == h && tm.identity ? 1.f : 0.f);
         }
-        for (int idx = ctid; idx < 2 * G * HPG; idx += ncompose) {
-          const int set = idx / (G * HPG), gg = (idx / HPG) % G, h = idx % HPG;
-          const TermPtrs &tm = set ? p.post : p.pre;
-          wdiag[idx] = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)gg * HPG + h) * HPG + h] : 0.f);
+        for (int c = ctid; c < NCH; c += ncompose) {
+          const E *src = chunk_src(c, q0, b, g);
+          chunk_store(c, src ? ld_raw16<HPG>(src) : raw16_zero<HPG>());
         }
-        ptx::named_bar_sync(1, ncompose);  // wdiag visible
-        for (int idx = ctid; idx < nrec; idx += ncompose) {
-          const unsigned short *src = rec_src(idx, q0, b, g);
-          rec_store(rec, idx, src ? __ldg(src) : (unsigned short)0, src != nullptr, g);
-        }
+        ptx::named_bar_sync(1, ncompose);
+        build_m(0, g);
       }
-      ptx::named_bar_sync(1, ncompose);  // staged weights / records visible, previous tile done
-      const float *recb = rec + (it & 1) * nrec;
-      if (active) {
-        if constexpr (PAIR) Wreg2.load(Wz + g * HPG * HPG);
-        else Wreg.load(Wz + g * HPG * HPG);
-      }
+      // this tile's matrices are visible; the previous tile's pass 2 is finished
+      // by every compose warp before the reduction buffers are rewritten
+      ptx::named_bar_sync(1, ncompose);
+      const float *mcur = mrec + buf * NM;
       bool ok = ptx::mbar_wait(bar_S + 2 * buf + kt, (it >> 1) & 1, WAIT);
       if (!ok) record_err(p, ERR_TIMEOUT_S);
       ptx::tc_fence_after();
-      if (PAIR && active) K2.set(kw1, kw2, kdd);
+      // the next tile's per-query weights: loads issued now, stored after pass 1
+      Raw16<HPG> nrv[MAXREC];
+      const int ntile = tile + gridDim.x;
+      int nq0 = 0, nb = 0, ng = 0;
+      if (ntile < ntiles) {
+        tile_coords(ntile, nq0, nb, ng);
+#pragma unroll
+        for (int k = 0; k < MAXREC; ++k) {
+          const int c = ctid + k * ncompose;
+          const E *src = c < NCH ? chunk_src(c, nq0, nb, ng) : nullptr;
+          nrv[k] = src ? ld_raw16<HPG>(src) : raw16_zero<HPG>();
+        }
+      }
 
-      // ---- pass 1 (see dc_tc_kernel)
+      // ---- pass 1: pre-composition (+ mask at the window's edges), warp-local
+      //      column max (redux), e = 2^(S - m_w) back to TMEM, warp-local column
+      //      sums.  The sums are exact fixed-point: every e is in [0, 1], and
+      //      e + 1 has the value e * 2^23 in its low mantissa bits, so an integer
+      //      redux of the bit patterns sums them (minus 32 * bits(1.0), modulo 2^32).
 #pragma unroll 1
       for (int grp = g_begin; grp < g_end; ++grp) {
         const int i0 = grp * GI;
-        float mine_m = -INFINITY, mine_s = 0.f;
+        float *mx = redm + rw * NQ + i0;
+        uint32_t *sx = reds + rw * NQ + i0;
         if (active && ok) {
           float v[HPG][GI];
 #pragma unroll
           for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
           ptx::tmem_wait_ld();
-          if constexpr (PAIR) {
+          if (all_valid(q0 + i0)) {
 #pragma unroll
-            for (int ii = 0; ii < GI; ii += 2) {
-              ptx::f2_t a[HPG], o[HPG];
+            for (int ii = 0; ii < GI; ++ii) {
+              float a[HPG], o[HPG];
 #pragma unroll
-              for (int h = 0; h < HPG; ++h) a[h] = ptx::f2_pack(v[h][ii], v[h][ii + 1]);
-              compose2<HPG, R>(a, o, Wreg2, recb + (i0 + ii) * geo.rec_floats, K2);
-              const bool vl0 = valid(q0 + i0 + ii), vl1 = valid(q0 + i0 + ii + 1);
+              for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
+              compose_m<HPG, R>(a, o, mcur + (i0 + ii) * MF, kw1, kw2, kdd);
 #pragma unroll
-              for (int h = 0; h < HPG; ++h) {
-                v[h][ii] = vl0 ? ptx::f2_lo(o[h]) : -INFINITY;
-                v[h][ii + 1] = vl1 ? ptx::f2_hi(o[h]) : -INFINITY;
-              }
+              for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
             }
           } else {
 #pragma unroll
@@ -951,65 +991,86 @@ __global__ void __launch_bounds__(32 * NW, 1)
               float a[HPG], o[HPG];
 #pragma unroll
               for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
-              compose<HPG, R>(a, o, Wreg, recb + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+              compose_m<HPG, R>(a, o, mcur + (i0 + ii) * MF, kw1, kw2, kdd);
               const bool vl = valid(q0 + i0 + ii);
 #pragma unroll
-              for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : -INFINITY;
+              for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : kMaskedLogit;
             }
           }
 #pragma unroll
-          for (int h = 0; h < HPG; ++h)
+          for (int h = 0; h < HPG; ++h) {
+            float m8[GI];
+            uint32_t s8[GI];
 #pragma unroll
             for (int ii = 0; ii < GI; ++ii) {
-              const float mw = ptx::warp_max(v[h][ii]);
-              if (lane == h * GI + ii) mine_m = mw;
-              v[h][ii] = exp2f((v[h][ii] - (mw == -INFINITY ? 0.f : mw)) * sl2e);
+              m8[ii] = ptx::warp_max(v[h][ii]);
+              v[h][ii] = ptx::ex2(v[h][ii] - m8[ii]);
+              s8[ii] = ptx::warp_sum_u32(__float_as_uint(v[h][ii] + 1.f));
             }
+            if (lane == 0) {
+#pragma unroll
+              for (int ii = 0; ii < GI; ii += 4) {
+                *reinterpret_cast<float4 *>(mx + h * BM + ii) = make_float4(m8[ii], m8[ii + 1], m8[ii + 2], m8[ii + 3]);
+                *reinterpret_cast<uint4 *>(sx + h * BM + ii) = make_uint4(s8[ii], s8[ii + 1], s8[ii + 2], s8[ii + 3]);
+              }
+            }
+          }
 #pragma unroll
           for (int h = 0; h < HPG; ++h) ptx::tmem_st<GI>(tl + h * BM + i0, v[h]);
-          float x[32];
+        } else if (lane == 0) {
+          // nothing of this warp survives the mask: its factor will be 0
 #pragma unroll
           for (int h = 0; h < HPG; ++h)
 #pragma unroll
-            for (int ii = 0; ii < GI; ++ii) x[h * GI + ii] = v[h][ii];
-#pragma unroll
-          for (int off = 16, cnt = 32; off >= 1; off >>= 1, cnt >>= 1) {
-            const bool upper = (lane & off) != 0;
-#pragma unroll
-            for (int j = 0; j < cnt / 2; ++j) {
-              const float send = upper ? x[j] : x[j + cnt / 2];
-              const float keep = upper ? x[j + cnt / 2] : x[j];
-              x[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+            for (int ii = 0; ii < GI; ii += 4) {
+              *reinterpret_cast<float4 *>(mx + h * BM + ii) =
+                  make_float4(kMaskedLogit, kMaskedLogit, kMaskedLogit, kMaskedLogit);
+              *reinterpret_cast<uint4 *>(sx + h * BM + ii) = make_uint4(0u, 0u, 0u, 0u);
             }
-          }
-          mine_s = x[0];
         }
-        redm[rw * NQ + col_of(lane, i0)] = mine_m;
-        reds[rw * NQ + col_of(lane, i0)] = mine_s;
       }
-      // post-set weights into the registers of the pre-set ones (dead after
-      // pass 1); their latency overlaps the column reduction and its barriers
-      if (active) {
-        if constexpr (PAIR) Wreg2.load(Wz + (G + g) * HPG * HPG);
-        else Wreg.load(Wz + (G + g) * HPG * HPG);
-        load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
+      if (ntile < ntiles) {
+#pragma unroll
+        for (int k = 0; k < MAXREC; ++k) {
+          const int c = ctid + k * ncompose;
+          if (c < NCH) chunk_store(c, nrv[k]);
+        }
       }
       ptx::tmem_wait_st();
       ptx::named_bar_sync(1, ncompose);
+      // combine the slots of each column j = h * BM + i: m = max_w m_w,
+      // l = sum_w sum_w 2^(m_w - m); factor_w = 2^(m_w - m) / l turns a slot's e
+      // into the normalised probability.  A column whose keys are all masked
+      // (m at the mask value) gets factor 0: the reference's NaN -> 0 row.
       for (int j = ctid; j < NQ; j += ncompose) {
-        float m = -INFINITY;
-        for (int w = 0; w < nslots; ++w) m = fmaxf(m, redm[w * NQ + j]);
-        float l = 0.f;
-        for (int w = 0; w < nslots; ++w) {
-          const float mw = redm[w * NQ + j];
-          const float f = mw == -INFINITY ? 0.f : exp2f((mw - m) * sl2e);
-          redm[w * NQ + j] = f;
-          l += reds[w * NQ + j] * f;
+        float mw[8];
+        uint32_t sw[8];
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          mw[w] = w < nslots ? redm[w * NQ + j] : kMaskedLogit;
+          sw[w] = w < nslots ? reds[w * NQ + j] : 32u * 0x3F800000u;
         }
-        const float il = l > 0.f ? 1.f / l : 0.f;
-        for (int w = 0; w < nslots; ++w) redm[w * NQ + j] *= il;
+        float m = mw[0];
+#pragma unroll
+        for (int w = 1; w < 8; ++w) m = fmaxf(m, mw[w]);
+        float l = 0.f;
+#pragma unroll
+        for (int w = 0; w < 8; ++w) {
+          mw[w] = ptx::ex2(mw[w] - m);
+          l = fmaf(mw[w], static_cast<float>(sw[w] - 32u * 0x3F800000u) * 0x1p-23f, l);
+        }
+        const float il = (m > 0.5f * kMaskedLogit && l > 0.f) ? __frcp_rn(l) : 0.f;
+        const int h = j / BM, i = j % BM;
+#pragma unroll
+        for (int w = 0; w < 8; ++w)
+          if (w < nslots) fac[(w * BM + i) * HPG + h] = mw[w] * il;
       }
       ptx::named_bar_sync(1, ncompose);
+      // post-set key weights into the registers of the pre set (dead after
+      // pass 1); their latency overlaps building the next tile's matrices
+      if (active) load_key(p.post, 1.f, ktok, hbase, key_ok);
+      // the next tile's matrices, from the weights stored after pass 1
+      if (ntile < ntiles) build_m(buf ^ 1, ng);
       // P' of key tile 0 overwrites Q: every QK product of this tile must be complete
       if (ok && kt == 0 && nkt > 1) {
         ok = ptx::mbar_wait(bar_S + 2 * buf + nkt - 1, (it >> 1) & 1, WAIT);
@@ -1017,23 +1078,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
       }
 
       // ---- pass 2: normalise, post-composition, P' -> SMEM
-      if (PAIR && active) K2.set(kw1, kw2, kdd);
-      // fetch the next tile's records now (raw 16-bit); they land during pass 2
-      unsigned short nrv[MAXREC];
-      bool nhas[MAXREC];
-      const int ntile = tile + gridDim.x;
-      int nq0 = 0, nb = 0, ng = 0;
-      if (ntile < ntiles) {
-        tile_coords(ntile, nq0, nb, ng);
-#pragma unroll
-        for (int k = 0; k < MAXREC; ++k) {
-          const int idx = ctid + k * ncompose;
-          const unsigned short *src = idx < nrec ? rec_src(idx, nq0, nb, ng) : nullptr;
-          nhas[k] = src != nullptr;
-          nrv[k] = src ? __ldg(src) : (unsigned short)0;
-        }
-      }
-      const float *fac = redm + rw * NQ;
+      const float *fw = fac + rw * BM * HPG;
       unsigned char *pbase = p_tile(buf, kt) + (s_local & 7) * 16 + (s_local >> 3) * (BM * 16);
 #pragma unroll 1
       for (int grp = g_begin; grp < g_end; ++grp) {
@@ -1043,32 +1088,15 @@ __global__ void __launch_bounds__(32 * NW, 1)
 #pragma unroll
           for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
           ptx::tmem_wait_ld();
-          if constexpr (PAIR) {
 #pragma unroll
-            for (int ii = 0; ii < GI; ii += 2) {
-              ptx::f2_t a[HPG], o[HPG];
+          for (int ii = 0; ii < GI; ++ii) {
+            float a[HPG], o[HPG], f[HPG];
+            ld_row<HPG>(fw + (i0 + ii) * HPG, f);
 #pragma unroll
-              for (int h = 0; h < HPG; ++h) {
-                const float2 f = *reinterpret_cast<const float2 *>(fac + h * BM + i0 + ii);
-                a[h] = ptx::f2_mul(ptx::f2_pack(v[h][ii], v[h][ii + 1]), ptx::f2_pack(f.x, f.y));
-              }
-              compose2<HPG, R>(a, o, Wreg2, recb + (BM + i0 + ii) * geo.rec_floats, K2);
+            for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * f[h];
+            compose_m<HPG, R>(a, o, mcur + (BM + i0 + ii) * MF, kw1, kw2, kdd);
 #pragma unroll
-              for (int h = 0; h < HPG; ++h) {
-                v[h][ii] = ptx::f2_lo(o[h]);
-                v[h][ii + 1] = ptx::f2_hi(o[h]);
-              }
-            }
-          } else {
-#pragma unroll
-            for (int ii = 0; ii < GI; ++ii) {
-              float a[HPG], o[HPG];
-#pragma unroll
-              for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * fac[h * BM + i0 + ii];
-              compose<HPG, R>(a, o, Wreg, recb + (BM + i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
-#pragma unroll
-              for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
-            }
+            for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
           }
         } else {
 #pragma unroll
@@ -1082,14 +1110,11 @@ __global__ void __launch_bounds__(32 * NW, 1)
             unsigned char *tile_p = pbase + h * (rows_kt * BM * 2);
 #pragma unroll
             for (int c = 0; c < GI; c += 8 < GI ? 8 : GI) {
+              // up to 8 queries -> one 16-byte row of an 8x8 core matrix
               constexpr int W8 = GI < 8 ? GI : 8;
               uint32_t pk[W8 / 2];
 #pragma unroll
-              for (int u = 0; u < W8 / 2; ++u) {
-                const E lo = from_f<E>(v[h][c + 2 * u]), hi = from_f<E>(v[h][c + 2 * u + 1]);
-                pk[u] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&lo)) |
-                        (static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&hi)) << 16);
-              }
+              for (int u = 0; u < W8 / 2; ++u) pk[u] = pack2<E>(v[h][c + 2 * u], v[h][c + 2 * u + 1]);
               const int i = i0 + c;
               unsigned char *dst = tile_p + (i >> 3) * 128 + (i & 7) * 2;
               if constexpr (W8 == 8) {
@@ -1101,14 +1126,6 @@ __global__ void __launch_bounds__(32 * NW, 1)
               }
             }
           }
-        }
-      }
-      if (ntile < ntiles) {
-        float *nrec_buf = rec + ((it + 1) & 1) * nrec;
-#pragma unroll
-        for (int k = 0; k < MAXREC; ++k) {
-          const int idx = ctid + k * ncompose;
-          if (idx < nrec) rec_store(nrec_buf, idx, nrv[k], nhas[k], ng);
         }
       }
       ptx::fence_proxy_async_smem();
@@ -1178,6 +1195,8 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
   int nslot = 3;
   while (nslot > 2 && make_geo_p(HPG, R, rlast, nslot, p.G).total + 1024 > 227 * 1024) --nslot;
   const size_t smem = make_geo_p(HPG, R, rlast, nslot, p.G).total + 1024;
+  // the staged static mixes grow with G: past the shared-memory limit run the per-tile kernel
+  if (smem > 227 * 1024) return launch_t<E, HPG, R>(p, st);
   const int64_t sb = (int64_t)p.T * p.H * D, st_ = (int64_t)p.H * D, sh = D;
   CUtensorMap mq, mk, mv, mkl, mvl, mo;
   if (!make_map(&mq, p.q, p.dtype, p.B, p.T, p.H, BM, sb, st_, sh, true) ||
@@ -1185,7 +1204,7 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
       !make_map(&mv, p.v, p.dtype, p.B, p.T, p.H, KT_ROWS, sb, st_, sh, true) ||
       !make_map(&mkl, p.k, p.dtype, p.B, p.T, p.H, rlast, sb, st_, sh, true) ||
       !make_map(&mvl, p.v, p.dtype, p.B, p.T, p.H, rlast, sb, st_, sh, true) ||
-      !make_map(&mo, p.out, p.dtype, p.B, p.T, p.H, BM, p.out_sb, p.out_st, p.out_sh, false))
+      !make_map(&mo, p.out, p.dtype, p.B, p.T, p.H, BM < 32 ? BM : 32, p.out_sb, p.out_st, p.out_sh, false))
     return cudaErrorInvalidValue;
   TcParams tp;
   tp.B = p.B; tp.T = p.T; tp.H = p.H; tp.G = p.G; tp.window = p.window; tp.slen_default = p.T;
@@ -1201,7 +1220,7 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
   const WarpRoles roles = make_roles(nkt, rlast, CS, HPG);
   // the compose threads prefetch the next tile's per-query records, at most
   // 4 each (MAXREC in the kernel); otherwise run the per-tile kernel
-  if (roles.nwarps == 0 || roles.nwarps > 22 || 2 * BM * round_up(HPG * (2 * R + 1), 4) > 4 * 32 * roles.ncw)
+  if (roles.nwarps == 0 || roles.nwarps > 22 || 2 * BM * (2 * R + 1) > 4 * 32 * roles.ncw)
     return launch_t<E, HPG, R>(p, st);
   auto kern = roles.nwarps <= 16   ? dc_tcp_kernel<E, HPG, R, CS, 16>
               : roles.nwarps <= 18 ? dc_tcp_kernel<E, HPG, R, CS, 18>
