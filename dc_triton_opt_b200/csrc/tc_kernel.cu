@@ -579,24 +579,46 @@ __global__ void __launch_bounds__(32 * NW, 1)
   const int ntiles = nqb * p.B * p.G;
   const int H = p.H, T = p.T;
   const int rows_of[2] = {nkt == 1 ? rlast : KT_ROWS, rlast};
-  // K/V jobs of one tile: one per (key tile, head), except that the short last
-  // key tile of all heads is packed into a single job when it fits one slot
+  // K/V jobs of one tile: one per (key tile, head) for full key tiles.  The
+  // short last key tile is packed: all heads in one job when they fit a slot;
+  // when replicated (two copies of its K rows, see replicated_last) two heads
+  // per K job, laid out [head][d half][copy][rows] and read by the MMA from
+  // 128 - 2 * rlast rows before the copies, so that they land in TMEM lane
+  // quarters 2 and 3; its V then fits one packed job.
   const bool rep_last = replicated_last(nkt, rlast, HPG);
   const bool packed_last = !rep_last && HPG > 1 && HPG * rlast * 256 <= TILE_BYTES;
-  const int nK = HPG * (nkt - 1) + (packed_last ? 1 : HPG);
-  struct Job { int kt, h0, nh, rows, half; };  // half: byte distance of the d-halves
+  const int kph = rep_last ? (HPG < 2 ? HPG : 2) : 1;
+  const int nlastK = packed_last ? 1 : rep_last ? HPG / kph : HPG;
+  const bool vpack = packed_last || (rep_last && HPG > 1 && HPG * rlast * 256 <= TILE_BYTES);
+  const int nlastV = vpack ? 1 : HPG;
+  const int nfull = HPG * (nkt - 1);
+  const int nKk = nfull + nlastK, nKv = nfull + nlastV;
+  // half: byte distance of the d halves; aoff: start of the 128-row MMA operand
+  // relative to a head's data
+  struct Job { int kt, h0, nh, rows, half, ncopy, aoff; };
   // K jobs visit the last key tile first: its compose warps then start with
   // the others instead of one key-tile load later; V jobs keep key-tile order
   // (the first PV product of a tile initialises the accumulator)
-  const int nlast = packed_last ? 1 : HPG;
   auto job_of = [&](int jj, bool isv) {
-    if (!isv && nkt > 1) jj = jj < nlast ? HPG * (nkt - 1) + jj : jj - nlast;
+    if (!isv && nkt > 1) jj = jj < nlastK ? nfull + jj : jj - nlastK;
     Job j;
-    if (jj < HPG * (nkt - 1)) { j.kt = jj / HPG; j.h0 = jj % HPG; j.nh = 1; }
-    else if (packed_last) { j.kt = nkt - 1; j.h0 = 0; j.nh = HPG; }
-    else { j.kt = nkt - 1; j.h0 = jj - HPG * (nkt - 1); j.nh = 1; }
-    j.rows = rows_of[j.kt];
-    j.half = (packed_last && j.kt == nkt - 1) ? j.rows * 128 : TILE_BYTES / 2;
+    j.ncopy = 1;
+    j.aoff = 0;
+    if (jj < nfull) {
+      j.kt = jj / HPG; j.h0 = jj % HPG; j.nh = 1; j.rows = KT_ROWS; j.half = TILE_BYTES / 2;
+    } else {
+      const int l = jj - nfull;
+      j.kt = nkt - 1;
+      j.rows = rows_of[j.kt];
+      if (!isv && rep_last) {
+        j.nh = kph; j.h0 = l * kph; j.ncopy = 2; j.half = 2 * j.rows * 128;
+        j.aoff = -(KT_ROWS - 2 * j.rows) * 128;
+      } else if (isv ? vpack : packed_last) {
+        j.nh = HPG; j.h0 = 0; j.half = j.rows * 128;
+      } else {
+        j.nh = 1; j.h0 = l; j.half = TILE_BYTES / 2;
+      }
+    }
     return j;
   };
 
@@ -659,14 +681,12 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const bool last = jb.kt == nkt - 1;
       const CUtensorMap *m = isv ? (last ? &tm_vl : &tm_v) : (last ? &tm_kl : &tm_k);
       const int kb = q0 - p.window + 1;
-      const int ncopy = (!isv && last && rep_last) ? 2 : 1;  // K rows at 64 and 96 (see replicated_last)
-      if (lane == 0) ptx::mbar_expect_tx(bar_full + slot, ncopy * jb.nh * jb.rows * 256);
+      if (lane == 0) ptx::mbar_expect_tx(bar_full + slot, jb.ncopy * jb.nh * jb.rows * 256);
       __syncwarp();
       unsigned char *dst = smem + geo.ring_off + slot * TILE_BYTES;
-      if (lane < 2 * jb.nh * ncopy) {
+      if (lane < 2 * jb.nh * jb.ncopy) {
         const int c = lane & 1, u = (lane >> 1) % jb.nh, r = (lane >> 1) / jb.nh;
-        ptx::tma_load_4d(dst + u * 2 * jb.half + c * jb.half + (ncopy > 1 ? (r + 2) * 32 * 128 : 0), m,
-                         bar_full + slot, c * 64,
+        ptx::tma_load_4d(dst + u * 2 * jb.half + c * jb.half + r * jb.rows * 128, m, bar_full + slot, c * 64,
                          g * HPG + jb.h0 + u, kb + jb.kt * KT_ROWS, b);
       }
       __syncwarp();
@@ -688,13 +708,13 @@ __global__ void __launch_bounds__(32 * NW, 1)
                          c * 64, g * HPG + h, q0, b);
       }
       __syncwarp();
-      for (int jj = 0; jj < nK && ok; ++jj) load_kv(false, q0, b, g, jj);
+      for (int jj = 0; jj < nKk && ok; ++jj) load_kv(false, q0, b, g, jj);
       if (it >= 1)
-        for (int jj = 0; jj < nK && ok; ++jj) load_kv(true, pq0, pb, pg, jj);
+        for (int jj = 0; jj < nKv && ok; ++jj) load_kv(true, pq0, pb, pg, jj);
       pq0 = q0; pb = b; pg = g;
     }
     if (it >= 1)
-      for (int jj = 0; jj < nK && ok; ++jj) load_kv(true, pq0, pb, pg, jj);
+      for (int jj = 0; jj < nKv && ok; ++jj) load_kv(true, pq0, pb, pg, jj);
   } else if (role == ROLE_MMA) {
     // ================================================= MMA issuer
     // Whole warp runs the loops; one elected lane issues each tcgen05 op, with
@@ -717,7 +737,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
       const int buf = pit & 1;
       if (!wait_u(bar_P + buf, (pit >> 1) & 1, ERR_TIMEOUT_P)) return;
       ptx::tc_fence_after();
-      for (int jj = 0; jj < nK && ok; ++jj, ++job) {
+      for (int jj = 0; jj < nKv && ok; ++jj, ++job) {
         const int slot = job % nslot;
         if (!wait_u(bar_full + slot, (job / nslot) & 1, ERR_TIMEOUT_FULL)) return;
         ptx::tc_fence_after();
@@ -751,14 +771,16 @@ __global__ void __launch_bounds__(32 * NW, 1)
       if (!wait_u(bar_q + buf, (it >> 1) & 1, ERR_TIMEOUT_Q)) break;
       ptx::tc_fence_after();
       const uint64_t qd0 = ptx::smem_desc(ptx::smem_u32(smem + geo.q_off + buf * NQ * 256), 16, 1024, 2);
-      for (int jj = 0; jj < nK && ok; ++jj, ++job) {
+      for (int jj = 0; jj < nKk && ok; ++jj, ++job) {
         const int slot = job % nslot;
         if (!wait_u(bar_full + slot, (job / nslot) & 1, ERR_TIMEOUT_FULL)) break;
         ptx::tc_fence_after();
         const Job jb = job_of(jj, false);
         for (int u = 0; u < jb.nh; ++u) {
           const int h = jb.h0 + u;
-          const uint64_t ad = ptx::smem_desc(ring_addr + slot * TILE_BYTES + u * 2 * jb.half, 16, 1024, 2);
+          const uint64_t ad = ptx::smem_desc(
+              static_cast<uint32_t>(static_cast<int>(ring_addr + slot * TILE_BYTES + u * 2 * jb.half) + jb.aoff), 16,
+              1024, 2);
           const uint64_t bd = ptx::desc_add(qd0, h * BM * 256);
           const uint32_t dd = tbase + buf * 256 + jb.kt * KT_ROWS + h * BM;
 #pragma unroll
