@@ -260,6 +260,36 @@ __device__ __forceinline__ void compose_m(const float (&a)[HPG], float (&o)[HPG]
     for (int r = 0; r < R; ++r) o[h] = fmaf(kw2[r * HPG + h], ak[r], o[h]);
 }
 
+// compose_m for two queries at once on paired fp32 (.f32x2): lane x of a pair
+// is query i, lane y query i + 1; M2 holds the two queries' matrices
+// interleaved, [h'][h][query].  Per-key weights are duplicated pairs.  Each
+// half performs the operations of compose_m in the same order.
+template <int HPG, int R>
+__device__ __forceinline__ void compose_m2(const ptx::f2_t (&a)[HPG], ptx::f2_t (&o)[HPG], const float *M2,
+                                           const ptx::f2_t (&kw1)[HPG * R], const ptx::f2_t (&kw2)[R * HPG],
+                                           const ptx::f2_t (&kdd)[HPG]) {
+  ptx::f2_t ak[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    ak[r] = 0ull;
+#pragma unroll
+    for (int h = 0; h < HPG; ++h) ak[r] = ptx::f2_fma(kw1[h * R + r], a[h], ak[r]);
+  }
+#pragma unroll
+  for (int h = 0; h < HPG; ++h) o[h] = ptx::f2_mul(kdd[h], a[h]);
+#pragma unroll
+  for (int h1 = 0; h1 < HPG; ++h1) {
+    float mr[2 * HPG];
+    ld_row<2 * HPG>(M2 + h1 * 2 * HPG, mr);
+#pragma unroll
+    for (int h = 0; h < HPG; ++h) o[h] = ptx::f2_fma(ptx::f2_pack(mr[2 * h], mr[2 * h + 1]), a[h1], o[h]);
+  }
+#pragma unroll
+  for (int h = 0; h < HPG; ++h)
+#pragma unroll
+    for (int r = 0; r < R; ++r) o[h] = ptx::f2_fma(kw2[r * HPG + h], ak[r], o[h]);
+}
+
 // Two floats rounded to E (bf16 / fp16) and packed low | high << 16.
 template <typename E>
 __device__ __forceinline__ uint32_t pack2(float lo, float hi) {

@@ -554,6 +554,10 @@ __global__ void __launch_bounds__(32 * NW, 1)
   constexpr int BM = NQ / HPG;
   constexpr int GI = 32 / HPG;
   constexpr int NG = BM / GI;
+  // compose two queries per paired-fp32 instruction (compose_m2); at 8 heads
+  // per group the duplicated key weights and the wider rows spill, so those
+  // groups compose one query at a time
+  constexpr bool PAIR = HPG <= 4;
   static_assert(NG == 4 && NG % CS == 0, "group geometry");
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -915,15 +919,26 @@ __global__ void __launch_bounds__(32 * NW, 1)
         float m = Wt[((set * G + g) * HPG + h1) * HPG + h] + (h1 == h ? rr[h] : 0.f);
 #pragma unroll
         for (int r = 0; r < R; ++r) m = fmaf(rr[HPG + h1 * R + r], rr[HPG + HPG * R + r * HPG + h], m);
-        dst[idx] = set ? m : m * sl2e;
+        // with PAIR the pair layout [set][query / 2][h'][h][query % 2] (compose_m2)
+        dst[PAIR ? set * BM * MF + (i >> 1) * 2 * MF + (h1 * HPG + h) * 2 + (i & 1) : idx] = set ? m : m * sl2e;
       }
     };
+    // with PAIR the key's weights as duplicated pairs for compose_m2
+    ptx::f2_t kw1d[HPG * R], kw2d[R * HPG], kddd[HPG];
     auto load_key = [&](const TermPtrs &tm, float f, int64_t ktok, int hbase, bool key_ok) {
       load_key_weights_vec<E, HPG, R>(tm, ktok, H, hbase, key_ok, kw1, kw2, kdd);
 #pragma unroll
       for (int j = 0; j < R * HPG; ++j) kw2[j] *= f;
 #pragma unroll
       for (int j = 0; j < HPG; ++j) kdd[j] *= f;
+      if constexpr (PAIR) {
+#pragma unroll
+        for (int j = 0; j < HPG * R; ++j) kw1d[j] = ptx::f2_dup(kw1[j]);
+#pragma unroll
+        for (int j = 0; j < R * HPG; ++j) kw2d[j] = ptx::f2_dup(kw2[j]);
+#pragma unroll
+        for (int j = 0; j < HPG; ++j) kddd[j] = ptx::f2_dup(kdd[j]);
+      }
     };
 
     int it = 0;
@@ -997,26 +1012,45 @@ __global__ void __launch_bounds__(32 * NW, 1)
 #pragma unroll
           for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
           ptx::tmem_wait_ld();
-          if (all_valid(q0 + i0)) {
+          // with PAIR, queries in pairs on .f32x2 (pair base (i0 + ii) * MF in the pair layout)
+          if constexpr (!PAIR) {
+            const bool full = all_valid(q0 + i0);
 #pragma unroll
             for (int ii = 0; ii < GI; ++ii) {
               float a[HPG], o[HPG];
 #pragma unroll
               for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
               compose_m<HPG, R>(a, o, mcur + (i0 + ii) * MF, kw1, kw2, kdd);
+              const bool vl = full || valid(q0 + i0 + ii);
 #pragma unroll
-              for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
+              for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : kMaskedLogit;
+            }
+          } else if (all_valid(q0 + i0)) {
+#pragma unroll
+            for (int ii = 0; ii < GI; ii += 2) {
+              ptx::f2_t a[HPG], o[HPG];
+#pragma unroll
+              for (int h = 0; h < HPG; ++h) a[h] = ptx::f2_pack(v[h][ii], v[h][ii + 1]);
+              compose_m2<HPG, R>(a, o, mcur + (i0 + ii) * MF, kw1d, kw2d, kddd);
+#pragma unroll
+              for (int h = 0; h < HPG; ++h) {
+                v[h][ii] = ptx::f2_lo(o[h]);
+                v[h][ii + 1] = ptx::f2_hi(o[h]);
+              }
             }
           } else {
 #pragma unroll
-            for (int ii = 0; ii < GI; ++ii) {
-              float a[HPG], o[HPG];
+            for (int ii = 0; ii < GI; ii += 2) {
+              ptx::f2_t a[HPG], o[HPG];
 #pragma unroll
-              for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
-              compose_m<HPG, R>(a, o, mcur + (i0 + ii) * MF, kw1, kw2, kdd);
-              const bool vl = valid(q0 + i0 + ii);
+              for (int h = 0; h < HPG; ++h) a[h] = ptx::f2_pack(v[h][ii], v[h][ii + 1]);
+              compose_m2<HPG, R>(a, o, mcur + (i0 + ii) * MF, kw1d, kw2d, kddd);
+              const bool vl0 = valid(q0 + i0 + ii), vl1 = valid(q0 + i0 + ii + 1);
 #pragma unroll
-              for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : kMaskedLogit;
+              for (int h = 0; h < HPG; ++h) {
+                v[h][ii] = vl0 ? ptx::f2_lo(o[h]) : kMaskedLogit;
+                v[h][ii + 1] = vl1 ? ptx::f2_hi(o[h]) : kMaskedLogit;
+              }
             }
           }
 #pragma unroll
@@ -1085,7 +1119,8 @@ __global__ void __launch_bounds__(32 * NW, 1)
         const int h = j / BM, i = j % BM;
 #pragma unroll
         for (int w = 0; w < 8; ++w)
-          if (w < nslots) fac[(w * BM + i) * HPG + h] = mw[w] * il;
+          if (w < nslots)
+            fac[w * BM * HPG + (PAIR ? (i >> 1) * 2 * HPG + h * 2 + (i & 1) : i * HPG + h)] = mw[w] * il;
       }
       ptx::named_bar_sync(1, ncompose);
       // post-set key weights into the registers of the pre set (dead after
@@ -1110,15 +1145,32 @@ __global__ void __launch_bounds__(32 * NW, 1)
 #pragma unroll
           for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
           ptx::tmem_wait_ld();
+          if constexpr (!PAIR) {
 #pragma unroll
-          for (int ii = 0; ii < GI; ++ii) {
-            float a[HPG], o[HPG], f[HPG];
-            ld_row<HPG>(fw + (i0 + ii) * HPG, f);
+            for (int ii = 0; ii < GI; ++ii) {
+              float a[HPG], o[HPG], f[HPG];
+              ld_row<HPG>(fw + (i0 + ii) * HPG, f);
 #pragma unroll
-            for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * f[h];
-            compose_m<HPG, R>(a, o, mcur + (BM + i0 + ii) * MF, kw1, kw2, kdd);
+              for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * f[h];
+              compose_m<HPG, R>(a, o, mcur + (BM + i0 + ii) * MF, kw1, kw2, kdd);
 #pragma unroll
-            for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
+              for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
+            }
+          } else
+#pragma unroll
+          for (int ii = 0; ii < GI; ii += 2) {
+            ptx::f2_t a[HPG], o[HPG];
+            float f[2 * HPG];
+            ld_row<2 * HPG>(fw + (i0 + ii) * HPG, f);  // factors [query / 2][h][query % 2]
+#pragma unroll
+            for (int h = 0; h < HPG; ++h)
+              a[h] = ptx::f2_mul(ptx::f2_pack(v[h][ii], v[h][ii + 1]), ptx::f2_pack(f[2 * h], f[2 * h + 1]));
+            compose_m2<HPG, R>(a, o, mcur + (BM + i0 + ii) * MF, kw1d, kw2d, kddd);
+#pragma unroll
+            for (int h = 0; h < HPG; ++h) {
+              v[h][ii] = ptx::f2_lo(o[h]);
+              v[h][ii + 1] = ptx::f2_hi(o[h]);
+            }
           }
         } else {
 #pragma unroll
