@@ -73,6 +73,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
   return true;
 }
 
+// mbar_wait for the warps that only load and issue (TMA, MMA, epilogue): the
+// thread polls and sleeps `backoff_ns` between polls, so that a waiting warp
+// takes almost no issue slots from the compute warps of its sub-partition.
+__device__ __forceinline__ bool mbar_wait_backoff(uint64_t *bar, uint32_t parity, uint32_t limit_us,
+                                                  uint32_t backoff_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t deadline = globaltimer_ns() + static_cast<uint64_t>(limit_us) * 1000ull;
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() > deadline) return false;
+    __nanosleep(backoff_ns);
+  }
+  return true;
+}
+
 // ---------------------------------------------------------------- fences
 __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");

@@ -671,7 +671,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     int job = 0;
     bool ok = !p.skip_loads;
     auto wait_all = [&](uint64_t *bar, int parity, int code) {
-      const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait(bar, parity, WAIT));
+      const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait_backoff(bar, parity, WAIT, 64));
       if (ok && !got) {
         ok = false;
         if (lane == 0) record_err(p, code);
@@ -730,7 +730,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
     int job = 0;
     bool ok = true;
     auto wait_u = [&](uint64_t *bar, int parity, int code) {
-      const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait(bar, parity, WAIT));
+      const bool got = __all_sync(0xffffffffu, ok && ptx::mbar_wait_backoff(bar, parity, WAIT, 64));
       if (ok && !got) {
         ok = false;
         if (lane == 0) record_err(p, code);
@@ -817,7 +817,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
       int q0, b, g;
       tile_coords(tile, q0, b, g);
       const int buf = it & 1;
-      if (!ptx::mbar_wait(bar_O + buf, (it >> 1) & 1, WAIT)) { record_err(p, ERR_TIMEOUT_O); break; }
+      if (!ptx::mbar_wait_backoff(bar_O + buf, (it >> 1) & 1, WAIT, 256)) { record_err(p, ERR_TIMEOUT_O); break; }
       ptx::tc_fence_after();
 #pragma unroll 1
       for (int c = 0; c < NQ / 32; ++c) {
