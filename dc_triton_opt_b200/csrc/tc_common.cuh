@@ -26,13 +26,13 @@ enum Err { ERR_TIMEOUT_Q = 1, ERR_TIMEOUT_FULL = 2, ERR_TIMEOUT_FREE = 3, ERR_TI
 struct Geo {
   int nkt, nslot;
   int q_off, ring_off, p_off, misc_off;
-  int wz_off, rec_off, red_off, bar_off, tmem_off;
-  int rec_floats;  // per (set, query) record: dq[HPG] | qa[HPG*R] | qb[R*HPG], padded to 4
+  int rec_off, mrec_off, red_off, fac_off, bar_off, tmem_off;
   int total;
 };
 
 __host__ __device__ constexpr int round_up(int x, int a) { return (x + a - 1) / a * a; }
 
+// Shared memory of the one-tile-per-CTA kernel (dc_tc_kernel).
 __host__ __device__ inline Geo make_geo(int HPG, int R, int nkt) {
   Geo g{};
   const int BM = NQ / HPG;
@@ -42,11 +42,11 @@ __host__ __device__ inline Geo make_geo(int HPG, int R, int nkt) {
   g.ring_off = g.q_off + NQ * 256;
   g.p_off = g.ring_off + g.nslot * TILE_BYTES;
   g.misc_off = g.p_off + nkt * NQ * KT_ROWS * 2;
-  g.rec_floats = round_up(HPG * (2 * R + 1), 4);
   int o = g.misc_off;
-  g.wz_off = o;   o += 2 * HPG * HPG * 4;
-  g.rec_off = round_up(o, 16); o = g.rec_off + 2 * BM * g.rec_floats * 4;
-  g.red_off = o;  o += 2 * 4 * nkt * NQ * 4;
+  g.rec_off = round_up(o, 16); o = g.rec_off + 2 * BM * HPG * (2 * R + 1) * 4;  // per-query weights
+  g.mrec_off = round_up(o, 16); o = g.mrec_off + 2 * BM * HPG * HPG * 4;         // mixing matrices
+  g.red_off = round_up(o, 16); o = g.red_off + 2 * 4 * nkt * NQ * 4;             // column maxima | sums
+  g.fac_off = o; o += 4 * nkt * NQ * 4;                                          // probability factors
   g.bar_off = round_up(o, 8); o = g.bar_off + 16 * 8;
   g.tmem_off = o; o += 16;
   g.total = o;

@@ -48,8 +48,6 @@ __global__ void __launch_bounds__(MAXT, 1)
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                           ~static_cast<uintptr_t>(1023));
   const Geo geo = make_geo(HPG, R, nkt);
-  float *Wz = reinterpret_cast<float *>(smem + geo.wz_off);      // [2][HPG*HPG]
-  float *rec = reinterpret_cast<float *>(smem + geo.rec_off);    // [2][BM][rec_floats]
   float *red = reinterpret_cast<float *>(smem + geo.red_off);    // [2][4*nkt][NQ]
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + geo.bar_off);
   uint64_t *bar_q = bars + 0, *bar_full = bars + 1, *bar_free = bars + 4;
@@ -187,34 +185,35 @@ __global__ void __launch_bounds__(MAXT, 1)
     __syncwarp();
   } else {
     // ================================================= compose warps
-    // stage the static mix and the per-query weights (fp32) while the first loads fly
-    for (int idx = threadIdx.x; idx < 2 * HPG * HPG; idx += ncompose) {
-      const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
-      const TermPtrs &tm = set ? p.post : p.pre;
-      const int h = j / HPG, hp = j % HPG;
-      Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
-    }
-    for (int idx = threadIdx.x; idx < 2 * BM * geo.rec_floats; idx += ncompose) {
-      const int set = idx / (BM * geo.rec_floats), rem = idx % (BM * geo.rec_floats);
-      const int i = rem / geo.rec_floats, j = rem % geo.rec_floats;
+    // Composition as in dc_tcp_kernel: per-query mixing matrices M_t (every
+    // query-dependent term of a set folded into one HPG x HPG matrix, the pre
+    // set scaled by scale * log2(e)), key weights in registers, two queries per
+    // paired-fp32 instruction at 1-4 heads per group, fixed-point warp sums.
+    constexpr bool PAIR = HPG <= 4;
+    constexpr int RAWF = HPG * (2 * R + 1), MF = HPG * HPG, NCK = 2 * R + 1, NCH = 2 * BM * NCK;
+    float *raw = reinterpret_cast<float *>(smem + geo.rec_off);    // [set][BM][RAWF]
+    float *mrec = reinterpret_cast<float *>(smem + geo.mrec_off);  // [set][BM][h'][h] (pair layout with PAIR)
+    float *redm = red;                                             // [4*nkt][NQ] column maxima (base 2)
+    uint32_t *reds = reinterpret_cast<uint32_t *>(red + 4 * nkt * NQ);  // [4*nkt][NQ] fixed-point sums
+    float *fac = reinterpret_cast<float *>(smem + geo.fac_off);    // [4*nkt][BM][HPG] (pair layout with PAIR)
+    const float sl2e = p.scale * kLog2e;
+    // per-query weights of the block in chunks of HPG contiguous elements:
+    // chunk (set, query i, k), k = 0: qdd; 1..R: qw1 [h][r]; R+1..2R: qw2 [r][h]
+    for (int c = threadIdx.x; c < NCH; c += ncompose) {
+      const int set = c / (BM * NCK), rem = c % (BM * NCK), i = rem / NCK, k = rem % NCK;
       const TermPtrs &tm = set ? p.post : p.pre;
       const int t = q0 + i;
-      float val = 0.f;
+      const int64_t tok = (int64_t)b * T + t;
+      const E *src = nullptr;
       if (t < T) {
-        const int64_t tok = (int64_t)b * T + t;
-        if (j < HPG) {
-          const int h = j;
-          val = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)g * HPG + h) * HPG + h] : 0.f) +
-                (tm.qdd ? ld_w<E>(tm.qdd, tok * H + hbase + h) : 0.f);
-        } else if (j < HPG + HPG * R) {
-          const int h = (j - HPG) / R, r = (j - HPG) % R;
-          val = tm.qw1 ? ld_w<E>(tm.qw1, (tok * H + hbase + h) * R + r) : 0.f;
-        } else if (j < HPG + 2 * HPG * R) {
-          const int r = (j - HPG - HPG * R) / HPG, h = (j - HPG - HPG * R) % HPG;
-          val = tm.qw2 ? ld_w<E>(tm.qw2, (tok * R + r) * H + hbase + h) : 0.f;
-        }
+        if (k == 0) src = tm.qdd ? elem<E>(tm.qdd, tok * H + hbase) : nullptr;
+        else if (k <= R) src = tm.qw1 ? elem<E>(tm.qw1, (tok * H + hbase) * R + (k - 1) * HPG) : nullptr;
+        else src = tm.qw2 ? elem<E>(tm.qw2, (tok * R + (k - 1 - R)) * H + hbase) : nullptr;
       }
-      rec[idx] = val;
+      const Raw16<HPG> v = src ? ld_raw16<HPG>(src) : raw16_zero<HPG>();
+      float *dst = raw + (set * BM + i) * RAWF + k * HPG;
+#pragma unroll
+      for (int h = 0; h < HPG; ++h) dst[h] = raw16_get<E, HPG>(v, h);
     }
     // warp -> (lane quarter sub, key tile kt, column half cs); warps sharing
     // (sub, kt) split the NG column groups of the tile between them
@@ -225,112 +224,155 @@ __global__ void __launch_bounds__(MAXT, 1)
     const int s = kb + kt * KT_ROWS + s_local;    // absolute key index
     const bool key_ok = s >= 0 && s < slen;
     const uint32_t tl = tbase + (static_cast<uint32_t>(32 * sub) << 16) + kt * KT_ROWS;
-    // does any (query, key) pair of this warp survive the mask?
-    const int wk0 = kb + kt * KT_ROWS + 32 * sub, wk1 = wk0 + 31;
+    const int wk0 = kb + kt * KT_ROWS + 32 * sub;
     const int klo = max(0, kb), khi = min(q0 + BM - 1, slen - 1);
-    const bool active = wk1 >= klo && wk0 <= khi;
+    const bool active = wk0 + 31 >= klo && wk0 <= khi;
     const int64_t ktok = (int64_t)b * T + s;
-    // softmax scale folded into the exponent: composition is linear, so
-    // softmax(compose(scale*L)) = softmax(scale*compose(L)) for scale > 0
-    const float sl2e = p.scale * kLog2e;
+    const bool keys_in = wk0 >= 0 && wk0 + 31 < slen;
+    auto all_valid = [&](int t0) {
+      return keys_in && wk0 + 31 <= t0 && t0 + GI - 1 - wk0 < p.window && t0 + GI - 1 < T;
+    };
+    auto valid = [&](int t) { return key_ok && s <= t && t - s < p.window && t < T; };
     bool ok = true;
 
-    WSrc<HPG> Wreg;
     float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
-
-    auto valid = [&](int t) { return key_ok && s <= t && t - s < p.window && t < T; };
-    auto col_of = [&](int L, int i0) { return (L / GI) * BM + i0 + (L % GI); };
-    float *redm = red;                  // [4*nkt][NQ] warp-local column max, later the scale factor
-    float *reds = red + 4 * nkt * NQ;   // [4*nkt][NQ] warp-local column sums
-
-    if (active) load_key_weights<E, HPG, R>(p.pre, ktok, H, hbase, key_ok, kw1, kw2, kdd);
-    ptx::named_bar_sync(1, ncompose);  // staged weights visible
-    if (active) {
-Wreg.load(Wz);
+    ptx::f2_t kw1d[HPG * R], kw2d[R * HPG], kddd[HPG];
+    auto load_key = [&](const TermPtrs &tm, float f) {
+      load_key_weights_vec<E, HPG, R>(tm, ktok, H, hbase, key_ok && active, kw1, kw2, kdd);
+#pragma unroll
+      for (int j = 0; j < R * HPG; ++j) kw2[j] *= f;
+#pragma unroll
+      for (int j = 0; j < HPG; ++j) kdd[j] *= f;
+      if constexpr (PAIR) {
+#pragma unroll
+        for (int j = 0; j < HPG * R; ++j) kw1d[j] = ptx::f2_dup(kw1[j]);
+#pragma unroll
+        for (int j = 0; j < R * HPG; ++j) kw2d[j] = ptx::f2_dup(kw2[j]);
+#pragma unroll
+        for (int j = 0; j < HPG; ++j) kddd[j] = ptx::f2_dup(kdd[j]);
+      }
+    };
+    load_key(p.pre, sl2e);
+    ptx::named_bar_sync(1, ncompose);  // per-query weights staged
+    for (int idx = threadIdx.x; idx < 2 * BM * MF; idx += ncompose) {
+      const int set = idx / (BM * MF), i = (idx / MF) % BM, h1 = (idx % MF) / HPG, h = idx % HPG;
+      const TermPtrs &tm = set ? p.post : p.pre;
+      const float *rr = raw + (set * BM + i) * RAWF;
+      float m = (tm.w ? tm.w[((int64_t)g * HPG + h1) * HPG + h] : 0.f) + (h1 == h ? (tm.identity ? 1.f : 0.f) + rr[h] : 0.f);
+#pragma unroll
+      for (int r = 0; r < R; ++r) m = fmaf(rr[HPG + h1 * R + r], rr[HPG + HPG * R + r * HPG + h], m);
+      mrec[PAIR ? set * BM * MF + (i >> 1) * 2 * MF + (h1 * HPG + h) * 2 + (i & 1) : idx] = set ? m : m * sl2e;
     }
+    ptx::named_bar_sync(1, ncompose);  // matrices visible
     if (!ptx::mbar_wait(bar_S + kt, 0, p.wait_us)) { ok = false; record_err(p, ERR_TIMEOUT_S); }
     ptx::tc_fence_after();
 
-    // ---- pass 1: pre-composition + mask, warp-local column max (redux), e = exp(S - m_w),
-    //      warp-local column sums (shuffle transpose-reduce); e written back to TMEM
+    // ---- pass 1: pre-composition (+ mask at the window's edges), warp-local column max,
+    //      e = 2^(S - m_w) back to TMEM, fixed-point warp-local column sums
 #pragma unroll 1
     for (int grp = g_begin; grp < g_end; ++grp) {
       const int i0 = grp * GI;
-      float mine_m = -INFINITY, mine_s = 0.f;
+      float *mx = redm + rw * NQ + i0;
+      uint32_t *sx = reds + rw * NQ + i0;
       if (active && ok) {
         float v[HPG][GI];
 #pragma unroll
         for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
         ptx::tmem_wait_ld();
+        const bool full = all_valid(q0 + i0);
+        if constexpr (PAIR) {
 #pragma unroll
-        for (int ii = 0; ii < GI; ++ii) {
-          float a[HPG], o[HPG];
+          for (int ii = 0; ii < GI; ii += 2) {
+            ptx::f2_t a[HPG], o[HPG];
 #pragma unroll
-          for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
-          compose<HPG, R>(a, o, Wreg, rec + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
-          const bool vl = valid(q0 + i0 + ii);
+            for (int h = 0; h < HPG; ++h) a[h] = ptx::f2_pack(v[h][ii], v[h][ii + 1]);
+            compose_m2<HPG, R>(a, o, mrec + (i0 + ii) * MF, kw1d, kw2d, kddd);
+            const bool vl0 = full || valid(q0 + i0 + ii), vl1 = full || valid(q0 + i0 + ii + 1);
 #pragma unroll
-          for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : -INFINITY;
-        }
-#pragma unroll
-        for (int h = 0; h < HPG; ++h)
+            for (int h = 0; h < HPG; ++h) {
+              v[h][ii] = vl0 ? ptx::f2_lo(o[h]) : kMaskedLogit;
+              v[h][ii + 1] = vl1 ? ptx::f2_hi(o[h]) : kMaskedLogit;
+            }
+          }
+        } else {
 #pragma unroll
           for (int ii = 0; ii < GI; ++ii) {
-            const float mw = ptx::warp_max(v[h][ii]);
-            if (lane == h * GI + ii) mine_m = mw;
-            v[h][ii] = exp2f((v[h][ii] - (mw == -INFINITY ? 0.f : mw)) * sl2e);
+            float a[HPG], o[HPG];
+#pragma unroll
+            for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
+            compose_m<HPG, R>(a, o, mrec + (i0 + ii) * MF, kw1, kw2, kdd);
+            const bool vl = full || valid(q0 + i0 + ii);
+#pragma unroll
+            for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : kMaskedLogit;
           }
+        }
+#pragma unroll
+        for (int h = 0; h < HPG; ++h) {
+          float m8[GI];
+          uint32_t s8[GI];
+#pragma unroll
+          for (int ii = 0; ii < GI; ++ii) {
+            m8[ii] = ptx::warp_max(v[h][ii]);
+            v[h][ii] = ptx::ex2(v[h][ii] - m8[ii]);
+            s8[ii] = ptx::warp_sum_u32(__float_as_uint(v[h][ii] + 1.f));
+          }
+          if (lane == 0) {
+#pragma unroll
+            for (int ii = 0; ii < GI; ii += 4) {
+              *reinterpret_cast<float4 *>(mx + h * BM + ii) = make_float4(m8[ii], m8[ii + 1], m8[ii + 2], m8[ii + 3]);
+              *reinterpret_cast<uint4 *>(sx + h * BM + ii) = make_uint4(s8[ii], s8[ii + 1], s8[ii + 2], s8[ii + 3]);
+            }
+          }
+        }
 #pragma unroll
         for (int h = 0; h < HPG; ++h) ptx::tmem_st<GI>(tl + h * BM + i0, v[h]);
-        float x[32];
+      } else if (lane == 0) {
 #pragma unroll
         for (int h = 0; h < HPG; ++h)
 #pragma unroll
-          for (int ii = 0; ii < GI; ++ii) x[h * GI + ii] = v[h][ii];
-        // transpose-reduce: afterwards lane L holds the column sum of value L
-#pragma unroll
-        for (int off = 16, cnt = 32; off >= 1; off >>= 1, cnt >>= 1) {
-          const bool upper = (lane & off) != 0;
-#pragma unroll
-          for (int j = 0; j < cnt / 2; ++j) {
-            const float send = upper ? x[j] : x[j + cnt / 2];
-            const float keep = upper ? x[j + cnt / 2] : x[j];
-            x[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
+          for (int ii = 0; ii < GI; ii += 4) {
+            *reinterpret_cast<float4 *>(mx + h * BM + ii) =
+                make_float4(kMaskedLogit, kMaskedLogit, kMaskedLogit, kMaskedLogit);
+            *reinterpret_cast<uint4 *>(sx + h * BM + ii) = make_uint4(0u, 0u, 0u, 0u);
           }
-        }
-        mine_s = x[0];
       }
-      redm[rw * NQ + col_of(lane, i0)] = mine_m;
-      reds[rw * NQ + col_of(lane, i0)] = mine_s;
     }
-    // the post-set weights replace the pre-set ones (dead after pass 1); issued
-    // here, their latency overlaps the column reduction and its two barriers
-    if (active) {
-      Wreg.load(Wz + HPG * HPG);
-      load_key_weights<E, HPG, R>(p.post, ktok, H, hbase, key_ok, kw1, kw2, kdd);
-    }
+    // the post-set key weights replace the pre-set ones (dead after pass 1)
+    load_key(p.post, 1.f);
     ptx::tmem_wait_st();
     ptx::named_bar_sync(1, ncompose);
-    // combine the warps of each column: m = max_w m_w, l = sum_w s_w 2^((m_w - m) sl2e);
-    // factor_w = 2^((m_w - m) sl2e) / l turns e_w into the normalised probability
-    if (threadIdx.x < NQ) {
-      const int j = threadIdx.x;
-      float m = -INFINITY;
-      for (int w = 0; w < 4 * nkt; ++w) m = fmaxf(m, redm[w * NQ + j]);
-      float l = 0.f;
-      for (int w = 0; w < 4 * nkt; ++w) {
-        const float mw = redm[w * NQ + j];
-        const float f = mw == -INFINITY ? 0.f : exp2f((mw - m) * sl2e);
-        redm[w * NQ + j] = f;
-        l += reds[w * NQ + j] * f;
+    // combine the slots of each column: m = max_w m_w, l = sum_w sum_w 2^(m_w - m),
+    // factor_w = 2^(m_w - m) / l; an all-masked column gets factor 0
+    constexpr int MAXSL = 12;  // 4 lane quarters x at most 3 key tiles
+    const int nslots = 4 * nkt;
+    for (int j = threadIdx.x; j < NQ; j += ncompose) {
+      float mw[MAXSL];
+      uint32_t sw[MAXSL];
+#pragma unroll
+      for (int w = 0; w < MAXSL; ++w) {
+        mw[w] = w < nslots ? redm[w * NQ + j] : kMaskedLogit;
+        sw[w] = w < nslots ? reds[w * NQ + j] : 32u * 0x3F800000u;
       }
-      const float il = l > 0.f ? 1.f / l : 0.f;
-      for (int w = 0; w < 4 * nkt; ++w) redm[w * NQ + j] *= il;
+      float m = mw[0];
+#pragma unroll
+      for (int w = 1; w < MAXSL; ++w) m = fmaxf(m, mw[w]);
+      float l = 0.f;
+#pragma unroll
+      for (int w = 0; w < MAXSL; ++w) {
+        mw[w] = ptx::ex2(mw[w] - m);
+        l = fmaf(mw[w], static_cast<float>(sw[w] - 32u * 0x3F800000u) * 0x1p-23f, l);
+      }
+      const float il = (m > 0.5f * kMaskedLogit && l > 0.f) ? __frcp_rn(l) : 0.f;
+      const int h = j / BM, i = j % BM;
+#pragma unroll
+      for (int w = 0; w < MAXSL; ++w)
+        if (w < nslots)
+          fac[w * BM * HPG + (PAIR ? (i >> 1) * 2 * HPG + h * 2 + (i & 1) : i * HPG + h)] = mw[w] * il;
     }
     ptx::named_bar_sync(1, ncompose);
 
     // ---- pass 2: normalise, post-composition, P' -> SMEM (PV B operand)
-    const float *fac = redm + rw * NQ;
+    const float *fw = fac + rw * BM * HPG;
     unsigned char *prow = smem + geo.p_off + (s_local & 7) * 16 + (s_local >> 3) * (BM * 16);
 #pragma unroll 1
     for (int grp = g_begin; grp < g_end; ++grp) {
@@ -340,14 +382,33 @@ Wreg.load(Wz);
 #pragma unroll
         for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
         ptx::tmem_wait_ld();
+        if constexpr (PAIR) {
 #pragma unroll
-        for (int ii = 0; ii < GI; ++ii) {
-          float a[HPG], o[HPG];
+          for (int ii = 0; ii < GI; ii += 2) {
+            ptx::f2_t a[HPG], o[HPG];
+            float f[2 * HPG];
+            ld_row<2 * HPG>(fw + (i0 + ii) * HPG, f);
 #pragma unroll
-          for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * fac[h * BM + i0 + ii];
-          compose<HPG, R>(a, o, Wreg, rec + (BM + i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
+            for (int h = 0; h < HPG; ++h)
+              a[h] = ptx::f2_mul(ptx::f2_pack(v[h][ii], v[h][ii + 1]), ptx::f2_pack(f[2 * h], f[2 * h + 1]));
+            compose_m2<HPG, R>(a, o, mrec + (BM + i0 + ii) * MF, kw1d, kw2d, kddd);
 #pragma unroll
-          for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
+            for (int h = 0; h < HPG; ++h) {
+              v[h][ii] = ptx::f2_lo(o[h]);
+              v[h][ii + 1] = ptx::f2_hi(o[h]);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int ii = 0; ii < GI; ++ii) {
+            float a[HPG], o[HPG], f[HPG];
+            ld_row<HPG>(fw + (i0 + ii) * HPG, f);
+#pragma unroll
+            for (int h = 0; h < HPG; ++h) a[h] = v[h][ii] * f[h];
+            compose_m<HPG, R>(a, o, mrec + (BM + i0 + ii) * MF, kw1, kw2, kdd);
+#pragma unroll
+            for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
+          }
         }
       } else {
 #pragma unroll
@@ -364,11 +425,7 @@ Wreg.load(Wz);
           constexpr int W8 = GI < 8 ? GI : 8;
           uint32_t pk[W8 / 2];
 #pragma unroll
-          for (int u = 0; u < W8 / 2; ++u) {
-            const E lo = from_f<E>(v[h][c + 2 * u]), hi = from_f<E>(v[h][c + 2 * u + 1]);
-            pk[u] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&lo)) |
-                    (static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&hi)) << 16);
-          }
+          for (int u = 0; u < W8 / 2; ++u) pk[u] = pack2<E>(v[h][c + 2 * u], v[h][c + 2 * u + 1]);
           const int i = i0 + c;
           unsigned char *dst = tile + (i >> 3) * 128 + (i & 7) * 2;
           if constexpr (W8 == 8) {
