@@ -1,8 +1,8 @@
 // Two-pass streaming tensor-core DC-attention forward (sm_100a).
 //
 // Covers what the single-pass kernels of tc_kernel.cu cannot hold on chip:
-// full-causal layers (config 3 of the benchmark), windows longer than three
-// key tiles, and head groups of 16.  One CTA owns (query block, batch, head
+// full-causal layers (config 3 of the benchmark) and windows longer than
+// three key tiles, at up to 8 heads per group.  One CTA owns (query block, batch, head
 // group) and streams the block's key range [k_lo, q0 + BM) in tiles of 128
 // keys, twice:
 //   pass A  S^T = K Q^T per head (TMEM) -> pre-composition -> mask ->
@@ -46,7 +46,7 @@ struct Shape {
 };
 
 struct GeoS {
-  int q_off, ring_off, p_off, wz_off, rec_off, red_off, stat_off, bar_off, tmem_off, total, rec_floats;
+  int q_off, ring_off, p_off, raw_off, mrec_off, red_off, stat_off, scr_off, bar_off, tmem_off, total;
 };
 
 template <int HPG, int R>
@@ -57,11 +57,11 @@ __host__ __device__ inline GeoS make_geo_s() {
   g.ring_off = S::NQT * 256;
   g.p_off = g.ring_off + S::NSLOT * TILE_BYTES;
   int o = g.p_off + S::NPB * KT_ROWS * S::NQT * 2;
-  g.rec_floats = round_up(HPG * (2 * R + 1), 4);
-  g.wz_off = o; o += 2 * HPG * HPG * 4;
-  g.rec_off = round_up(o, 16); o = g.rec_off + 2 * S::BM * g.rec_floats * 4;
-  g.red_off = o; o += 2 * 4 * S::NQT * 4;   // per lane quarter: running max, running sum
-  g.stat_off = o; o += 2 * S::NQT * 4;      // combined: max, 1 / sum
+  g.raw_off = round_up(o, 16); o = g.raw_off + 2 * S::BM * HPG * (2 * R + 1) * 4;  // per-query weights
+  g.mrec_off = round_up(o, 16); o = g.mrec_off + 2 * S::BM * HPG * HPG * 4;        // mixing matrices
+  g.red_off = round_up(o, 16); o = g.red_off + 2 * 4 * S::NQT * 4;  // per lane quarter: running max, sum
+  g.stat_off = o; o += 2 * S::NQT * 4;                              // combined [query][head]: max, 1 / sum
+  g.scr_off = round_up(o, 16); o = g.scr_off + NCW * 64 * 4;        // per warp: 32 maxima, 32 sums
   g.bar_off = round_up(o, 8); o = g.bar_off + 24 * 8;
   g.tmem_off = o; o += 16;
   g.total = o;
@@ -83,8 +83,6 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                           ~static_cast<uintptr_t>(1023));
   const GeoS geo = make_geo_s<HPG, R>();
-  float *Wz = reinterpret_cast<float *>(smem + geo.wz_off);
-  float *rec = reinterpret_cast<float *>(smem + geo.rec_off);
   float *redm = reinterpret_cast<float *>(smem + geo.red_off), *reds = redm + 4 * NQT;
   float *mval = reinterpret_cast<float *>(smem + geo.stat_off), *linv = mval + NQT;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + geo.bar_off);
@@ -242,51 +240,109 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
     __syncwarp();
   } else {
     // ================================================= compose warps
+    // Composition as in the single-pass kernels (tc_kernel.cu): per-query
+    // mixing matrices M_t built once per CTA (the pre set scaled by
+    // scale * log2(e)), key weights in registers, fixed-point warp sums, and
+    // two queries per paired-fp32 instruction at 1-4 heads per group.
+    constexpr bool PAIR = HPG <= 4;
+    constexpr int RAWF = HPG * (2 * R + 1), MF = HPG * HPG, NCK = 2 * R + 1, NCH = 2 * BM * NCK;
     const int sub = warp & 3, cs = warp >> 2;
     const int g_begin = cs * GPW;
     const int s_local = 32 * sub + lane;
     const int ctid = threadIdx.x;  // compose threads are 0 .. 32*NCW-1
     const float sl2e = p.scale * kLog2e;
+    float *raw = reinterpret_cast<float *>(smem + geo.raw_off);    // [set][BM][RAWF]
+    float *mrec = reinterpret_cast<float *>(smem + geo.mrec_off);  // [set][BM][h'][h] (pair layout with PAIR)
+    uint32_t *scr = reinterpret_cast<uint32_t *>(smem + geo.scr_off) + warp * 64;  // this warp's [max | sum] x 32
     auto col_of = [&](int L, int i0) { return (L / GI) * BM + i0 + (L % GI); };
+    auto midx = [&](int set, int i, int h1, int h) {
+      return PAIR ? set * BM * MF + (i >> 1) * 2 * MF + (h1 * HPG + h) * 2 + (i & 1)
+                  : ((set * BM + i) * HPG + h1) * HPG + h;
+    };
 
-    for (int idx = ctid; idx < 2 * HPG * HPG; idx += 32 * NCW) {
-      const int set = idx / (HPG * HPG), j = idx % (HPG * HPG);
-      const TermPtrs &tm = set ? p.post : p.pre;
-      const int h = j / HPG, hp = j % HPG;
-      Wz[idx] = (hp == h || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + hp) * HPG + h];
-    }
-    for (int idx = ctid; idx < 2 * BM * geo.rec_floats; idx += 32 * NCW) {
-      const int set = idx / (BM * geo.rec_floats), rem = idx % (BM * geo.rec_floats);
-      const int i = rem / geo.rec_floats, j = rem % geo.rec_floats;
+    for (int c = ctid; c < NCH; c += 32 * NCW) {
+      const int set = c / (BM * NCK), rem = c % (BM * NCK), i = rem / NCK, k = rem % NCK;
       const TermPtrs &tm = set ? p.post : p.pre;
       const int t = q0 + i;
-      float val = 0.f;
+      const int64_t tok = (int64_t)b * T + t;
+      const E *src = nullptr;
       if (t < T) {
-        const int64_t tok = (int64_t)b * T + t;
-        if (j < HPG) {
-          val = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)g * HPG + j) * HPG + j] : 0.f) +
-                (tm.qdd ? ld_w<E>(tm.qdd, tok * H + hbase + j) : 0.f);
-        } else if (j < HPG + HPG * R) {
-          const int h = (j - HPG) / R, r = (j - HPG) % R;
-          val = tm.qw1 ? ld_w<E>(tm.qw1, (tok * H + hbase + h) * R + r) : 0.f;
-        } else if (j < HPG + 2 * HPG * R) {
-          const int r = (j - HPG - HPG * R) / HPG, h = (j - HPG - HPG * R) % HPG;
-          val = tm.qw2 ? ld_w<E>(tm.qw2, (tok * R + r) * H + hbase + h) : 0.f;
-        }
+        if (k == 0) src = tm.qdd ? elem<E>(tm.qdd, tok * H + hbase) : nullptr;
+        else if (k <= R) src = tm.qw1 ? elem<E>(tm.qw1, (tok * H + hbase) * R + (k - 1) * HPG) : nullptr;
+        else src = tm.qw2 ? elem<E>(tm.qw2, (tok * R + (k - 1 - R)) * H + hbase) : nullptr;
       }
-      rec[idx] = val;
+      const Raw16<HPG> v = src ? ld_raw16<HPG>(src) : raw16_zero<HPG>();
+      float *dst = raw + (set * BM + i) * RAWF + k * HPG;
+#pragma unroll
+      for (int h = 0; h < HPG; ++h) dst[h] = raw16_get<E, HPG>(v, h);
+    }
+    ptx::named_bar_sync(1, 32 * NCW);
+    for (int idx = ctid; idx < 2 * BM * MF; idx += 32 * NCW) {
+      const int set = idx / (BM * MF), i = (idx / MF) % BM, h1 = (idx % MF) / HPG, h = idx % HPG;
+      const TermPtrs &tm = set ? p.post : p.pre;
+      const float *rr = raw + (set * BM + i) * RAWF;
+      float m = (tm.w ? tm.w[((int64_t)g * HPG + h1) * HPG + h] : 0.f) +
+                (h1 == h ? (tm.identity ? 1.f : 0.f) + rr[h] : 0.f);
+#pragma unroll
+      for (int r = 0; r < R; ++r) m = fmaf(rr[HPG + h1 * R + r], rr[HPG + HPG * R + r * HPG + h], m);
+      mrec[midx(set, i, h1, h)] = set ? m : m * sl2e;
     }
     ptx::named_bar_sync(1, 32 * NCW);
 
-    WSrc<HPG> Wreg;
-    float kw1[HPG * R], kw2[R * HPG], kdd[HPG];
-    float m_run[GPW], l_run[GPW];
+    // per-key weights of the pre (k*) and post (p*) sets; with PAIR also as duplicated pairs
+    struct KeyW {
+      float w1[HPG * R], w2[R * HPG], dd[HPG];
+      ptx::f2_t w1d[HPG * R], w2d[R * HPG], ddd[HPG];
+    };
+    KeyW kpre, kpost;
+    auto load_key = [&](KeyW &kw, const TermPtrs &tm, float f, int64_t tok, bool okk) {
+      load_key_weights_vec<E, HPG, R>(tm, tok, H, hbase, okk, kw.w1, kw.w2, kw.dd);
 #pragma unroll
-    for (int k = 0; k < GPW; ++k) { m_run[k] = -INFINITY; l_run[k] = 0.f; }
+      for (int j = 0; j < R * HPG; ++j) kw.w2[j] *= f;
+#pragma unroll
+      for (int j = 0; j < HPG; ++j) kw.dd[j] *= f;
+      if constexpr (PAIR) {
+#pragma unroll
+        for (int j = 0; j < HPG * R; ++j) kw.w1d[j] = ptx::f2_dup(kw.w1[j]);
+#pragma unroll
+        for (int j = 0; j < R * HPG; ++j) kw.w2d[j] = ptx::f2_dup(kw.w2[j]);
+#pragma unroll
+        for (int j = 0; j < HPG; ++j) kw.ddd[j] = ptx::f2_dup(kw.dd[j]);
+      }
+    };
+    // composition of GI queries from i0 (set: pre 0 / post 1) in place on v
+    auto compose_group = [&](float (&v)[HPG][GI], int set, int i0, const KeyW &kw) {
+      if constexpr (PAIR) {
+#pragma unroll
+        for (int ii = 0; ii < GI; ii += 2) {
+          ptx::f2_t a[HPG], o[HPG];
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) a[h] = ptx::f2_pack(v[h][ii], v[h][ii + 1]);
+          compose_m2<HPG, R>(a, o, mrec + set * BM * MF + (i0 + ii) * MF, kw.w1d, kw.w2d, kw.ddd);
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) {
+            v[h][ii] = ptx::f2_lo(o[h]);
+            v[h][ii + 1] = ptx::f2_hi(o[h]);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int ii = 0; ii < GI; ++ii) {
+          float a[HPG], o[HPG];
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
+          compose_m<HPG, R>(a, o, mrec + set * BM * MF + (i0 + ii) * MF, kw.w1, kw.w2, kw.dd);
+#pragma unroll
+          for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
+        }
+      }
+    };
+    float m_run[GPW], l_run[GPW];  // running statistics of column `lane` of each group
+#pragma unroll
+    for (int k = 0; k < GPW; ++k) { m_run[k] = kMaskedLogit; l_run[k] = 0.f; }
     bool ok = true;
 
     // ---- pass A: running column statistics of the composed logits
-    Wreg.load(Wz);
     for (int kt = 0; kt < nkt; ++kt) {
       const int sidx = kt, sb = sidx % NSB;
       const int s = k_lo + kt * KT_ROWS + s_local;
@@ -295,62 +351,61 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       const int wk0 = k_lo + kt * KT_ROWS + 32 * sub;
       const bool active = 32 * sub < rows && wk0 <= min(q0 + BM - 1, slen - 1) &&
                           (p.window <= 0 || wk0 + 31 >= q0 - p.window + 1);
-      if (active) load_key_weights<E, HPG, R>(p.pre, (int64_t)b * T + s, H, hbase, key_ok, kw1, kw2, kdd);
+      const bool keys_in = wk0 + 31 < slen && 32 * sub + 31 < rows;
+      auto all_valid = [&](int t0) {
+        return keys_in && wk0 + 31 <= t0 && (p.window <= 0 || t0 + GI - 1 - wk0 < p.window) && t0 + GI - 1 < T;
+      };
+      auto valid = [&](int t) { return key_ok && s <= t && (p.window <= 0 || t - s < p.window) && t < T; };
+      if (active) load_key(kpre, p.pre, sl2e, (int64_t)b * T + s, key_ok);
       if (ok && !ptx::mbar_wait(bar_S + sb, (sidx / NSB) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_S); }
       ptx::tc_fence_after();
       const uint32_t tl = tbase + (static_cast<uint32_t>(32 * sub) << 16) + sb * NQT;
 #pragma unroll 1
       for (int k = 0; k < GPW; ++k) {
         const int i0 = (g_begin + k) * GI;
-        if (!(active && ok)) continue;
+        if (!(active && ok)) {
+          // nothing of this warp survives the mask: no change to the statistics
+          continue;
+        }
         float v[HPG][GI];
 #pragma unroll
         for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
         ptx::tmem_wait_ld();
+        compose_group(v, 0, i0, kpre);
+        if (!all_valid(q0 + i0)) {
 #pragma unroll
-        for (int ii = 0; ii < GI; ++ii) {
-          float a[HPG], o[HPG];
+          for (int ii = 0; ii < GI; ++ii) {
+            const bool vl = valid(q0 + i0 + ii);
 #pragma unroll
-          for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
-          compose<HPG, R>(a, o, Wreg, rec + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
-          const int t = q0 + i0 + ii;
-          const bool vl = key_ok && s <= t && (p.window <= 0 || t - s < p.window) && t < T;
-#pragma unroll
-          for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? o[h] : -INFINITY;
+            for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? v[h][ii] : kMaskedLogit;
+          }
         }
-        float mt = -INFINITY;
-        float x[32];
+        // warp-local max and fixed-point sum of each column (value L = h * GI + ii)
 #pragma unroll
         for (int h = 0; h < HPG; ++h)
 #pragma unroll
           for (int ii = 0; ii < GI; ++ii) {
             const float mw = ptx::warp_max(v[h][ii]);
-            if (lane == h * GI + ii) mt = mw;
-            x[h * GI + ii] = exp2f((v[h][ii] - (mw == -INFINITY ? 0.f : mw)) * sl2e);
+            const uint32_t sw = ptx::warp_sum_u32(__float_as_uint(ptx::ex2(v[h][ii] - mw) + 1.f));
+            if (lane == 0) {
+              scr[h * GI + ii] = __float_as_uint(mw);
+              scr[32 + h * GI + ii] = sw;
+            }
           }
-#pragma unroll
-        for (int off = 16, cnt = 32; off >= 1; off >>= 1, cnt >>= 1) {
-          const bool upper = (lane & off) != 0;
-#pragma unroll
-          for (int j = 0; j < cnt / 2; ++j) {
-            const float send = upper ? x[j] : x[j + cnt / 2];
-            const float keep = upper ? x[j + cnt / 2] : x[j];
-            x[j] = keep + __shfl_xor_sync(0xffffffffu, send, off);
-          }
-        }
-        // fold this tile's (max, sum) of value `lane` into the running statistics
-        if (mt != -INFINITY) {
-          const float mn = fmaxf(m_run[k], mt);
-          l_run[k] = (m_run[k] == -INFINITY ? 0.f : l_run[k] * exp2f((m_run[k] - mn) * sl2e)) +
-                     x[0] * exp2f((mt - mn) * sl2e);
-          m_run[k] = mn;
-        }
+        __syncwarp();
+        // lane L folds column L's (max, sum) of this tile into its running statistics
+        const float mt = __uint_as_float(scr[lane]);
+        const float st = static_cast<float>(scr[32 + lane] - 32u * 0x3F800000u) * 0x1p-23f;
+        __syncwarp();
+        const float mn = fmaxf(m_run[k], mt);
+        l_run[k] = l_run[k] * ptx::ex2(m_run[k] - mn) + st * ptx::ex2(mt - mn);
+        m_run[k] = mn;
       }
       ptx::tc_fence_before();
       __syncwarp();
       if (lane == 0) ptx::mbar_arrive(bar_Sfree + sb);
     }
-    // ---- combine the four lane quarters of every column
+    // ---- combine the four lane quarters of every column; statistics in [query][head]
 #pragma unroll
     for (int k = 0; k < GPW; ++k) {
       const int col = col_of(lane, (g_begin + k) * GI);
@@ -359,15 +414,14 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
     }
     ptx::named_bar_sync(1, 32 * NCW);
     for (int j = ctid; j < NQT; j += 32 * NCW) {
-      float m = -INFINITY;
+      float m = kMaskedLogit;
       for (int q = 0; q < 4; ++q) m = fmaxf(m, redm[q * NQT + j]);
       float l = 0.f;
-      for (int q = 0; q < 4; ++q) {
-        const float mq = redm[q * NQT + j];
-        if (mq != -INFINITY) l += reds[q * NQT + j] * exp2f((mq - m) * sl2e);
-      }
-      mval[j] = m == -INFINITY ? 0.f : m * sl2e;
-      linv[j] = l > 0.f ? 1.f / l : 0.f;
+      for (int q = 0; q < 4; ++q) l += reds[q * NQT + j] * ptx::ex2(redm[q * NQT + j] - m);
+      const int h = j / BM, i = j % BM;
+      const bool dead = !(m > 0.5f * kMaskedLogit && l > 0.f);  // every key masked: output 0
+      mval[i * HPG + h] = dead ? 0.f : m;
+      linv[i * HPG + h] = dead ? 0.f : __frcp_rn(l);
     }
     ptx::named_bar_sync(1, 32 * NCW);
 
@@ -380,9 +434,15 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       const int wk0 = k_lo + kt * KT_ROWS + 32 * sub;
       const bool active = 32 * sub < rows && wk0 <= min(q0 + BM - 1, slen - 1) &&
                           (p.window <= 0 || wk0 + 31 >= q0 - p.window + 1);
-      if (active) load_key_weights<E, HPG, R>(p.pre, (int64_t)b * T + s, H, hbase, key_ok, kw1, kw2, kdd);
-      float pw1[HPG * R], pw2[R * HPG], pdd[HPG];
-      if (active) load_key_weights<E, HPG, R>(p.post, (int64_t)b * T + s, H, hbase, key_ok, pw1, pw2, pdd);
+      const bool keys_in = wk0 + 31 < slen && 32 * sub + 31 < rows;
+      auto all_valid = [&](int t0) {
+        return keys_in && wk0 + 31 <= t0 && (p.window <= 0 || t0 + GI - 1 - wk0 < p.window) && t0 + GI - 1 < T;
+      };
+      auto valid = [&](int t) { return key_ok && s <= t && (p.window <= 0 || t - s < p.window) && t < T; };
+      if (active) {
+        load_key(kpre, p.pre, sl2e, (int64_t)b * T + s, key_ok);
+        load_key(kpost, p.post, 1.f, (int64_t)b * T + s, key_ok);
+      }
       if (ok && !ptx::mbar_wait(bar_S + sb, (sidx / NSB) & 1, WAIT)) { ok = false; record_err(p, ERR_TIMEOUT_S); }
       // P' buffer pb was last read by the PV of tile kt - NPB
       if (ok && kt >= NPB && !ptx::mbar_wait(bar_Pfree + pb, ((kt - NPB) / NPB) & 1, WAIT)) {
@@ -392,8 +452,6 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       ptx::tc_fence_after();
       const uint32_t tl = tbase + (static_cast<uint32_t>(32 * sub) << 16) + sb * NQT;
       unsigned char *prow = smem + geo.p_off + pb * (KT_ROWS * NQT * 2) + (s_local & 7) * 16 + (s_local >> 3) * (BM * 16);
-      WSrc<HPG> Wpost;
-      Wpost.load(Wz + HPG * HPG);
 #pragma unroll 1
       for (int k = 0; k < GPW; ++k) {
         const int i0 = (g_begin + k) * GI;
@@ -402,23 +460,18 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
 #pragma unroll
           for (int h = 0; h < HPG; ++h) ptx::tmem_ld<GI>(tl + h * BM + i0, v[h]);
           ptx::tmem_wait_ld();
+          compose_group(v, 0, i0, kpre);
+          const bool full = all_valid(q0 + i0);
 #pragma unroll
           for (int ii = 0; ii < GI; ++ii) {
-            float a[HPG], o[HPG];
+            float mv[HPG], li[HPG];
+            ld_row<HPG>(mval + (i0 + ii) * HPG, mv);
+            ld_row<HPG>(linv + (i0 + ii) * HPG, li);
+            const bool vl = full || valid(q0 + i0 + ii);
 #pragma unroll
-            for (int h = 0; h < HPG; ++h) a[h] = v[h][ii];
-            compose<HPG, R>(a, o, Wreg, rec + (i0 + ii) * geo.rec_floats, kw1, kw2, kdd);
-            const int t = q0 + i0 + ii;
-            const bool vl = key_ok && s <= t && (p.window <= 0 || t - s < p.window) && t < T;
-#pragma unroll
-            for (int h = 0; h < HPG; ++h) {
-              const int col = h * BM + i0 + ii;
-              a[h] = vl ? exp2f(fmaf(o[h], sl2e, -mval[col])) * linv[col] : 0.f;
-            }
-            compose<HPG, R>(a, o, Wpost, rec + (BM + i0 + ii) * geo.rec_floats, pw1, pw2, pdd);
-#pragma unroll
-            for (int h = 0; h < HPG; ++h) v[h][ii] = o[h];
+            for (int h = 0; h < HPG; ++h) v[h][ii] = vl ? ptx::ex2(v[h][ii] - mv[h]) * li[h] : 0.f;
           }
+          compose_group(v, 1, i0, kpost);
         } else {
 #pragma unroll
           for (int h = 0; h < HPG; ++h)
@@ -434,11 +487,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
               constexpr int W8 = GI < 8 ? GI : 8;
               uint32_t pk[W8 / 2];
 #pragma unroll
-              for (int u = 0; u < W8 / 2; ++u) {
-                const E lo = from_f<E>(v[h][c + 2 * u]), hi = from_f<E>(v[h][c + 2 * u + 1]);
-                pk[u] = static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&lo)) |
-                        (static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&hi)) << 16);
-              }
+              for (int u = 0; u < W8 / 2; ++u) pk[u] = pack2<E>(v[h][c + 2 * u], v[h][c + 2 * u + 1]);
               const int i = i0 + c;
               unsigned char *dst = tile + (i >> 3) * 128 + (i & 7) * 2;
               if constexpr (W8 == 8) {
@@ -542,7 +591,6 @@ static cudaError_t launch_e(const dc_attn_params &p, cudaStream_t st) {
     case 2: return launch_r<E, 2>(p, st);
     case 4: return launch_r<E, 4>(p, st);
     case 8: return launch_r<E, 8>(p, st);
-    case 16: return launch_r<E, 16>(p, st);
   }
   return cudaErrorInvalidValue;
 }
@@ -553,8 +601,9 @@ bool tcs_supports(const dc_attn_params &p, std::string *why) {
   auto no = [&](const char *m) { if (why) *why = m; return false; };
   const int HPG = p.H / p.G;
   if (p.D != 128) return no("D must be 128");
-  if (HPG != 1 && HPG != 2 && HPG != 4 && HPG != 8 && HPG != 16)
-    return no("heads per group must be 1, 2, 4, 8 or 16");
+  // (16 heads per group: the per-query mixing matrices do not fit beside the
+  // rings; those layers run on the kernel with the static mix on tensor cores)
+  if (HPG != 1 && HPG != 2 && HPG != 4 && HPG != 8) return no("heads per group must be 1, 2, 4 or 8");
   if (p.R > 2) return no("rank R > 2");
   if (!(p.scale > 0.f)) return no("non-positive softmax scale");
   if (p.pre.qmat || p.post.qmat) return no("per-query mixing matrices use the SIMT kernel");

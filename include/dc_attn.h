@@ -77,7 +77,7 @@ enum dc_kernel {
   DC_KERNEL_TC = 2,   /* tcgen05/TMEM/TMA kernel, single pass (windows up to
                          three key tiles, heads per group <= 8)              */
   DC_KERNEL_TCS = 3,  /* tcgen05 two-pass streaming kernel (any window incl.
-                         full causal, heads per group <= 16)                 */
+                         full causal, heads per group <= 8)                  */
   DC_KERNEL_TCM = 4   /* two-pass streaming kernel with the static head mix
                          on the tensor cores (16 or 32 heads per group)     */
 };
