@@ -615,6 +615,11 @@ __global__ void __launch_bounds__(32 * NW, 1)
   // per group the duplicated key weights and the wider rows spill, so those
   // groups compose one query at a time
   constexpr bool PAIR = HPG <= 4;
+  // build the next tile's matrices inside the statistics window (by the
+  // threads that do not combine columns) and run tiles without a barrier
+  // between them; at 8 heads per group the larger matrices make that window
+  // the longer path, so those build after it and keep the tile barrier
+  constexpr bool EARLY_M = HPG <= 4;
   static_assert(NG == 4 && NG % CS == 0, "group geometry");
 
   extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -968,9 +973,9 @@ __global__ void __launch_bounds__(32 * NW, 1)
       for (int h = 0; h < HPG; ++h) dst[h] = raw16_get<E, HPG>(v, h);
     };
     // per-query matrices of a tile (group g) from the raw values -> mrec[par]
-    auto build_m = [&](int par, int g) {
+    auto build_m = [&](int par, int g, int tid, int nthr) {
       float *dst = mrec + par * NM;
-      for (int idx = ctid; idx < NM; idx += ncompose) {
+      for (int idx = tid; idx < NM; idx += nthr) {
         const int set = idx / (BM * MF), i = (idx / MF) % BM, h1 = (idx % MF) / HPG, h = idx % HPG;
         const float *rr = raw + (set * BM + i) * RAWF;
         float m = Wt[((set * G + g) * HPG + h1) * HPG + h] + (h1 == h ? rr[h] : 0.f);
@@ -1031,11 +1036,17 @@ __global__ void __launch_bounds__(32 * NW, 1)
           chunk_store(c, src ? ld_raw16<HPG>(src) : raw16_zero<HPG>());
         }
         ptx::named_bar_sync(1, ncompose);
-        build_m(0, g);
+        build_m(0, g, ctid, ncompose);
+        if constexpr (EARLY_M) ptx::named_bar_sync(1, ncompose);  // the first tile's matrices are visible
       }
-      // this tile's matrices are visible; the previous tile's pass 2 is finished
-      // by every compose warp before the reduction buffers are rewritten
-      ptx::named_bar_sync(1, ncompose);
+      // (8 heads per group: 64-entry matrices; built after the statistics by all
+      // compose threads, and a barrier here makes them visible)
+      if constexpr (!EARLY_M) ptx::named_bar_sync(1, ncompose);
+      // No barrier between tiles: a tile's matrices are built before the
+      // previous tile's second statistics barrier, and a buffer is rewritten
+      // only after a barrier that every reader of its last contents has passed
+      // (reduction slots: after the combine; factors: after the next tile's
+      // first statistics barrier), so warps may run ahead into this tile.
       const float *mcur = mrec + buf * NM;
       bool ok = ptx::mbar_wait(bar_S + 2 * buf + kt, (it >> 1) & 1, WAIT);
       if (!ok) record_err(p, ERR_TIMEOUT_S);
@@ -1179,12 +1190,18 @@ __global__ void __launch_bounds__(32 * NW, 1)
           if (w < nslots)
             fac[w * BM * HPG + (PAIR ? (i >> 1) * 2 * HPG + h * 2 + (i & 1) : i * HPG + h)] = mw[w] * il;
       }
+      // the next tile's matrices, from the weights stored after pass 1, built
+      // by the compose threads that do not combine columns (all of them when
+      // there are no others)
+      if constexpr (EARLY_M) {
+        const int nb0 = ncompose > NQ ? NQ : 0;
+        if (ntile < ntiles && ctid >= nb0) build_m(buf ^ 1, ng, ctid - nb0, ncompose - nb0);
+      }
       ptx::named_bar_sync(1, ncompose);
-      // post-set key weights into the registers of the pre set (dead after
-      // pass 1); their latency overlaps building the next tile's matrices
+      // post-set key weights into the registers of the pre set (dead after pass 1)
       if (active) load_key(p.post, 1.f, ktok, hbase, key_ok);
-      // the next tile's matrices, from the weights stored after pass 1
-      if (ntile < ntiles) build_m(buf ^ 1, ng);
+      if constexpr (!EARLY_M)
+        if (ntile < ntiles) build_m(buf ^ 1, ng, ctid, ncompose);
       // P' of key tile 0 overwrites Q: every QK product of this tile must be complete
       if (ok && kt == 0 && nkt > 1) {
         ok = ptx::mbar_wait(bar_S + 2 * buf + nkt - 1, (it >> 1) & 1, WAIT);
