@@ -46,6 +46,10 @@ WORKLOADS = {
     "config2": dict(B=16, T=4096, H=32, D=128, window=256, G=1, R=2),
     "config3": dict(B=4, T=4096, H=32, D=128, window=None, G=4, R=2),
     "config4": dict(B=64, T=8192, H=32, D=128, window=256, G=1, R=2),
+    # the reference's decomposed form (dc_attention_torch.py:22-84): per-query
+    # N x N mixing matrices (qmat = I + N(0, 0.05)) and no other term, at the
+    # config-1 layer shape
+    "decomposed": dict(B=16, T=4096, H=32, D=128, window=128, G=1, R=0, qmat=True),
 }
 FALLBACK_HBM_GBS, FALLBACK_BF16_TFLOPS = 6650.0, 1590.0
 
@@ -60,11 +64,14 @@ def pairs_range(t0, t1, W):
     return sum(t + 1 if (W is None or t + 1 < W) else W for t in range(t0, t1))
 
 
-def flops(B, H, D, G, R, npairs):
+def flops(B, H, D, G, R, npairs, qmat=False):
     """Algorithmic FLOPs: QK^T + PV, plus pre+post composition (static mix 2*HPG,
-    query- and key-wise rank-R aggregate+apply 8R, qdd/kdd 4) per (b,h,t,s)."""
+    query- and key-wise rank-R aggregate+apply 8R, qdd/kdd 4) per (b,h,t,s);
+    with qmat (the decomposed form) the composition is the per-query mix alone
+    (2*HPG per set)."""
     hpg = H // G
-    return 4 * D * H * B * npairs + 2 * (2 * hpg + 8 * R + 4) * H * B * npairs
+    comp = 2 * hpg if qmat else 2 * hpg + 8 * R + 4
+    return 4 * D * H * B * npairs + 2 * comp * H * B * npairs
 
 
 def algo_bytes(B, T, H, D, R, esize=2):
@@ -91,6 +98,11 @@ def make_inputs(cfg, device, dtype=torch.bfloat16, seed=0):
     rn = lambda *s: torch.randn(*s, generator=g, device=device, dtype=torch.float32)
     q, k, v = (rn(B, T, H, D).to(dtype) for _ in range(3))
     sets = []
+    if cfg.get("qmat"):
+        eye = torch.eye(hpg, device=device).repeat(G, 1)
+        for _ in range(2):
+            sets.append(DCTerms(identity=False, qmat=(eye + 0.05 * rn(B, T, H, hpg)).to(dtype)))
+        return q, k, v, sets[0], sets[1]
     for _ in range(2):
         sets.append(DCTerms(
             identity=False, w=torch.eye(hpg, device=device)[None] + 0.02 * rn(G, hpg, hpg),
@@ -217,7 +229,8 @@ def config_desc(args, cfg, world):
     d = {"workload": args.workload, "B": cfg["B"], "T": cfg["T"], "H": cfg["H"], "D": cfg["D"],
          "window": cfg["window"] if cfg["window"] is not None else "full_causal", "G": cfg["G"],
          "HPG": cfg["H"] // cfg["G"], "R": cfg["R"],
-         "terms": "static W + query- and key-wise rank R + qdd + kdd (pre and post)",
+         "terms": ("per-query N x N mixing matrices only (decomposed form, pre and post)" if cfg.get("qmat") else
+                   "static W + query- and key-wise rank R + qdd + kdd (pre and post)"),
          "l2": "inputs larger than L2 (no flush)", "parallelism": f"batch-sharded x{world}, no collectives"}
     return d
 
@@ -275,7 +288,7 @@ def run_ours(args, cfg, world, rank, local):
     host_sets = []
     for tm in (pre, post):
         kw = {}
-        for f in ("qw1", "qw2", "kw1", "kw2", "qdd", "kdd"):
+        for f in ("qw1", "qw2", "kw1", "kw2", "qdd", "kdd", "qmat"):
             t = getattr(tm, f)
             if t is not None:
                 kw[f] = t.cpu().pin_memory()
@@ -299,12 +312,14 @@ def run_ours(args, cfg, world, rank, local):
     barrier()
     e2e_ms = max_over_ranks(ev0.elapsed_time(ev1) / e2e_steps, device)
 
-    fl_rank = flops(B, H, D, G, R, pairs(T, W))
+    fl_rank = flops(B, H, D, G, R, pairs(T, W), qmat=bool(rcfg.get("qmat")))
     total_fl = fl_rank * world
     value = total_fl / (ms_step * 1e-3) / 1e12
     e2e_val = total_fl / (e2e_ms * 1e-3) / 1e12
     hbm, tc_peak, peak_src = peaks()
     by = algo_bytes(B, T, H, D, R)
+    if rcfg.get("qmat"):  # two [B,T,H,HPG] qmat tensors instead of the rank/gate weights
+        by = 4 * B * T * H * D * 2 + 2 * B * T * H * (H // G) * 2
     achieved = by / (ms_step * 1e-3) / 1e9
     tflops_rank = fl_rank / (ms_step * 1e-3) / 1e12
     strong = best = None
@@ -316,7 +331,7 @@ def run_ours(args, cfg, world, rank, local):
     if rank != 0:
         return
     cpu = None
-    if world == 1 and not args.no_cpu_baseline:
+    if world == 1 and not args.no_cpu_baseline and not cfg.get("qmat"):
         v_cpu, cores, sample = cpu_port_sample(cfg, target_s=12.0)
         cpu = {"value": v_cpu, "unit": "TFLOP/s", "cores": cores, "kind": "port", "sample": sample}
     wl_key = f"{args.workload}_G{G}_W{W}"

@@ -57,6 +57,7 @@ struct TermPtrs {
   int identity;
   const float *w;
   const void *qw1, *qw2, *kw1, *kw2, *qdd, *kdd;
+  const void *qmat;  // [B, T, H, HPG] per-query mix inside the group (decomposed form)
 };
 
 struct TcParams {
@@ -303,6 +304,17 @@ __device__ __forceinline__ float ld_w(const void *base, int64_t idx) {
   return to_f<E>(reinterpret_cast<const E *>(base)[idx]);
 }
 
+// Entry (h1 -> h) of query t's per-query mix: the weight of a[h1] in the
+// composed value of head h, qmat[b, t, hbase + h, h1] (dc_attention_torch.py:59-61
+// mixes logits as mixed[i] = sum_j pre_w[i, j] L[j]); 0 without qmat or for
+// t outside the sequence.
+template <typename E>
+__device__ __forceinline__ float qmat_at(const TermPtrs &tm, int b, int t, int T, int H, int hpg, int hbase, int h1,
+                                         int h) {
+  if (!tm.qmat || t >= T) return 0.f;
+  return ld_w<E>(tm.qmat, (((int64_t)b * T + t) * H + hbase + h) * hpg + h1);
+}
+
 // N consecutive 16-bit elements (N * 2 bytes, aligned to that size), raw.
 template <int N>
 struct Raw16 {
@@ -456,6 +468,7 @@ static TermPtrs to_ptrs(const dc_terms &t) {
   r.identity = t.identity;
   r.w = t.w;
   r.qw1 = t.qw1; r.qw2 = t.qw2; r.kw1 = t.kw1; r.kw2 = t.kw2; r.qdd = t.qdd; r.kdd = t.kdd;
+  r.qmat = t.qmat;
   return r;
 }
 

@@ -258,7 +258,8 @@ __global__ void __launch_bounds__(MAXT, 1)
       const int set = idx / (BM * MF), i = (idx / MF) % BM, h1 = (idx % MF) / HPG, h = idx % HPG;
       const TermPtrs &tm = set ? p.post : p.pre;
       const float *rr = raw + (set * BM + i) * RAWF;
-      float m = (tm.w ? tm.w[((int64_t)g * HPG + h1) * HPG + h] : 0.f) + (h1 == h ? (tm.identity ? 1.f : 0.f) + rr[h] : 0.f);
+      float m = (tm.w ? tm.w[((int64_t)g * HPG + h1) * HPG + h] : 0.f) + (h1 == h ? (tm.identity ? 1.f : 0.f) + rr[h] : 0.f) +
+                qmat_at<E>(tm, b, q0 + i, T, H, HPG, hbase, h1, h);
 #pragma unroll
       for (int r = 0; r < R; ++r) m = fmaf(rr[HPG + h1 * R + r], rr[HPG + HPG * R + r * HPG + h], m);
       mrec[PAIR ? set * BM * MF + (i >> 1) * 2 * MF + (h1 * HPG + h) * 2 + (i & 1) : idx] = set ? m : m * sl2e;
@@ -973,12 +974,13 @@ __global__ void __launch_bounds__(32 * NW, 1)
       for (int h = 0; h < HPG; ++h) dst[h] = raw16_get<E, HPG>(v, h);
     };
     // per-query matrices of a tile (group g) from the raw values -> mrec[par]
-    auto build_m = [&](int par, int g, int tid, int nthr) {
+    auto build_m = [&](int par, int q0, int b, int g, int tid, int nthr) {
       float *dst = mrec + par * NM;
       for (int idx = tid; idx < NM; idx += nthr) {
         const int set = idx / (BM * MF), i = (idx / MF) % BM, h1 = (idx % MF) / HPG, h = idx % HPG;
         const float *rr = raw + (set * BM + i) * RAWF;
-        float m = Wt[((set * G + g) * HPG + h1) * HPG + h] + (h1 == h ? rr[h] : 0.f);
+        float m = Wt[((set * G + g) * HPG + h1) * HPG + h] + (h1 == h ? rr[h] : 0.f) +
+                  qmat_at<E>(set ? p.post : p.pre, b, q0 + i, T, H, HPG, g * HPG, h1, h);
 #pragma unroll
         for (int r = 0; r < R; ++r) m = fmaf(rr[HPG + h1 * R + r], rr[HPG + HPG * R + r * HPG + h], m);
         // with PAIR the pair layout [set][query / 2][h'][h][query % 2] (compose_m2)
@@ -1036,7 +1038,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
           chunk_store(c, src ? ld_raw16<HPG>(src) : raw16_zero<HPG>());
         }
         ptx::named_bar_sync(1, ncompose);
-        build_m(0, g, ctid, ncompose);
+        build_m(0, q0, b, g, ctid, ncompose);
         if constexpr (EARLY_M) ptx::named_bar_sync(1, ncompose);  // the first tile's matrices are visible
       }
       // (8 heads per group: 64-entry matrices; built after the statistics by all
@@ -1195,13 +1197,13 @@ __global__ void __launch_bounds__(32 * NW, 1)
       // there are no others)
       if constexpr (EARLY_M) {
         const int nb0 = ncompose > NQ ? NQ : 0;
-        if (ntile < ntiles && ctid >= nb0) build_m(buf ^ 1, ng, ctid - nb0, ncompose - nb0);
+        if (ntile < ntiles && ctid >= nb0) build_m(buf ^ 1, nq0, nb, ng, ctid - nb0, ncompose - nb0);
       }
       ptx::named_bar_sync(1, ncompose);
       // post-set key weights into the registers of the pre set (dead after pass 1)
       if (active) load_key(p.post, 1.f, ktok, hbase, key_ok);
       if constexpr (!EARLY_M)
-        if (ntile < ntiles) build_m(buf ^ 1, ng, ctid, ncompose);
+        if (ntile < ntiles) build_m(buf ^ 1, nq0, nb, ng, ctid, ncompose);
       // P' of key tile 0 overwrites Q: every QK product of this tile must be complete
       if (ok && kt == 0 && nkt > 1) {
         ok = ptx::mbar_wait(bar_S + 2 * buf + nkt - 1, (it >> 1) & 1, WAIT);
@@ -1411,7 +1413,6 @@ bool tc_supports(const dc_attn_params &p, std::string *why) {
   if (tc::num_key_tiles(HPG, p.window) > 3) return no("window too large (BM + window - 1 > 384)");
   if (p.R > 2) return no("rank R > 2");
   if (!(p.scale > 0.f)) return no("non-positive softmax scale");
-  if (p.pre.qmat || p.post.qmat) return no("per-query mixing matrices use the SIMT kernel");
   auto al = [](const void *x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
   if (!al(p.q) || !al(p.k) || !al(p.v) || !al(p.out)) return no("q, k, v, out must be 16-byte aligned");
   if (p.out_sb % 8 || p.out_st % 8 || p.out_sh % 8) return no("output strides must be multiples of 8 elements");

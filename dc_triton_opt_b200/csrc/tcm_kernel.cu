@@ -45,22 +45,28 @@ constexpr int NCW = 8;             // compose warps (2 per lane quarter)
 // one producer lane and one MMA warp consuming it in order (an mbarrier parity
 // wait is only unambiguous for a consumer at most one phase behind, so a ring
 // never has two consumers).  Pass A streams K alone, so its ring spans the
-// whole pool; pass B has NSK K slots, NSV V slots and P'.
-constexpr int NSK = 5, NSV = 3;
-constexpr int NLK = 4, NLV = 3;  // issuing lanes of the K and V producers (<= slots)
-static_assert(NLK <= NSK && NLV <= NSV, "a producer round may not wrap its ring");
+// whole pool; pass B has NSK K slots, NSV V slots and P'.  With per-query
+// mixing matrices (the decomposed form, QM) every query has its own mix B
+// operands, and the pass-B K ring gives up two slots for them.
+constexpr int NSK_MAX = 5, NSV = 3;
+constexpr int NLV = 3;  // issuing lanes of the V producer (<= slots)
+__host__ __device__ constexpr int nsk_of(bool qm) { return qm ? 3 : 5; }
+__host__ __device__ constexpr int nlk_of(bool qm) { return qm ? 3 : 4; }  // K producer lanes (<= slots)
+static_assert(nlk_of(false) <= nsk_of(false) && nlk_of(true) <= nsk_of(true) && NLV <= NSV,
+              "a producer round may not wrap its ring");
 // Heads whose MMAs are interleaved: the K steps of one head accumulate into one
 // TMEM tile and serialise, so independent heads are issued K step by K step.
 constexpr int HJ = 1;
-static_assert(NSK >= HJ && NSV >= HJ, "an interleaved group needs its jobs resident");
+static_assert(nsk_of(true) >= HJ && NSV >= HJ, "an interleaved group needs its jobs resident");
 constexpr int NKA_MAX = 10;
 constexpr uint32_t S_COL = 0, D_COL = 128, O_COL = 256;
 // Pass A double-buffers S in the O columns (idle until pass B): S tile n of
 // pass A uses buffer n & 1; pass B uses buffer 0 only.
 __host__ __device__ constexpr uint32_t s_col(int buf) { return buf ? O_COL : S_COL; }
 
-template <int HPG>
+template <int HPG, bool QM = false>
 struct Shape {
+  static constexpr int NSK = nsk_of(QM), NLK = nlk_of(QM);
   static constexpr int BM = 256 / HPG;        // queries per CTA
   static constexpr int HH = HPG / 2;          // heads per lane half
   static constexpr int NQG = 64 / HPG;        // queries per compose sub-group (32 values per thread)
@@ -82,18 +88,18 @@ struct GeoM {
   int p_off, a_off, bm_off, rec_off, stat_off, bar_off, tmem_off, total, recf;
 };
 
-template <int HPG, int R>
+template <int HPG, int R, bool QM>
 __host__ __device__ inline GeoM make_geo_m() {
-  using SH = Shape<HPG>;
+  using SH = Shape<HPG, QM>;
   GeoM g{};
   g.p_off = SH::POFF;                           // P': HPG x 64 keys x BM (32 KB); pass-A stats exchange
   g.a_off = SH::POOL;                           // mix operands, BM x 64 keys x HPG fp16 (32 KB)
-  g.bm_off = g.a_off + SH::BM * SH::ATILE;      // mix B operands: 2 sets x HPG x HPG fp16
-  int o = g.bm_off + 2 * HPG * HPG * 2;
+  g.bm_off = g.a_off + SH::BM * SH::ATILE;      // mix B operands: 2 sets x [BM queries with QM] x HPG x HPG fp16
+  int o = g.bm_off + 2 * (QM ? SH::BM : 1) * HPG * HPG * 2;
   g.recf = round_up(HPG * (2 * R + 1), 4);
   g.rec_off = round_up(o, 16); o = g.rec_off + 2 * SH::BM * g.recf * 4;
   g.stat_off = o; o += 2 * SH::NCOL * 4;
-  g.bar_off = round_up(o, 8); o = g.bar_off + (2 * (NKA_MAX + NSK + NSV) + 16) * 8;
+  g.bar_off = round_up(o, 8); o = g.bar_off + (2 * (NKA_MAX + NSK_MAX + NSV) + 16) * 8;
   g.tmem_off = o; o += 16;
   g.total = o;
   return g;
@@ -145,12 +151,13 @@ __device__ __forceinline__ uint32_t pack_e2(float lo, float hi) {
          (static_cast<uint32_t>(*reinterpret_cast<const uint16_t *>(&b)) << 16);
 }
 
-template <typename E, int HPG, int R>
+template <typename E, int HPG, int R, bool QM>
 __global__ void __launch_bounds__(32 * (NCW + 4), 1)
     dc_tcm_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                   const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_o,
                   const TcParams p) {
-  using SH = Shape<HPG>;
+  using SH = Shape<HPG, QM>;
+  constexpr int NSK = SH::NSK, NLK = SH::NLK;
   constexpr int BM = SH::BM, HH = SH::HH, NQG = SH::NQG, NSG = SH::NSG, KB = SH::KB;
   constexpr int ATILE = SH::ATILE, PHEAD = SH::PHEAD, NCOL = SH::NCOL;
   static_assert(HH * NQG == 32, "a compose sub-group is 32 values per thread");
@@ -158,7 +165,7 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
   extern __shared__ __align__(1024) unsigned char smem_raw[];
   unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                                           ~static_cast<uintptr_t>(1023));
-  const GeoM geo = make_geo_m<HPG, R>();
+  const GeoM geo = make_geo_m<HPG, R, QM>();
   const int recf = geo.recf;
   float *rec = reinterpret_cast<float *>(smem + geo.rec_off);
   float *redm = reinterpret_cast<float *>(smem + geo.p_off), *reds = redm + 4 * NCOL;
@@ -351,7 +358,7 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
           if (!ok) return;
           ptx::tc_fence_after();
           const uint64_t aq = ptx::desc_add(da0, sg * NQG * ATILE);
-          const uint64_t bq = ptx::desc_add(db0, set * (HPG * HPG * 2));
+          const uint64_t bq = ptx::desc_add(db0, (QM ? set * BM + sg * NQG : set) * (HPG * HPG * 2));
           const uint32_t dq = tbase + D_COL + sg * NQG * HH;
 #pragma unroll
           for (int ks = 0; ks < HPG / 16; ++ks)
@@ -362,7 +369,8 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
                 if (ptx::elect_one())
                   ptx::mma_f16_ss(dq + (static_cast<uint32_t>(16 * v) << 16) + ii * HH,
                                   ptx::desc_add(aq, ii * ATILE + ks * 256),
-                                  ptx::desc_add(bq, v * (HH * HPG * 2) + ks * 256), idesc_mix, ks > 0);
+                                  ptx::desc_add(bq, (QM ? ii * HPG * HPG * 2 : 0) + v * (HH * HPG * 2) + ks * 256),
+                                  idesc_mix, ks > 0);
           if (ptx::elect_one()) ptx::mma_commit(bar_D + sg);
           __syncwarp();
         }
@@ -465,14 +473,19 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
     unsigned char *ptile = smem + geo.p_off;
 
     // ---- static mix operands (fp16, K-major, no swizzle) and per-query records
-    for (int idx = ctid; idx < 2 * HPG * HPG; idx += 32 * NCW) {
-      const int set = idx / (HPG * HPG), rem = idx % (HPG * HPG);
+    // (with QM one operand per (set, query): the static mix plus that query's
+    // off-diagonal qmat entries; their diagonal joins the fp32 gates below)
+    constexpr int NB = QM ? BM : 1;
+    for (int idx = ctid; idx < 2 * NB * HPG * HPG; idx += 32 * NCW) {
+      const int set = idx / (NB * HPG * HPG), i = (idx / (HPG * HPG)) % NB, rem = idx % (HPG * HPG);
       const int hout = rem / HPG, kin = rem % HPG;  // B[n][k] of output half hout / HH
       const TermPtrs &tm = set ? p.post : p.pre;
-      const float wv = (kin == hout || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + kin) * HPG + hout];
+      float wv = (kin == hout || !tm.w) ? 0.f : tm.w[((int64_t)g * HPG + kin) * HPG + hout];
+      if (QM && kin != hout) wv += qmat_at<E>(tm, b, q0 + i, T, H, HPG, hbase, kin, hout);
       const int v = hout / HH, n = hout % HH;
-      __half *dst = reinterpret_cast<__half *>(smem + geo.bm_off + set * (HPG * HPG * 2) + v * (HH * HPG * 2) +
-                                               ((n / 8) * KB + kin / 8) * 128 + (n % 8) * 16 + (kin % 8) * 2);
+      __half *dst = reinterpret_cast<__half *>(smem + geo.bm_off + (set * NB + i) * (HPG * HPG * 2) +
+                                               v * (HH * HPG * 2) + ((n / 8) * KB + kin / 8) * 128 + (n % 8) * 16 +
+                                               (kin % 8) * 2);
       *dst = __float2half_rn(wv);
     }
     for (int idx = ctid; idx < 2 * BM * recf; idx += 32 * NCW) {
@@ -485,7 +498,8 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
         const int64_t tok = (int64_t)b * T + t;
         if (j < HPG) {
           val = (tm.identity ? 1.f : 0.f) + (tm.w ? tm.w[((int64_t)g * HPG + j) * HPG + j] : 0.f) +
-                (tm.qdd ? ld_w<E>(tm.qdd, tok * H + hbase + j) : 0.f);
+                (tm.qdd ? ld_w<E>(tm.qdd, tok * H + hbase + j) : 0.f) +
+                (QM ? qmat_at<E>(tm, b, t, T, H, HPG, hbase, j, j) : 0.f);
         } else if (j < HPG + HPG * R) {
           const int h = (j - HPG) / R, r = (j - HPG) % R;
           val = tm.qw1 ? ld_w<E>(tm.qw1, (tok * H + hbase + h) * R + r) : 0.f;
@@ -786,10 +800,10 @@ __global__ void __launch_bounds__(32 * (NCW + 4), 1)
   }
 }
 
-template <typename E, int HPG, int R>
+template <typename E, int HPG, int R, bool QM>
 static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
-  using SH = Shape<HPG>;
-  const GeoM geo = make_geo_m<HPG, R>();
+  using SH = Shape<HPG, QM>;
+  const GeoM geo = make_geo_m<HPG, R, QM>();
   const size_t smem = geo.total + 1024;
   const int64_t sb = (int64_t)p.T * p.H * D, st_ = (int64_t)p.H * D, sh = D;
   CUtensorMap mq, mk, mv, mo;
@@ -809,7 +823,7 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   tp.skip_loads = (p.test_flags & DC_TEST_SKIP_LOADS) != 0;
   tp.pre = to_ptrs(p.pre);
   tp.post = to_ptrs(p.post);
-  auto kern = dc_tcm_kernel<E, HPG, R>;
+  auto kern = dc_tcm_kernel<E, HPG, R, QM>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((p.T + SH::BM - 1) / SH::BM, p.B * p.G);
@@ -819,7 +833,9 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
 
 template <typename E, int HPG>
 static cudaError_t launch_h(const dc_attn_params &p, cudaStream_t st) {
-  return p.R <= 1 ? launch_t<E, HPG, 1>(p, st) : launch_t<E, HPG, 2>(p, st);
+  if (p.pre.qmat || p.post.qmat)
+    return p.R <= 1 ? launch_t<E, HPG, 1, true>(p, st) : launch_t<E, HPG, 2, true>(p, st);
+  return p.R <= 1 ? launch_t<E, HPG, 1, false>(p, st) : launch_t<E, HPG, 2, false>(p, st);
 }
 
 template <typename E>
@@ -835,7 +851,6 @@ bool tcm_supports(const dc_attn_params &p, std::string *why) {
   if (p.G <= 0 || (p.H / p.G != 16 && p.H / p.G != 32)) return no("heads per group must be 16 or 32");
   if (p.R > 2) return no("rank R > 2");
   if (!(p.scale > 0.f)) return no("non-positive softmax scale");
-  if (p.pre.qmat || p.post.qmat) return no("per-query mixing matrices use the SIMT kernel");
   auto al = [](const void *x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
   if (!al(p.q) || !al(p.k) || !al(p.v) || !al(p.out)) return no("q, k, v, out must be 16-byte aligned");
   if (p.out_sb % 8 || p.out_st % 8 || p.out_sh % 8) return no("output strides must be multiples of 8 elements");

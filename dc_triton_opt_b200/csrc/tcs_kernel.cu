@@ -282,7 +282,7 @@ __global__ void __launch_bounds__(32 * (NCW + 2), 1)
       const TermPtrs &tm = set ? p.post : p.pre;
       const float *rr = raw + (set * BM + i) * RAWF;
       float m = (tm.w ? tm.w[((int64_t)g * HPG + h1) * HPG + h] : 0.f) +
-                (h1 == h ? (tm.identity ? 1.f : 0.f) + rr[h] : 0.f);
+                (h1 == h ? (tm.identity ? 1.f : 0.f) + rr[h] : 0.f) + qmat_at<E>(tm, b, q0 + i, T, H, HPG, hbase, h1, h);
 #pragma unroll
       for (int r = 0; r < R; ++r) m = fmaf(rr[HPG + h1 * R + r], rr[HPG + HPG * R + r * HPG + h], m);
       mrec[midx(set, i, h1, h)] = set ? m : m * sl2e;
@@ -606,7 +606,6 @@ bool tcs_supports(const dc_attn_params &p, std::string *why) {
   if (HPG != 1 && HPG != 2 && HPG != 4 && HPG != 8) return no("heads per group must be 1, 2, 4 or 8");
   if (p.R > 2) return no("rank R > 2");
   if (!(p.scale > 0.f)) return no("non-positive softmax scale");
-  if (p.pre.qmat || p.post.qmat) return no("per-query mixing matrices use the SIMT kernel");
   auto al = [](const void *x) { return (reinterpret_cast<uintptr_t>(x) & 15u) == 0; };
   if (!al(p.q) || !al(p.k) || !al(p.v) || !al(p.out)) return no("q, k, v, out must be 16-byte aligned");
   if (p.out_sb % 8 || p.out_st % 8 || p.out_sh % 8) return no("output strides must be multiples of 8 elements");

@@ -332,3 +332,68 @@ def test_persistent_kernel_many_tiles_per_cta(G):
     ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, 128, G, None)
     got = run_general(q, k, v, pre, post, 128 ** -0.5, 128, G, None, "bf16", "tc")
     assert_close(got, ref, f"persistent G{G} B{B} T{T}")
+
+
+# ---------------------------------------------------------------- per-query mixing matrices (qmat)
+
+def _with_qmat(pre, post, B, T, H, G, seed, decomposed=False):
+    """Add a per-query mix qmat [B,T,H,HPG] to both sets.  decomposed=True gives
+    the reference's decomposed form instead: no identity, no other term, and
+    qmat = I + N(0, 0.05) (dc_attention_torch.py:22-84 folds the residual into
+    its matrices)."""
+    rng = np.random.default_rng(seed)
+    hpg = H // G
+    out = []
+    for t in (pre, post):
+        qm = (0.05 * rng.standard_normal((B, T, H, hpg))).astype(np.float32)
+        if decomposed:
+            qm += np.tile(np.eye(hpg, dtype=np.float32), (G, 1))[None, None]
+            t = O.Terms(identity=False)
+        t.qmat = qm
+        out.append(t)
+    return out
+
+
+@pytest.mark.parametrize("kernel,G,window,T,R", [
+    ("tc", 8, 128, 200, 1),    # persistent kernel, HPG 4
+    ("tc", 32, 96, 150, 1),    # persistent kernel, HPG 1
+    ("tc", 16, 128, 300, 2),   # persistent kernel, HPG 2
+    ("tc", 4, 256, 300, 2),    # one-tile-per-CTA kernel, three key tiles, HPG 8
+    ("tcs", 8, None, 260, 1),  # streaming kernel, full causal
+    ("tcm", 1, 128, 200, 1),   # tensor-core mix, 32 heads per group
+    ("tcm", 2, None, 150, 2),  # tensor-core mix, 16 heads per group, full causal
+])
+@pytest.mark.parametrize("decomposed", [False, True])
+def test_qmat_tensor_core_kernels(kernel, G, window, T, R, decomposed):
+    """Per-query mixing matrices on every tensor-core kernel: folded into the
+    per-query matrices (tc, tcs) or, at 16/32 heads per group, a per-query mix
+    operand of the tcgen05 mix MMA (off-diagonal entries in fp16, diagonal in
+    fp32)."""
+    dt = torch.bfloat16
+    q, k, v, pre, post = O.make_inputs(1, T, 32, 128, G, R, seed=G * 13 + T)
+    pre, post = _with_qmat(pre, post, 1, T, 32, G, seed=T + G, decomposed=decomposed)
+    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    ref = O.dc_attn_oracle(q, k, v, pre, post, 128 ** -0.5, window, G, None)
+    got = run_general(q, k, v, pre, post, 128 ** -0.5, window, G, None, "bf16", kernel)
+    assert_close(got, ref, f"qmat {kernel} G{G} W{window} T{T} decomposed={decomposed}")
+
+
+def test_decomposed_form_runs_on_tensor_cores():
+    """The reference's decomposed entry point (N x N per-query matrices, G = 1)
+    at the config-0 layer shape goes to the tensor-core mix kernel, not the
+    CUDA-core one, and matches the oracle."""
+    dt = torch.bfloat16
+    B, T, N, W = 1, 512, 32, 128
+    q, k, v, pre, post = O.make_inputs(B, T, N, 128, 1, 1, seed=5)
+    pre, post = _with_qmat(pre, post, B, T, N, 1, seed=6, decomposed=True)
+    q, k, v = rnd(q, dt), rnd(k, dt), rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    ref = O.decomposed(q, k, v, pre.qmat, post.qmat, 128 ** -0.5, W, np.full(B, T))
+    qd, kd, vd = T_(q, dt), T_(k, dt), T_(v, dt)
+    pw, qw = T_(pre.qmat, dt), T_(post.qmat, dt)
+    assert dc.select_kernel(qd, kd, vd, dc.DCTerms(qmat=pw), dc.DCTerms(qmat=qw), W, 1) == "tcm"
+    got = dc.dc_attention_decomposed_window_chunked(qd, kd, vd, pw, qw, 128 ** -0.5, W,
+                                                    torch.full((B,), T, device=DEV, dtype=torch.int32), 64)
+    torch.cuda.synchronize()
+    assert_close(got.float().cpu().numpy(), ref, "decomposed on tcm")
