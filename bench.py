@@ -322,12 +322,13 @@ def run_ours(args, cfg, world, rank, local):
         by = 4 * B * T * H * D * 2 + 2 * B * T * H * (H // G) * 2
     achieved = by / (ms_step * 1e-3) / 1e9
     tflops_rank = fl_rank / (ms_step * 1e-3) / 1e12
-    strong = best = None
+    strong = best = others = None
     if not args.no_extra:
         del qh, kh, vh, host_sets, out_host
         strong = strong_scaling_config4(world, rank, local)
         if rank == 0:
             best = repo_best(local)
+            others = other_layers(local)
     if rank != 0:
         return
     cpu = None
@@ -356,6 +357,7 @@ def run_ours(args, cfg, world, rank, local):
     if not args.no_extra:
         line["strong_scaling"] = strong
         line["repo_best"] = best
+        line["other_layers"] = others
     print(json.dumps(line), flush=True)
 
 
@@ -373,6 +375,38 @@ def time_calls(call, steps, warmup, stream, world):
     ev1.record(stream)
     torch.cuda.synchronize()
     return max_over_ranks(ev0.elapsed_time(ev1) / steps, stream.device)
+
+
+# The other BASELINE layers, timed in the same run (device time only): the
+# W256 half of the headline metric at the reference's best grouping (G8), its
+# G sweep ends, the full-causal layer and the decomposed form.
+OTHER_LAYERS = [("config2", dict(G=8)), ("config2", dict(G=32)), ("config2", dict(G=1)),
+                ("config3", {}), ("decomposed", {})]
+
+
+def other_layers(local, steps=5, warmup=3):
+    import dc_triton_opt_b200 as dc
+    device = torch.device("cuda", local)
+    res = {}
+    hbm, tc_peak, _ = peaks()
+    for name, over in OTHER_LAYERS:
+        cfg = dict(WORKLOADS[name], **over)
+        q, k, v, pre, post = make_inputs(cfg, device, seed=99)
+        B, T, H, D, G, R, W = (cfg[x] for x in ("B", "T", "H", "D", "G", "R", "window"))
+        out = torch.empty_like(q)
+        call = lambda: dc.dc_attn_fwd(q, k, v, pre, post, D ** -0.5, W, G, out=out)
+        ms = time_calls(call, steps, warmup, torch.cuda.current_stream(device), 1)
+        fl = flops(B, H, D, G, R, pairs(T, W), qmat=bool(cfg.get("qmat")))
+        by = (4 * B * T * H * D * 2 + 2 * B * T * H * (H // G) * 2) if cfg.get("qmat") else algo_bytes(B, T, H, D, R)
+        key = f"{name}_G{G}_W{W if W is not None else 'causal'}"
+        res[key] = {"B": B, "T": T, "window": W if W is not None else "full_causal", "G": G, "R": R,
+                    "kernel": dc.select_kernel(q, k, v, pre, post, W, G), "ms_per_call": ms,
+                    "tflops": fl / (ms * 1e-3) / 1e12, "tensor_frac": fl / (ms * 1e-3) / 1e12 / tc_peak,
+                    "hbm_gbs": by / (ms * 1e-3) / 1e9, "hbm_frac": by / (ms * 1e-3) / 1e9 / hbm}
+        del q, k, v, pre, post, out
+        torch.cuda.empty_cache()
+    res["timing"] = f"CUDA events, {warmup} warm-up + {steps} calls, inputs larger than L2"
+    return res
 
 
 def strong_scaling_config4(world, rank, local, steps=5, warmup=3):
@@ -488,7 +522,7 @@ def main():
     ap.add_argument("--kernel", default="auto", choices=["auto", "simt", "tc", "tcs", "tcm"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
-                    help="skip the config-4 strong-scaling and repo-best blocks")
+                    help="skip the config-4 strong-scaling, repo-best and other-layer blocks")
     args = ap.parse_args()
     cfg = dict(WORKLOADS[args.workload])
     for k in ("G", "window", "B", "T"):

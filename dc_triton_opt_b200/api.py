@@ -389,16 +389,28 @@ def _residual_call(q, k, v, dc_weights, scaling, window, seq_lens, G, out):
                        scaling, window, G, seq_lens, out)
 
 
+def _fp32_to_bf16(*ts):
+    """The reference's torch functions accept any float dtype.  fp32 inputs are
+    rounded to bf16 here (the kernels take bf16/fp16 operands and accumulate in
+    fp32); the caller then gets its result back in fp32."""
+    return [None if t is None else (t.to(torch.bfloat16) if t.dtype == torch.float32 else t) for t in ts]
+
+
 def dc_attention_window_chunked_residual_grouped(
         q, k, v, dc_weights: Sequence[torch.Tensor], scaling: float, window: Optional[int] = None,
         seq_lens: Optional[torch.Tensor] = None, chunk_size: Optional[int] = None, G: int = 1):
     """Drop-in for ``dc_attention_torch.dc_attention_window_chunked_residual_grouped``
     (``dc_attention_torch.py:159-258``): q,k,v [B,T,N,D], six [B,T,N] weights,
     window default 256, returns a contiguous [B,N,T,D] tensor of q's dtype.
-    ``chunk_size`` is accepted and ignored (the reference's mask is exact)."""
+    ``chunk_size`` is accepted and ignored (the reference's mask is exact).
+    fp32 inputs are computed from their bf16 rounding, output in fp32."""
     B, T, N, D = q.shape
     if window is None:
         window = 256
+    if q.dtype == torch.float32:
+        q, k, v, *ws = _fp32_to_bf16(q, k, v, *dc_weights)
+        return dc_attention_window_chunked_residual_grouped(q, k, v, ws, scaling, window, seq_lens,
+                                                            chunk_size, G).float()
     out = torch.empty((B, N, T, D), device=q.device, dtype=q.dtype)
     _residual_call(q, k, v, dc_weights, scaling, window, seq_lens, G, out.permute(0, 2, 1, 3))
     return out
@@ -417,7 +429,12 @@ def dc_attention_decomposed_window_chunked(q, k, v, pre_w, post_w, scaling, wind
     """Drop-in for ``dc_attention_torch.dc_attention_decomposed_window_chunked``
     (``dc_attention_torch.py:22-84``): per-query N x N matrices
     (``mixed[i] = sum_j pre_w[b,t,i,j] L[j]``), no residual, output [B,T,N,D].
-    ``window`` is clamped to [1, T] as in the reference (``:38``)."""
+    ``window`` is clamped to [1, T] as in the reference (``:38``).  fp32 inputs
+    are computed from their bf16 rounding, output in fp32."""
     B, T, N, D = q.shape
     window = max(1, min(int(window), T))
+    if q.dtype == torch.float32:
+        q, k, v, pre_w, post_w = _fp32_to_bf16(q, k, v, pre_w, post_w)
+        return dc_attention_decomposed_window_chunked(q, k, v, pre_w, post_w, scaling, window, seq_lens,
+                                                      chunk_size).float()
     return dc_attn_fwd(q, k, v, DCTerms(qmat=pre_w), DCTerms(qmat=post_w), scaling, window, 1, seq_lens)

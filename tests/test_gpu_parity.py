@@ -397,3 +397,29 @@ def test_decomposed_form_runs_on_tensor_cores():
                                                     torch.full((B,), T, device=DEV, dtype=torch.int32), 64)
     torch.cuda.synchronize()
     assert_close(got.float().cpu().numpy(), ref, "decomposed on tcm")
+
+
+def test_fp32_inputs_through_the_drop_ins():
+    """The reference's torch functions are dtype-generic; fp32 callers of the
+    drop-ins get an fp32 result computed from the bf16-rounded inputs."""
+    case = next(c for c in load_cases() if c.kind == "grouped")
+    f32 = lambda x: torch.from_numpy(np.ascontiguousarray(x)).to(DEV).float()
+    q, k, v = f32(case.q), f32(case.k), f32(case.v)
+    ws = [f32(w) for w in case.ws]
+    got = dc.dc_attention_window_chunked_residual_grouped(q, k, v, ws, case.scale, case.window, None,
+                                                          case.chunk, G=case.G)
+    assert got.dtype == torch.float32
+    bq, bk, bv = (x.bfloat16() for x in (q, k, v))
+    want = dc.dc_attention_window_chunked_residual_grouped(bq, bk, bv, [w.bfloat16() for w in ws], case.scale,
+                                                           case.window, None, case.chunk, G=case.G)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want.float())
+    if case.seq_lens is None:
+        assert_close(got.cpu().numpy(), case.out, "fp32 drop-in")
+    case = next(c for c in load_cases() if c.kind == "decomposed")
+    sl = torch.tensor(case.seq_lens if case.seq_lens is not None else [case.T] * case.q.shape[0], device=DEV)
+    got = dc.dc_attention_decomposed_window_chunked(f32(case.q), f32(case.k), f32(case.v), f32(case.pre_w),
+                                                    f32(case.post_w), case.scale, case.window, sl, case.chunk)
+    torch.cuda.synchronize()
+    assert got.dtype == torch.float32
+    assert_close(got.cpu().numpy(), case.out, "fp32 decomposed drop-in")
