@@ -1,4 +1,4 @@
-"""B200-native (sm_100a) DC-attention forward.
+"""B200-native (sm_100a) DC-attention forward and backward.
 
 Drop-in replacements for the reference project's torch-callable DC-attention
 entry points, backed by hand-written CUDA kernels behind a C ABI
@@ -8,7 +8,8 @@ entry points, backed by hand-written CUDA kernels behind a C ABI
 from .api import (DCTerms, dc_attn_fwd, dc_attn_fwd_host, device_error, dc_attention_decomposed_window_chunked,
                   dc_attention_window_chunked_residual,
                   dc_attention_window_chunked_residual_grouped, select_kernel)
+from .backward import DCResidual, TritonDCResidual, dc_attn, dc_attn_bwd
 
 __all__ = ["DCTerms", "dc_attn_fwd", "dc_attn_fwd_host", "dc_attention_window_chunked_residual_grouped",
            "dc_attention_window_chunked_residual", "dc_attention_decomposed_window_chunked",
-           "select_kernel", "device_error"]
+           "select_kernel", "device_error", "dc_attn", "dc_attn_bwd", "DCResidual", "TritonDCResidual"]

@@ -24,7 +24,8 @@ DEV_ERRORS = {0: "DC_DEV_OK", 1: "DC_DEV_ERR_TIMEOUT_Q", 2: "DC_DEV_ERR_TIMEOUT_
               3: "DC_DEV_ERR_TIMEOUT_FREE", 4: "DC_DEV_ERR_TIMEOUT_S", 5: "DC_DEV_ERR_TIMEOUT_P",
               6: "DC_DEV_ERR_TIMEOUT_O"}
 EXPORTS = ("dc_attn_fwd", "dc_attn_fwd_residual", "dc_attn_select_kernel", "dc_attn_read_error",
-           "dc_attn_last_kernel", "dc_attn_last_error", "dc_attn_abi_version", "dc_attn_params_size")
+           "dc_attn_last_kernel", "dc_attn_last_error", "dc_attn_abi_version", "dc_attn_params_size",
+           "dc_attn_bwd", "dc_attn_bwd_params_size")
 
 
 class DcTerms(ctypes.Structure):
@@ -45,6 +46,17 @@ class DcAttnParams(ctypes.Structure):
                 ("out_sh", ctypes.c_int64), ("seq_lens", ctypes.c_void_p),
                 ("err_flag", ctypes.c_void_p), ("pre", DcTerms), ("post", DcTerms),
                 ("wait_us", ctypes.c_uint32), ("test_flags", ctypes.c_int32)]
+
+
+class DcTermGrads(ctypes.Structure):
+    _fields_ = [("w", ctypes.c_void_p), ("qw1", ctypes.c_void_p), ("qw2", ctypes.c_void_p),
+                ("qdd", ctypes.c_void_p), ("qmat", ctypes.c_void_p)]
+
+
+class DcAttnBwdParams(ctypes.Structure):
+    _fields_ = [("fwd", DcAttnParams), ("dout", ctypes.c_void_p), ("dq", ctypes.c_void_p),
+                ("dk", ctypes.c_void_p), ("dv", ctypes.c_void_p), ("dpre", DcTermGrads),
+                ("dpost", DcTermGrads)]
 
 
 _lib = None
@@ -78,10 +90,15 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.dc_attn_fwd_residual.argtypes = [vp] * 9 + [vp, i64, i64, i64, vp] + [i32] * 5 + \
             [ctypes.c_float, i32, i32, i32, vp]
         lib.dc_attn_fwd_residual.restype = ctypes.c_int
+        lib.dc_attn_bwd.argtypes = [ctypes.POINTER(DcAttnBwdParams), ctypes.c_void_p]
+        lib.dc_attn_bwd.restype = ctypes.c_int
+        lib.dc_attn_bwd_params_size.restype = ctypes.c_int
         if lib.dc_attn_abi_version() != ABI_VERSION:
             raise RuntimeError(f"libdcattn ABI {lib.dc_attn_abi_version()} != binding {ABI_VERSION}")
         if lib.dc_attn_params_size() != ctypes.sizeof(DcAttnParams):
             raise RuntimeError("dc_attn_params layout mismatch between library and binding")
+        if lib.dc_attn_bwd_params_size() != ctypes.sizeof(DcAttnBwdParams):
+            raise RuntimeError("dc_attn_bwd_params layout mismatch between library and binding")
         _lib = lib
         return lib
 

@@ -104,26 +104,9 @@ def _infer_rank(*sets: Optional[DCTerms]) -> int:
     return R
 
 
-def dc_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                pre: Optional[DCTerms] = None, post: Optional[DCTerms] = None,
-                scaling: Optional[float] = None, window: Optional[int] = None, G: int = 1,
-                seq_lens: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
-                kernel: str = "auto", check: bool = False, wait_us: int = 0,
-                test_flags: int = 0) -> torch.Tensor:
-    """General DC-attention forward.  q,k,v [B,T,H,D] (bf16 or fp16) -> [B,T,H,D].
-
-    ``window=None`` is full causal; otherwise key s is visible from query t iff
-    t - window < s <= t.  ``pre``/``post`` default to the identity (plain
-    attention).  ``out`` may be any tensor whose last dim is contiguous and whose
-    [b,t,h] strides are positive (e.g. a [B,N,T,D] tensor permuted to
-    [B,T,N,D]); it is written in place and returned.
-
-    Every wait inside the kernels is bounded (``wait_us``, default 2 s); a wait
-    that runs out makes the kernel skip the rest of its work and write a code
-    to the device error word.  ``check=True`` synchronises with the stream and
-    raises ``RuntimeError`` if that happened (otherwise read it later with
-    :func:`device_error`).  ``test_flags`` is for tests only.
-    """
+def _params(q, k, v, pre, post, scaling, window, G, seq_lens, out, kernel, wait_us=0, test_flags=0):
+    """Validate a forward call and build its dc_attn_params; returns
+    (params, out, keep) where `keep` holds converted temporaries alive."""
     _check(q.dim() == 4, f"q must be [B,T,H,D] (got {list(q.shape)})")
     _check(k.shape == q.shape and v.shape == q.shape, "k and v must match q's shape")
     _check(q.dtype in _DTYPES, f"q must be bfloat16 or float16 (got {q.dtype})")
@@ -134,8 +117,8 @@ def dc_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     _check(G >= 1 and H % G == 0, f"H={H} must be divisible by G={G}")
     R = _infer_rank(pre, post)
     device, dtype = q.device, q.dtype
-    keep = []
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    keep = [q, k, v]
     if out is None:
         out = torch.empty((B, T, H, D), device=device, dtype=dtype)
     _check(out.shape == (B, T, H, D) and out.dtype == dtype and out.device == device,
@@ -162,6 +145,33 @@ def dc_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     _check(0 <= int(wait_us) < 2 ** 32, "wait_us must be in [0, 2^32)")
     p.wait_us = int(wait_us)
     p.test_flags = int(test_flags)
+    return p, out, keep
+
+
+def dc_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                pre: Optional[DCTerms] = None, post: Optional[DCTerms] = None,
+                scaling: Optional[float] = None, window: Optional[int] = None, G: int = 1,
+                seq_lens: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None,
+                kernel: str = "auto", check: bool = False, wait_us: int = 0,
+                test_flags: int = 0) -> torch.Tensor:
+    """General DC-attention forward.  q,k,v [B,T,H,D] (bf16 or fp16) -> [B,T,H,D].
+
+    ``window=None`` is full causal; otherwise key s is visible from query t iff
+    t - window < s <= t.  ``pre``/``post`` default to the identity (plain
+    attention).  ``out`` may be any tensor whose last dim is contiguous and whose
+    [b,t,h] strides are positive (e.g. a [B,N,T,D] tensor permuted to
+    [B,T,N,D]); it is written in place and returned.
+
+    Every wait inside the kernels is bounded (``wait_us``, default 2 s); a wait
+    that runs out makes the kernel skip the rest of its work and write a code
+    to the device error word.  ``check=True`` synchronises with the stream and
+    raises ``RuntimeError`` if that happened (otherwise read it later with
+    :func:`device_error`).  ``test_flags`` is for tests only.
+    """
+    p, out, keep = _params(q, k, v, pre, post, scaling, window, G, seq_lens, out, kernel, wait_us, test_flags)
+    device = q.device
+    B, T, H, D = q.shape
+    R = p.R
     lib = _lib.load()
     with torch.cuda.device(device):
         stream = torch.cuda.current_stream(device).cuda_stream
@@ -181,13 +191,11 @@ _SIMT_WARNED = set()
 def _warn_simt(T, H, D, G, R, window, pre, post):
     """One warning per distinct request shape that AUTO had to run on the
     CUDA-core kernel (two orders of magnitude slower than the tensor-core ones)."""
-    has_qmat = any(tm is not None and tm.qmat is not None for tm in (pre, post))
-    key = (T, H, D, G, R, window, has_qmat)
+    key = (T, H, D, G, R, window)
     if key in _SIMT_WARNED:
         return
     _SIMT_WARNED.add(key)
-    why = ("per-query mixing matrices (qmat)" if has_qmat else
-           f"D={D}, heads per group={H // G}, R={R}, window={window}")
+    why = f"D={D}, heads per group={H // G}, R={R}, window={window}"
     warnings.warn(f"dc_attn_fwd: no tensor-core kernel supports this call ({why}); "
                   "it runs on the CUDA-core kernel, which is much slower", RuntimeWarning, stacklevel=3)
 

@@ -22,6 +22,8 @@ bool tcs_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tcs(const dc_attn_params &p, cudaStream_t st);
 bool tcm_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tcm(const dc_attn_params &p, cudaStream_t st);
+bool bwd_supports(const dc_attn_params &p, std::string *why);
+cudaError_t launch_bwd(const dc_attn_bwd_params &p, cudaStream_t st, std::string *why);
 }  // namespace dcattn
 
 // The library's own device error word, used when a caller passes no
@@ -176,6 +178,30 @@ int dc_attn_fwd(const dc_attn_params *pp, void *stream) {
 }
 
 int dc_attn_last_kernel(void) { return g_last_kernel; }
+
+int dc_attn_bwd_params_size(void) { return (int)sizeof(dc_attn_bwd_params); }
+
+int dc_attn_bwd(const dc_attn_bwd_params *bp, void *stream) {
+  if (!bp) return fail(DC_ERR_NULL, "params is NULL");
+  dc_attn_params f = bp->fwd;
+  if (!f.out) f.out = bp->dq;  // the forward output is not used; validate() wants a pointer
+  if (f.out_sb < 1 || f.out_st < 1 || f.out_sh < f.D) {
+    f.out_sh = f.D; f.out_st = (int64_t)f.H * f.D; f.out_sb = (int64_t)f.T * f.H * f.D;
+  }
+  int rc = validate(&f);
+  if (rc != DC_OK) return rc;
+  if (!bp->dout || !bp->dq || !bp->dk || !bp->dv) return fail(DC_ERR_NULL, "dout, dq, dk and dv must be non-NULL");
+  std::string why;
+  if (!dcattn::bwd_supports(f, &why)) return fail(DC_ERR_UNSUPPORTED, "backward: %s", why.c_str());
+  if ((rc = check_device()) != DC_OK) return rc;
+  dc_attn_bwd_params p = *bp;
+  p.fwd = f;
+  cudaError_t e = dcattn::launch_bwd(p, reinterpret_cast<cudaStream_t>(stream), &why);
+  if (e == cudaErrorInvalidValue && !why.empty()) return fail(DC_ERR_UNSUPPORTED, "backward: %s", why.c_str());
+  if (e != cudaSuccess) return fail(DC_ERR_LAUNCH, "backward launch failed: %s", cudaGetErrorString(e));
+  g_last_error.clear();
+  return DC_OK;
+}
 
 int dc_attn_read_error(int32_t *err_flag, int clear, void *stream) {
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

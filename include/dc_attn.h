@@ -148,6 +148,42 @@ DC_API int dc_attn_fwd_residual(const void *q, const void *k, const void *v,
                          int32_t D, int32_t G, float scaling, int32_t window,
                          int32_t chunk_size, int32_t dtype, void *stream);
 
+/* Gradients of one composition term set, fp32, caller-owned; a NULL pointer
+ * means the gradient is not wanted.  Shapes as in dc_terms.  The per-token
+ * gradients are written; w is a sum over every (b, t) and is zeroed by the
+ * library before it accumulates. */
+typedef struct dc_term_grads {
+  float *w;     /* [G, HPG, HPG]  */
+  float *qw1;   /* [B, T, H, R]   */
+  float *qw2;   /* [B, T, R, H]   */
+  float *qdd;   /* [B, T, H]      */
+  float *qmat;  /* [B, T, H, HPG] */
+} dc_term_grads;
+
+typedef struct dc_attn_bwd_params {
+  dc_attn_params fwd;  /* the forward call being differentiated (out, out
+                          strides, kernel, wait_us and test_flags unused) */
+  const void *dout;    /* [B, T, H, D] contiguous, dtype of the forward     */
+  void *dq;            /* [B, T, H, D] contiguous, dtype of the forward     */
+  float *dk, *dv;      /* [B, T, H, D] contiguous fp32: zeroed, then
+                          accumulated by the library (keys are shared by
+                          neighbouring query blocks)                        */
+  dc_term_grads dpre, dpost;
+} dc_attn_bwd_params;
+
+/* Backward of dc_attn_fwd for the query-side term family (identity, w,
+ * qw1/qw2 of rank <= 2, qdd, qmat; key-wise terms are not covered) and
+ * heads per group in {1, 2, 4, 8, 16, 32}, D = 128, windows whose key span
+ * fits one block (any practical sliding window; full causal only for short
+ * T).  Replaces TritonDCResidual.backward (triton_dc_residual.py:1707-1892),
+ * which returns dq in the input dtype and dk, dv and the six weight
+ * gradients in fp32, as here.  Everything is recomputed from q, k, v and the
+ * weights; no forward state is needed.  Returns DC_OK or a DC_ERR_* code. */
+DC_API int dc_attn_bwd(const dc_attn_bwd_params *p, void *stream);
+
+/* sizeof(dc_attn_bwd_params) in this build. */
+DC_API int dc_attn_bwd_params_size(void);
+
 /* Read the device error word `err_flag` (NULL = the library's word on the
  * current device) after the work queued on `stream` so far: the call enqueues
  * a copy on `stream` and synchronises with it.  Returns the DC_DEV_* code

@@ -25,21 +25,22 @@ def _t(x):
 
 
 def _compose(a, tm: Terms, b, hs, g, tq, sk):
+    f = lambda x: _t(x).to(a.dtype)
     out = a.clone() if tm.identity else torch.zeros_like(a)
     if tm.w is not None:
-        out += torch.einsum("hts,hk->kts", a, _t(tm.w)[g].float())
+        out = out + torch.einsum("hts,hk->kts", a, f(tm.w)[g])
     if tm.qw1 is not None:
-        agg = torch.einsum("hts,thr->rts", a, _t(tm.qw1)[b, tq, hs, :].float())
-        out += torch.einsum("rts,trh->hts", agg, _t(tm.qw2)[b, tq, :, hs].float())
+        agg = torch.einsum("hts,thr->rts", a, f(tm.qw1)[b, tq, hs, :])
+        out = out + torch.einsum("rts,trh->hts", agg, f(tm.qw2)[b, tq, :, hs])
     if tm.kw1 is not None:
-        agg = torch.einsum("hts,shr->rts", a, _t(tm.kw1)[b, sk, hs, :].float())
-        out += torch.einsum("rts,srh->hts", agg, _t(tm.kw2)[b, sk, :, hs].float())
+        agg = torch.einsum("hts,shr->rts", a, f(tm.kw1)[b, sk, hs, :])
+        out = out + torch.einsum("rts,srh->hts", agg, f(tm.kw2)[b, sk, :, hs])
     if tm.qdd is not None:
-        out += a * _t(tm.qdd)[b, tq, hs].float().T[:, :, None]
+        out = out + a * f(tm.qdd)[b, tq, hs].T[:, :, None]
     if tm.kdd is not None:
-        out += a * _t(tm.kdd)[b, sk, hs].float().T[:, None, :]
+        out = out + a * f(tm.kdd)[b, sk, hs].T[:, None, :]
     if tm.qmat is not None:
-        out += torch.einsum("tij,jts->its", _t(tm.qmat)[b, tq, hs, :].float(), a)
+        out = out + torch.einsum("tij,jts->its", f(tm.qmat)[b, tq, hs, :], a)
     return out
 
 
@@ -47,10 +48,42 @@ def _compose(a, tm: Terms, b, hs, g, tq, sk):
 def dc_attn_torch_cpu(q, k, v, pre: Terms, post: Terms, scale: float, window: Optional[int],
                       G: int = 1, seq_lens=None, chunk: int = 256, t_range=None) -> torch.Tensor:
     """fp32 torch-CPU forward; returns [B,T,H,D] (rows outside ``t_range`` are 0)."""
-    q, k, v = (_t(x).float() for x in (q, k, v))
+    return _forward(q, k, v, pre, post, scale, window, G, seq_lens, chunk, t_range, torch.float32)
+
+
+GRAD_TERMS = ("w", "qw1", "qw2", "qdd", "qmat")
+
+
+def dc_attn_torch_grads(q, k, v, pre: Terms, post: Terms, scale: float, window: Optional[int], G: int,
+                        seq_lens, dout, chunk: int = 256):
+    """Gradients of sum(out * dout) by torch autograd through the float64
+    forward (the backward's checker): a dict with dq, dk, dv and, per set
+    ("pre", "post"), the gradient of each query-side term present
+    (``GRAD_TERMS``), as numpy arrays."""
+    leaf = lambda x: torch.tensor(x, dtype=torch.float64, requires_grad=True)
+    qt, kt, vt = leaf(q), leaf(k), leaf(v)
+    sets, leaves = [], {}
+    for name, tm in (("pre", pre), ("post", post)):
+        r = Terms(identity=tm.identity, kw1=tm.kw1, kw2=tm.kw2, kdd=tm.kdd)
+        for n in GRAD_TERMS:
+            if getattr(tm, n) is not None:
+                leaves[(name, n)] = leaf(getattr(tm, n))
+                setattr(r, n, leaves[(name, n)])
+        sets.append(r)
+    with torch.enable_grad():
+        out = _forward(qt, kt, vt, sets[0], sets[1], scale, window, G, seq_lens, chunk, None, torch.float64)
+        (out * torch.as_tensor(dout, dtype=torch.float64)).sum().backward()
+    res = {"dq": qt.grad.numpy(), "dk": kt.grad.numpy(), "dv": vt.grad.numpy()}
+    for (name, n), t in leaves.items():
+        res[f"{name}_{n}"] = t.grad.numpy()
+    return res
+
+
+def _forward(q, k, v, pre: Terms, post: Terms, scale, window, G, seq_lens, chunk, t_range, dtype):
+    q, k, v = (_t(x).to(dtype) for x in (q, k, v))
     B, T, H, D = q.shape
     hpg = H // G
-    out = torch.zeros(B, T, H, D)
+    out = torch.zeros(B, T, H, D, dtype=dtype)
     ta, tb = (0, T) if t_range is None else t_range
     for b in range(B):
         slen = T if seq_lens is None else int(seq_lens[b])

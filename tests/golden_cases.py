@@ -71,3 +71,32 @@ class Case:
 def load_cases():
     z = np.load(PATH)
     return [Case(z, str(n)) for n in z["cases"]]
+
+
+GRAD_PATH = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "golden_grad.npz")
+WNAMES = ("pre_w1", "pre_w2", "pre_dd", "post_w1", "post_w2", "post_dd")
+
+
+class GradCase:
+    """One golden backward case (tests/golden/make_golden_grad.py): bf16 inputs,
+    the output gradient dout [B,N,T,D] of the reference's grouped function, and
+    the reference's autograd gradients (fp32)."""
+
+    def __init__(self, z, name):
+        self.name = name
+        self.B, self.T, self.H, self.D, self.G, self.window = (int(x) for x in z[f"{name}/meta"])
+        sl = z[f"{name}/seq_lens"]
+        self.seq_lens = None if sl.size == 0 else sl.astype(np.int32)
+        self.q, self.k, self.v = (_load_input(z, f"{name}/{k}") for k in ("q", "k", "v"))
+        self.ws = [_load_input(z, f"{name}/{n}") for n in WNAMES]
+        self.dout = _load_input(z, f"{name}/dout")               # [B,N,T,D]
+        self.dout_btnd = self.dout.transpose(0, 2, 1, 3).copy()  # [B,T,N,D]
+        self.grads = {k: z[f"{name}/{k}"] for k in ("dq", "dk", "dv")}
+        for n in WNAMES:
+            self.grads[f"d_{n}"] = z[f"{name}/d_{n}"]
+        self.scale = 1.0 / np.sqrt(self.D)
+
+
+def load_grad_cases():
+    with np.load(GRAD_PATH) as z:
+        return [GradCase(z, str(n)) for n in z["cases"]]

@@ -101,3 +101,28 @@ def test_torch_cpu_port_matches_numpy_oracle():
         a = O.dc_attn_oracle(q, k, v, pre, post, 0.2, window, 2, [90, 50])
         b = dc_attn_torch_cpu(q, k, v, pre, post, 0.2, window, 2, [90, 50], chunk=32).numpy()
         np.testing.assert_allclose(a, b, atol=2e-5, rtol=0)
+
+
+# ---------------------------------------------------------------- backward oracle
+
+from oracle.dc_oracle_torch import dc_attn_torch_grads  # noqa: E402
+from tests.golden_cases import load_grad_cases  # noqa: E402
+
+
+def _oracle_grads(c):
+    pre, post = O.residual_terms(*c.ws[:3]), O.residual_terms(*c.ws[3:])
+    g = dc_attn_torch_grads(c.q, c.k, c.v, pre, post, c.scale, c.window, c.G, c.seq_lens, c.dout_btnd)
+    # the residual weights are [B,T,N] views of the rank-1 factors [B,T,N,1] / [B,T,1,N]
+    return {"dq": g["dq"], "dk": g["dk"], "dv": g["dv"],
+            "d_pre_w1": g["pre_qw1"][..., 0], "d_pre_w2": g["pre_qw2"][:, :, 0], "d_pre_dd": g["pre_qdd"],
+            "d_post_w1": g["post_qw1"][..., 0], "d_post_w2": g["post_qw2"][:, :, 0], "d_post_dd": g["post_qdd"]}
+
+
+@pytest.mark.parametrize("case", load_grad_cases(), ids=lambda c: c.name)
+def test_backward_oracle_matches_reference_autograd(case):
+    """The float64 autograd oracle against autograd through the reference's own
+    torch function (fp32) on the same inputs and output gradient."""
+    got = _oracle_grads(case)
+    for k, ref in case.grads.items():
+        scale = max(float(np.abs(ref).max()), 1e-6)
+        np.testing.assert_allclose(got[k], ref, rtol=0, atol=2e-5 * max(1.0, scale), err_msg=k)

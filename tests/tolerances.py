@@ -29,3 +29,25 @@ def assert_close(got, ref, what="", max_abs=MAX_ABS, max_rel=MAX_REL, mean_abs=M
     mean_gate = max(mean_abs, mean_rel * (float(np.abs(ref).mean()) if ref.size else 0.0))
     assert mx <= max_abs and mx / scale <= max_rel and mean <= mean_gate, msg
     return mx, mean
+
+
+# Gradients (backward kernel, fp32 arithmetic; dq rounded to the input dtype,
+# dk / dv / weight gradients fp32) against the float64 autograd oracle or the
+# reference's fp32 autograd on the same inputs.  Gradient magnitudes differ by
+# orders between tensors, so the gate is relative to each tensor's largest
+# entry: max|d| <= GRAD_MAX_REL * max|ref| and
+# mean|d| <= GRAD_MEAN_REL * mean|ref| + 1e-4 * max|ref|.
+GRAD_MAX_REL = 1e-2
+GRAD_MEAN_REL = 4e-3
+
+
+def assert_grad_close(got, ref, what=""):
+    got = np.asarray(got, dtype=np.float64)
+    ref = np.asarray(ref, dtype=np.float64)
+    assert got.shape == ref.shape, f"{what}: shape {got.shape} != {ref.shape}"
+    assert np.all(np.isfinite(got)), f"{what}: non-finite gradient"
+    d = np.abs(got - ref)
+    scale = max(float(np.abs(ref).max()), 1e-12)
+    mx, mean = float(d.max()), float(d.mean())
+    msg = f"{what}: max|d|={mx:.3e} (max|ref|={scale:.3e}) mean|d|={mean:.3e}"
+    assert mx <= GRAD_MAX_REL * scale and mean <= GRAD_MEAN_REL * float(np.abs(ref).mean()) + 1e-4 * scale, msg
