@@ -322,13 +322,14 @@ def run_ours(args, cfg, world, rank, local):
         by = 4 * B * T * H * D * 2 + 2 * B * T * H * (H // G) * 2
     achieved = by / (ms_step * 1e-3) / 1e9
     tflops_rank = fl_rank / (ms_step * 1e-3) / 1e12
-    strong = best = others = None
+    strong = best = others = bwd = None
     if not args.no_extra:
         del qh, kh, vh, host_sets, out_host
         strong = strong_scaling_config4(world, rank, local)
         if rank == 0:
             best = repo_best(local)
             others = other_layers(local)
+            bwd = backward_layer(local)
     if rank != 0:
         return
     cpu = None
@@ -358,6 +359,7 @@ def run_ours(args, cfg, world, rank, local):
         line["strong_scaling"] = strong
         line["repo_best"] = best
         line["other_layers"] = others
+        line["backward"] = bwd
     print(json.dumps(line), flush=True)
 
 
@@ -407,6 +409,30 @@ def other_layers(local, steps=5, warmup=3):
         torch.cuda.empty_cache()
     res["timing"] = f"CUDA events, {warmup} warm-up + {steps} calls, inputs larger than L2"
     return res
+
+
+def backward_layer(local, steps=3, warmup=2):
+    """The backward (dc_attn_bwd) at the headline layer (config1 G8 W128, the
+    query-side terms: static W, rank-1 query-wise weights, qdd; key-wise terms
+    have no backward).  FLOPs counted: QK^T recompute, dP' = dO V^T, dV, dQ and
+    dK (10 D per (b, h, t, s) pair) plus twice the forward's composition."""
+    import dc_triton_opt_b200 as dc
+    device = torch.device("cuda", local)
+    cfg = dict(WORKLOADS["config1"])
+    q, k, v, pre, post = make_inputs(cfg, device, seed=5)
+    for t in (pre, post):
+        t.kw1 = t.kw2 = t.kdd = None
+    dout = torch.randn_like(q)
+    B, T, H, D, G, R, W = (cfg[x] for x in ("B", "T", "H", "D", "G", "R", "window"))
+    call = lambda: dc.dc_attn_bwd(dout, q, k, v, pre, post, D ** -0.5, W, G)
+    ms = time_calls(call, steps, warmup, torch.cuda.current_stream(device), 1)
+    npairs = pairs(T, W)
+    fl = 10 * D * H * B * npairs + 2 * (flops(B, H, D, G, R, npairs) - 4 * D * H * B * npairs)
+    del q, k, v, pre, post, dout
+    torch.cuda.empty_cache()
+    return {"workload": "config1", "G": G, "window": W, "R": R, "ms_per_call": ms,
+            "tflops": fl / (ms * 1e-3) / 1e12, "kernel": "dc_bwd_kernel (CUDA cores, fp32)",
+            "timing": f"CUDA events, {warmup} warm-up + {steps} calls"}
 
 
 def strong_scaling_config4(world, rank, local, steps=5, warmup=3):

@@ -974,13 +974,12 @@ __global__ void __launch_bounds__(32 * NW, 1)
       for (int h = 0; h < HPG; ++h) dst[h] = raw16_get<E, HPG>(v, h);
     };
     // per-query matrices of a tile (group g) from the raw values -> mrec[par]
-    auto build_m = [&](int par, int q0, int b, int g, int tid, int nthr) {
+    auto build_m = [&](int par, int g, int tid, int nthr) {
       float *dst = mrec + par * NM;
       for (int idx = tid; idx < NM; idx += nthr) {
         const int set = idx / (BM * MF), i = (idx / MF) % BM, h1 = (idx % MF) / HPG, h = idx % HPG;
         const float *rr = raw + (set * BM + i) * RAWF;
-        float m = Wt[((set * G + g) * HPG + h1) * HPG + h] + (h1 == h ? rr[h] : 0.f) +
-                  qmat_at<E>(set ? p.post : p.pre, b, q0 + i, T, H, HPG, g * HPG, h1, h);
+        float m = Wt[((set * G + g) * HPG + h1) * HPG + h] + (h1 == h ? rr[h] : 0.f);
 #pragma unroll
         for (int r = 0; r < R; ++r) m = fmaf(rr[HPG + h1 * R + r], rr[HPG + HPG * R + r * HPG + h], m);
         // with PAIR the pair layout [set][query / 2][h'][h][query % 2] (compose_m2)
@@ -1038,7 +1037,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
           chunk_store(c, src ? ld_raw16<HPG>(src) : raw16_zero<HPG>());
         }
         ptx::named_bar_sync(1, ncompose);
-        build_m(0, q0, b, g, ctid, ncompose);
+        build_m(0, g, ctid, ncompose);
         if constexpr (EARLY_M) ptx::named_bar_sync(1, ncompose);  // the first tile's matrices are visible
       }
       // (8 heads per group: 64-entry matrices; built after the statistics by all
@@ -1197,13 +1196,13 @@ __global__ void __launch_bounds__(32 * NW, 1)
       // there are no others)
       if constexpr (EARLY_M) {
         const int nb0 = ncompose > NQ ? NQ : 0;
-        if (ntile < ntiles && ctid >= nb0) build_m(buf ^ 1, nq0, nb, ng, ctid - nb0, ncompose - nb0);
+        if (ntile < ntiles && ctid >= nb0) build_m(buf ^ 1, ng, ctid - nb0, ncompose - nb0);
       }
       ptx::named_bar_sync(1, ncompose);
       // post-set key weights into the registers of the pre set (dead after pass 1)
       if (active) load_key(p.post, 1.f, ktok, hbase, key_ok);
       if constexpr (!EARLY_M)
-        if (ntile < ntiles) build_m(buf ^ 1, nq0, nb, ng, ctid, ncompose);
+        if (ntile < ntiles) build_m(buf ^ 1, ng, ctid, ncompose);
       // P' of key tile 0 overwrites Q: every QK product of this tile must be complete
       if (ok && kt == 0 && nkt > 1) {
         ok = ptx::mbar_wait(bar_S + 2 * buf + nkt - 1, (it >> 1) & 1, WAIT);
@@ -1386,7 +1385,11 @@ static cudaError_t launch_p(const dc_attn_params &p, cudaStream_t st) {
 
 template <typename E, int HPG>
 static cudaError_t launch_r(const dc_attn_params &p, cudaStream_t st) {
-  if (num_key_tiles(HPG, p.window) <= 2)
+  // per-query mixing matrices (the decomposed form) run on the one-tile-per-CTA
+  // kernel, which folds them into its per-query matrices; the persistent
+  // kernel's matrix build stays free of them
+  const bool qmat = p.pre.qmat || p.post.qmat;
+  if (num_key_tiles(HPG, p.window) <= 2 && !qmat)
     return p.R <= 1 ? launch_p<E, HPG, 1>(p, st) : launch_p<E, HPG, 2>(p, st);
   return p.R <= 1 ? launch_t<E, HPG, 1>(p, st) : launch_t<E, HPG, 2>(p, st);
 }
