@@ -44,7 +44,7 @@ namespace bwd {
 
 constexpr int D = 128;
 constexpr int DP = D + 8;     // padded smem row of a q / dO / k / v row (elements): 16-byte loads conflict-free
-constexpr int NT = 256;       // threads per CTA
+constexpr int NT = 512;       // threads per CTA
 constexpr int MAX_SMEM = 227 * 1024;
 
 struct Geo {
@@ -216,9 +216,14 @@ __global__ void __launch_bounds__(NT, 1) dc_bwd_kernel(const BwdParams p, const 
   };
   // per key j, mix the HPG values of query i: dst[(h, i)][j] = sum_h' M[i][h'][h] src[(h', i)][j]
   // (transposed: dst[(h', i)][j] = sum_h M[i][h'][h] src[(h, i)][j])
+  // (a task is one key of one query and OC of its outputs; in-place use needs
+  // OC == HPG so that a task reads every input before it writes)
   auto mix = [&](const float *M, const float *src, float *dst, bool transposed, bool mask) {
-    for (int idx = tid; idx < BM * SPR; idx += NT) {
-      const int j = idx % SPR, i = idx / SPR;
+    constexpr int OC = HPG < 8 ? HPG : 8;
+    const int noc = (src == dst) ? 1 : HPG / OC;
+    for (int idx = tid; idx < BM * SPR * noc; idx += NT) {
+      const int j = idx % SPR, i = (idx / SPR) % BM, o0 = (idx / (SPR * BM)) * (noc > 1 ? OC : 0);
+      const int o1 = noc > 1 ? o0 + OC : HPG;
       if (j >= span) continue;
       float a[HPG];
 #pragma unroll
@@ -226,7 +231,7 @@ __global__ void __launch_bounds__(NT, 1) dc_bwd_kernel(const BwdParams p, const 
       const bool ok = !mask || valid(q0 + i, k_lo + j);
       const float *Mi = M + i * HPG * HPG;
 #pragma unroll 4
-      for (int o = 0; o < HPG; ++o) {
+      for (int o = o0; o < o1; ++o) {
         float x = 0.f;
 #pragma unroll
         for (int k = 0; k < HPG; ++k) x = fmaf(transposed ? Mi[o * HPG + k] : Mi[k * HPG + o], a[k], x);
@@ -236,12 +241,15 @@ __global__ void __launch_bounds__(NT, 1) dc_bwd_kernel(const BwdParams p, const 
   };
   // dM[i][h'][h] = sum_j X[(h', i)][j] Y[(h, i)][j], then the weight gradients of one term set
   auto grad_m = [&](const float *X, const float *Y, int set) {
-    for (int idx = tid; idx < BM * HPG * HPG; idx += NT) {
+    // one warp per entry, lanes along the keys (contiguous, conflict-free)
+    for (int idx = warp; idx < BM * HPG * HPG; idx += NT / 32) {
       const int i = idx / (HPG * HPG), h1 = (idx / HPG) % HPG, h = idx % HPG;
       const float *x = X + (h1 * BM + i) * SP, *y = Y + (h * BM + i) * SP;
       float acc = 0.f;
-      for (int j = 0; j < span; ++j) acc = fmaf(x[j], y[j], acc);
-      dM[idx] = acc;
+      for (int j = lane; j < span; j += 32) acc = fmaf(x[j], y[j], acc);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+      if (lane == 0) dM[idx] = acc;
     }
     __syncthreads();
     const TermG &gr = set ? p.gpost : p.gpre;
