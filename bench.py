@@ -376,7 +376,10 @@ def time_calls(call, steps, warmup, stream, world):
         call()
     ev1.record(stream)
     torch.cuda.synchronize()
-    return max_over_ranks(ev0.elapsed_time(ev1) / steps, stream.device)
+    ms = ev0.elapsed_time(ev1) / steps
+    # world == 1: a measurement on this rank alone (rank 0's extra blocks run
+    # while the other ranks have finished), so no collective
+    return max_over_ranks(ms, stream.device) if world > 1 else ms
 
 
 # The other BASELINE layers, timed in the same run (device time only): the
