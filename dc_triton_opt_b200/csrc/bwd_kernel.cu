@@ -36,6 +36,7 @@
 #include <cuda_runtime.h>
 
 #include <string>
+#include <type_traits>
 
 #include "common.cuh"
 
@@ -49,7 +50,7 @@ constexpr int MAX_SMEM = 227 * 1024;
 
 struct Geo {
   int BM, NC, span, SP, SPR;
-  int l_off, p_off, d_off, q_off, do_off, kv_off, m_off, rec_off, dq_off, total;
+  int l_off, p_off, d_off, q_off, do_off, kv_off, m_off, rec_off, total;
 };
 
 __host__ __device__ inline int rup(int x, int a) { return (x + a - 1) / a * a; }
@@ -67,13 +68,14 @@ __host__ __device__ inline Geo make_geo(int BM, int W, int esize) {
   g.p_off = o; o += g.NC * g.SP * 4;                     // S, then P
   g.d_off = o; o += g.NC * g.SP * 4;                     // P', dP', dP, then dS
   o = rup(o, 16);
-  g.q_off = o; o += g.NC * DP * esize;                   // q rows
-  g.do_off = o; o += g.NC * DP * esize;                  // dO rows
-  g.kv_off = o; o += g.span * DP * esize;                // one head's K or V rows of the span
+  // row counts padded so that 16-row tensor-core fragments never leave a region
+  // (the pad rows are zeroed once and never written)
+  g.q_off = o; o += (rup(g.NC, 16) + 16) * DP * esize;   // q rows
+  g.do_off = o; o += (rup(g.NC, 16) + 16) * DP * esize;  // dO rows
+  g.kv_off = o; o += (rup(g.span, 16) + 16) * DP * esize;  // one head's K or V rows of the span
   o = rup(o, 16);
   g.m_off = o; o += 3 * BM * HPG * HPG * 4;              // Mpre, Mpost, dM
   g.rec_off = o; o += 2 * 2 * BM * HPG * R * 4;          // [set][qw1 | qw2][BM][HPG * R]
-  g.dq_off = o; o += BM * D * 4;                         // dQ accumulator of one head
   g.total = o;
   return g;
 }
@@ -81,6 +83,51 @@ __host__ __device__ inline Geo make_geo(int BM, int W, int esize) {
 __device__ __forceinline__ void red_add_v4(float *addr, float a, float b, float c, float d) {
   asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
                : "memory");
+}
+
+// ---- warp-level tensor-core products (mma.sync m16n8k16, fp32 accumulate).
+// Fragment layout (g = lane / 4, t = lane % 4): A 16x16 row-major as
+// a0 (g, 2t..2t+1), a1 (g+8, 2t..), a2 (g, 2t+8..), a3 (g+8, 2t+8..);
+// B 16x8 as b0 (k 2t..2t+1, n g), b1 (k 2t+8.., n g); C 16x8 as
+// c0 c1 (g, 2t..2t+1), c2 c3 (g+8, 2t..2t+1).
+template <typename E>
+__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], const uint32_t (&b)[2]) {
+  if constexpr (std::is_same<E, __nv_bfloat16>::value)
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+  else
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+                 "{%0,%1,%2,%3};"
+                 : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t (&r)[2], const void *p) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];"
+               : "=r"(r[0]), "=r"(r[1]) : "r"(smem_u32(p)));
+}
+
+template <typename E>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  E a = from_f<E>(lo), b = from_f<E>(hi);
+  return static_cast<uint32_t>(*reinterpret_cast<uint16_t *>(&a)) |
+         (static_cast<uint32_t>(*reinterpret_cast<uint16_t *>(&b)) << 16);
+}
+
+__device__ __forceinline__ void red_add_v2(float *addr, float a, float b) {
+  asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(addr), "f"(a), "f"(b) : "memory");
 }
 
 template <typename E>
@@ -119,7 +166,6 @@ __global__ void __launch_bounds__(NT, 1) dc_bwd_kernel(const BwdParams p, const 
   float *Mpre = reinterpret_cast<float *>(smem + geo.m_off);
   float *Mpost = Mpre + BM * HPG * HPG, *dM = Mpost + BM * HPG * HPG;
   float *rec = reinterpret_cast<float *>(smem + geo.rec_off);
-  float *dqa = reinterpret_cast<float *>(smem + geo.dq_off);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int b = blockIdx.y / p.G, g = blockIdx.y % p.G;
@@ -141,6 +187,18 @@ __global__ void __launch_bounds__(NT, 1) dc_bwd_kernel(const BwdParams p, const 
     }
     *reinterpret_cast<uint4 *>(Qs + c * DP + ch * 8) = uq;
     *reinterpret_cast<uint4 *>(dOs + c * DP + ch * 8) = ud;
+  }
+  {
+    const int nq = rup(NC, 16) + 16, nkv = rup(span, 16) + 16;
+    for (int idx = tid; idx < (nq - NC) * (DP / 8); idx += NT) {
+      const int r = NC + idx / (DP / 8), ch = idx % (DP / 8);
+      *reinterpret_cast<uint4 *>(Qs + r * DP + ch * 8) = make_uint4(0, 0, 0, 0);
+      *reinterpret_cast<uint4 *>(dOs + r * DP + ch * 8) = make_uint4(0, 0, 0, 0);
+    }
+    for (int idx = tid; idx < (nkv - span) * (DP / 8); idx += NT) {
+      const int r = span + idx / (DP / 8), ch = idx % (DP / 8);
+      *reinterpret_cast<uint4 *>(KVs + r * DP + ch * 8) = make_uint4(0, 0, 0, 0);
+    }
   }
   for (int idx = tid; idx < 2 * 2 * BM * HPG * R; idx += NT) {
     const int set = idx / (2 * BM * HPG * R), part = (idx / (BM * HPG * R)) % 2, rem = idx % (BM * HPG * R);
@@ -179,7 +237,6 @@ __global__ void __launch_bounds__(NT, 1) dc_bwd_kernel(const BwdParams p, const 
   }
 
   // ---- rows x staged K/V rows of one head: out[(h, i)][j] = f * sum_d A[(h, i)][d] KV[j][d]
-  constexpr int IC = 8;  // queries per task
   auto stage = [&](const E *src, int h) {
     for (int idx = tid; idx < span * (D / 8); idx += NT) {
       const int j = idx / (D / 8), ch = idx % (D / 8), s = k_lo + j;
@@ -188,30 +245,55 @@ __global__ void __launch_bounds__(NT, 1) dc_bwd_kernel(const BwdParams p, const 
       *reinterpret_cast<uint4 *>(KVs + j * DP + ch * 8) = u;
     }
   };
+  // out[(h, i)][j] = f * sum_d A[(h, i)][d] KV[j][d] on the tensor cores:
+  // M = keys (16 per tile, A operand = KV rows), N = queries (8 per tile,
+  // B operand = rows of A), K = d
   auto rows_x_kv = [&](const E *A, float *out, int h, float f) {
-    const int nic = (BM + IC - 1) / IC;
-    for (int idx = tid; idx < nic * SPR; idx += NT) {
-      const int j = idx % SPR, i0 = (idx / SPR) * IC;
-      if (j >= span) continue;
-      float acc[IC];
+    const int nmt = (span + 15) / 16, nnt = (BM + 7) / 8;
+    const int g8 = lane >> 2, t4 = lane & 3;
+    for (int tile = warp; tile < nmt * nnt; tile += NT / 32) {
+      const int mt = tile % nmt, nt = tile / nmt;
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int ii = 0; ii < IC; ++ii) acc[ii] = 0.f;
-      for (int d = 0; d < D; d += 8) {
-        float kv[8];
-        ld8<E>(KVs + j * DP + d, kv);
-#pragma unroll
-        for (int ii = 0; ii < IC; ++ii) {
-          if (i0 + ii < BM) {
-            float a[8];
-            ld8<E>(A + (h * BM + i0 + ii) * DP + d, a);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) acc[ii] = fmaf(a[e], kv[e], acc[ii]);
-          }
-        }
+      for (int ks = 0; ks < D / 16; ++ks) {
+        uint32_t af[4], bf[2];
+        ldsm_x4(af, KVs + (mt * 16 + (lane & 15)) * DP + ks * 16 + (lane >> 4) * 8);
+        ldsm_x2(bf, A + (h * BM + nt * 8 + (lane & 7)) * DP + ks * 16 + ((lane >> 3) & 1) * 8);
+        mma16816<E>(c, af, bf);
       }
 #pragma unroll
-      for (int ii = 0; ii < IC; ++ii)
-        if (i0 + ii < BM) out[(h * BM + i0 + ii) * SP + j] = f * acc[ii];
+      for (int e = 0; e < 4; ++e) {
+        const int j = mt * 16 + g8 + (e >> 1) * 8, i = nt * 8 + 2 * t4 + (e & 1);
+        if (j < span && i < BM) out[(h * BM + i) * SP + j] = f * c[e];
+      }
+    }
+  };
+  // dst[s_j][d] += f * sum_i X[(h, i)][j] Y[(h, i)][d] over the block's queries
+  // (dV with X = P', Y = dO; dK with X = dL, Y = Q): M = keys, N = d, K = queries
+  auto kv_grad = [&](const float *X, const E *Y, float *dst, int h, float f) {
+    const int nmt = (span + 15) / 16, nks = (BM + 15) / 16;
+    const int g8 = lane >> 2, t4 = lane & 3;
+    for (int tile = warp; tile < nmt * (D / 8); tile += NT / 32) {
+      const int mt = tile % nmt, nt = tile / nmt;
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int ks = 0; ks < nks; ++ks) {
+        uint32_t af[4], bf[2];
+#pragma unroll
+        for (int r = 0; r < 4; ++r) {
+          const int j = mt * 16 + g8 + (r & 1) * 8, i = ks * 16 + 2 * t4 + (r >> 1) * 8;
+          const float x0 = i < BM ? X[(h * BM + i) * SP + j] : 0.f;
+          const float x1 = i + 1 < BM ? X[(h * BM + i + 1) * SP + j] : 0.f;
+          af[r] = pack2<E>(x0, x1);
+        }
+        ldsm_x2_t(bf, Y + (h * BM + ks * 16 + (lane & 15)) * DP + nt * 8);
+        mma16816<E>(c, af, bf);
+      }
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const int j = mt * 16 + g8 + half * 8, s = k_lo + j;
+        if (j < span && s >= 0 && s < T)
+          red_add_v2(dst + row(s, h) + nt * 8 + 2 * t4, f * c[2 * half], f * c[2 * half + 1]);
+      }
     }
   };
   // per key j, mix the HPG values of query i: dst[(h, i)][j] = sum_h' M[i][h'][h] src[(h', i)][j]
@@ -318,21 +400,7 @@ __global__ void __launch_bounds__(NT, 1) dc_bwd_kernel(const BwdParams p, const 
   // ---- per head: dV += P'^T dO, then dP' = dO V^T over P'
   for (int h = 0; h < HPG; ++h) {
     __syncthreads();
-    for (int idx = tid; idx < (D / 8) * SPR; idx += NT) {
-      const int j = idx % SPR, ch = idx / SPR, s = k_lo + j;
-      if (j >= span || s < 0 || s >= T) continue;
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int i = 0; i < BM; ++i) {
-        const float pv = Db[(h * BM + i) * SP + j];
-        float o[8];
-        ld8<E>(dOs + (h * BM + i) * DP + ch * 8, o);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = fmaf(pv, o[e], acc[e]);
-      }
-      float *dst = p.dv + row(s, h) + ch * 8;
-      red_add_v4(dst, acc[0], acc[1], acc[2], acc[3]);
-      red_add_v4(dst + 4, acc[4], acc[5], acc[6], acc[7]);
-    }
+    kv_grad(Db, dOs, p.dv, h, 1.f);
     stage(vg, h);
     __syncthreads();
     rows_x_kv(dOs, Db, h, 1.f);
@@ -360,57 +428,38 @@ __global__ void __launch_bounds__(NT, 1) dc_bwd_kernel(const BwdParams p, const 
   for (int h = 0; h < HPG; ++h) {
     __syncthreads();
     stage(kg, h);
-    for (int idx = tid; idx < BM * D; idx += NT) dqa[idx] = 0.f;
     __syncthreads();
+    // dQ_h[i][d] = scale * sum_j dL[(h, i)][j] K[j][d]: M = queries, N = d, K = keys
     {
-      // dQ tasks (query i, 8 d's, key part): the key range is split so that
-      // every thread has work; partial sums meet in shared memory
-      const int ntask = BM * (D / 8);
-      const int parts = max(1, NT / ntask);
-      const int per = (span + parts - 1) / parts;
-      for (int idx = tid; idx < ntask * parts; idx += NT) {
-        const int ch = idx % (D / 8), i = (idx / (D / 8)) % BM, part = idx / ntask;
-        const int j0 = part * per, j1 = min(span, j0 + per);
-        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-        const float *dl = Lb + (h * BM + i) * SP;
-        for (int j = j0; j < j1; ++j) {
-          float kv[8];
-          ld8<E>(KVs + j * DP + ch * 8, kv);
-          const float x = dl[j];
+      const int nmt = (BM + 15) / 16, nks = (span + 15) / 16;
+      const int g8 = lane >> 2, t4 = lane & 3;
+      E *dq = reinterpret_cast<E *>(p.dq);
+      for (int tile = warp; tile < nmt * (D / 8); tile += NT / 32) {
+        const int mt = tile % nmt, nt = tile / nmt;
+        float c[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int ks = 0; ks < nks; ++ks) {
+          uint32_t af[4], bf[2];
 #pragma unroll
-          for (int e = 0; e < 8; ++e) acc[e] = fmaf(x, kv[e], acc[e]);
+          for (int r = 0; r < 4; ++r) {
+            const int i = mt * 16 + g8 + (r & 1) * 8, j = ks * 16 + 2 * t4 + (r >> 1) * 8;
+            const float* lr = Lb + (h * BM + i) * SP;
+            const float x0 = (i < BM && j < span) ? lr[j] : 0.f;
+            const float x1 = (i < BM && j + 1 < span) ? lr[j + 1] : 0.f;
+            af[r] = pack2<E>(x0, x1);
+          }
+          ldsm_x2_t(bf, KVs + (ks * 16 + (lane & 15)) * DP + nt * 8);
+          mma16816<E>(c, af, bf);
         }
 #pragma unroll
-        for (int e = 0; e < 8; ++e) atomicAdd(dqa + i * D + ch * 8 + e, acc[e]);
+        for (int half = 0; half < 2; ++half) {
+          const int i = mt * 16 + g8 + half * 8, t = q0 + i;
+          if (i < BM && t < T)
+            *reinterpret_cast<uint32_t *>(dq + row(t, h) + nt * 8 + 2 * t4) =
+                pack2<E>(p.scale * c[2 * half], p.scale * c[2 * half + 1]);
+        }
       }
     }
-    for (int idx = tid; idx < (D / 8) * SPR; idx += NT) {
-      const int j = idx % SPR, ch = idx / SPR, s = k_lo + j;
-      if (j >= span || s < 0 || s >= T) continue;
-      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      for (int i = 0; i < BM; ++i) {
-        const float x = Lb[(h * BM + i) * SP + j];
-        float qv[8];
-        ld8<E>(Qs + (h * BM + i) * DP + ch * 8, qv);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = fmaf(x, qv[e], acc[e]);
-      }
-      float *dst = p.dk + row(s, h) + ch * 8;
-      const float f = p.scale;
-      red_add_v4(dst, f * acc[0], f * acc[1], f * acc[2], f * acc[3]);
-      red_add_v4(dst + 4, f * acc[4], f * acc[5], f * acc[6], f * acc[7]);
-    }
-    __syncthreads();
-    E *dq = reinterpret_cast<E *>(p.dq);
-    for (int idx = tid; idx < BM * (D / 8); idx += NT) {
-      const int i = idx / (D / 8), ch = idx % (D / 8), t = q0 + i;
-      if (t >= T) continue;
-      uint4 u;
-      E *e = reinterpret_cast<E *>(&u);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) e[k] = from_f<E>(p.scale * dqa[i * D + ch * 8 + k]);
-      *reinterpret_cast<uint4 *>(dq + row(t, h) + ch * 8) = u;
-    }
+    kv_grad(Lb, Qs, p.dk, h, p.scale);
   }
 }
 
