@@ -434,7 +434,7 @@ def backward_layer(local, steps=3, warmup=2):
     del q, k, v, pre, post, dout
     torch.cuda.empty_cache()
     return {"workload": "config1", "G": G, "window": W, "R": R, "ms_per_call": ms,
-            "tflops": fl / (ms * 1e-3) / 1e12, "kernel": "dc_bwd_kernel (CUDA cores, fp32)",
+            "tflops": fl / (ms * 1e-3) / 1e12, "kernel": "dc_bwd_kernel (mma.sync tensor-core products, fp32 composition)",
             "timing": f"CUDA events, {warmup} warm-up + {steps} calls"}
 
 

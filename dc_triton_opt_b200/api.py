@@ -185,6 +185,34 @@ def dc_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     return out
 
 
+def dc_attn_fwd_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seqlens,
+                       pre: Optional[DCTerms] = None, post: Optional[DCTerms] = None,
+                       scaling: Optional[float] = None, window: Optional[int] = None, G: int = 1,
+                       out: Optional[torch.Tensor] = None, kernel: str = "auto") -> torch.Tensor:
+    """Forward over a packed batch of variable-length sequences.
+
+    q, k, v are [total, H, D] (the sequences back to back); per-token weights
+    are packed the same way ([total, H, R], [total, R, H], [total, H],
+    [total, H, HPG]).  Sequence i is tokens [cu_seqlens[i], cu_seqlens[i+1]);
+    attention never crosses a sequence boundary.  ``cu_seqlens`` is read on the
+    host (a CUDA tensor is copied, which synchronises).  Returns [total, H, D]."""
+    _check(q.dim() == 3, f"q must be [total, H, D] (got {list(q.shape)})")
+    cu = torch.as_tensor(cu_seqlens).to("cpu", torch.int32).contiguous()
+    _check(cu.dim() == 1 and cu.numel() >= 2, "cu_seqlens must be a 1-D list of nseq + 1 offsets")
+    unsq = lambda t: None if t is None else t.unsqueeze(0)
+    lift = lambda tm: None if tm is None else DCTerms(
+        identity=tm.identity, w=tm.w, **{f: unsq(getattr(tm, f)) for f in _PER_TOKEN})
+    q4, k4, v4 = q.unsqueeze(0), k.unsqueeze(0), v.unsqueeze(0)
+    o4 = None if out is None else out.unsqueeze(0)
+    p, o4, keep = _params(q4, k4, v4, lift(pre), lift(post), scaling, window, G, None, o4, kernel)
+    lib = _lib.load()
+    with torch.cuda.device(q.device):
+        stream = torch.cuda.current_stream(q.device).cuda_stream
+        _lib.check(lib.dc_attn_fwd_varlen(ctypes.byref(p), cu.data_ptr(), cu.numel() - 1, ctypes.c_void_p(stream)),
+                   "dc_attn_fwd_varlen")
+    return o4[0]
+
+
 _SIMT_WARNED = set()
 
 

@@ -179,6 +179,47 @@ int dc_attn_fwd(const dc_attn_params *pp, void *stream) {
 
 int dc_attn_last_kernel(void) { return g_last_kernel; }
 
+int dc_attn_fwd_varlen(const dc_attn_params *pp, const int32_t *cu, int32_t nseq, void *stream) {
+  int rc = validate(pp);
+  if (rc != DC_OK) return rc;
+  const dc_attn_params &p = *pp;
+  if (!cu) return fail(DC_ERR_NULL, "cu_seqlens is NULL");
+  if (p.B != 1) return fail(DC_ERR_SHAPE, "varlen: B must be 1 (sequences packed along T), got %d", p.B);
+  if (p.seq_lens) return fail(DC_ERR_SHAPE, "varlen: seq_lens must be NULL (the lengths come from cu_seqlens)");
+  if (nseq < 1) return fail(DC_ERR_SHAPE, "varlen: nseq=%d must be >= 1", nseq);
+  if (cu[0] != 0 || cu[nseq] != p.T) return fail(DC_ERR_SHAPE, "varlen: cu_seqlens must start at 0 and end at T=%d", p.T);
+  for (int i = 0; i < nseq; ++i)
+    if (cu[i + 1] < cu[i]) return fail(DC_ERR_SHAPE, "varlen: cu_seqlens must be non-decreasing (index %d)", i);
+  const int64_t es = 2, H = p.H, HPG = p.H / p.G, R = p.R;
+  auto off = [](const void *base, int64_t bytes) -> const void * {
+    return base ? static_cast<const char *>(base) + bytes : nullptr;
+  };
+  auto shift = [&](dc_terms &t, int64_t tok) {
+    t.qw1 = off(t.qw1, tok * H * R * es); t.qw2 = off(t.qw2, tok * R * H * es);
+    t.kw1 = off(t.kw1, tok * H * R * es); t.kw2 = off(t.kw2, tok * R * H * es);
+    t.qdd = off(t.qdd, tok * H * es); t.kdd = off(t.kdd, tok * H * es);
+    t.qmat = off(t.qmat, tok * H * HPG * es);
+  };
+  for (int i = 0; i < nseq;) {
+    const int len = cu[i + 1] - cu[i];
+    int j = i + 1;  // a run of sequences of this length: one batch with stride len tokens
+    while (j < nseq && cu[j + 1] - cu[j] == len) ++j;
+    if (len > 0) {
+      dc_attn_params q = p;
+      const int64_t tok = cu[i];
+      q.B = j - i; q.T = len;
+      q.q = off(p.q, tok * H * p.D * es); q.k = off(p.k, tok * H * p.D * es); q.v = off(p.v, tok * H * p.D * es);
+      q.out = static_cast<char *>(p.out) + tok * p.out_st * es;
+      q.out_sb = (int64_t)len * p.out_st;
+      shift(q.pre, tok);
+      shift(q.post, tok);
+      if ((rc = dc_attn_fwd(&q, stream)) != DC_OK) return rc;
+    }
+    i = j;
+  }
+  return DC_OK;
+}
+
 int dc_attn_bwd_params_size(void) { return (int)sizeof(dc_attn_bwd_params); }
 
 int dc_attn_bwd(const dc_attn_bwd_params *bp, void *stream) {

@@ -148,6 +148,18 @@ DC_API int dc_attn_fwd_residual(const void *q, const void *k, const void *v,
                          int32_t D, int32_t G, float scaling, int32_t window,
                          int32_t chunk_size, int32_t dtype, void *stream);
 
+/* Packed variable-length batch: p->B must be 1 and p->T the total token count;
+ * q, k, v, out and every per-token weight hold the sequences back to back,
+ * sequence i being tokens [cu_seqlens[i], cu_seqlens[i+1]) (host array of
+ * nseq + 1 non-decreasing values, cu_seqlens[0] = 0, cu_seqlens[nseq] = T).
+ * Attention never crosses a sequence boundary.  p->seq_lens must be NULL.
+ * Runs of consecutive sequences of equal length are launched together as one
+ * batch; each run is one dc_attn_fwd launch on `stream`.  The reference
+ * masks keys by seq_lens only (triton_dc_onekernel_v4_h100.py:661-664); this
+ * packed layout has no counterpart there.  Returns DC_OK or a DC_ERR_* code
+ * (the first failing run's). */
+DC_API int dc_attn_fwd_varlen(const dc_attn_params *p, const int32_t *cu_seqlens, int32_t nseq, void *stream);
+
 /* Gradients of one composition term set, fp32, caller-owned; a NULL pointer
  * means the gradient is not wanted.  Shapes as in dc_terms.  The per-token
  * gradients are written; w is a sum over every (b, t) and is zeroed by the

@@ -90,3 +90,19 @@ def test_residual_entry_null_weights():
                                   ctypes.c_float(0.1), 4, 16, 0, None)
     assert rc == -1
     assert "six DC weights" in lib.dc_attn_last_error().decode()
+
+
+@pytest.mark.parametrize("cu,B,needle", [
+    ([0, 10, 20], 2, "B must be 1"),
+    ([1, 10, 64], 1, "start at 0"),
+    ([0, 40, 30, 64], 1, "non-decreasing"),
+    ([0, 10, 63], 1, "end at T"),
+])
+def test_varlen_validation_needs_no_device(cu, B, needle):
+    """dc_attn_fwd_varlen checks its packed-batch description before any launch."""
+    lib = _lib.load()
+    p = _params(B=B)
+    arr = (ctypes.c_int32 * len(cu))(*cu)
+    rc = lib.dc_attn_fwd_varlen(ctypes.byref(p), arr, len(cu) - 1, None)
+    assert rc == -2  # DC_ERR_SHAPE
+    assert needle in lib.dc_attn_last_error().decode()
