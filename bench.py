@@ -322,7 +322,7 @@ def run_ours(args, cfg, world, rank, local):
         by = 4 * B * T * H * D * 2 + 2 * B * T * H * (H // G) * 2
     achieved = by / (ms_step * 1e-3) / 1e9
     tflops_rank = fl_rank / (ms_step * 1e-3) / 1e12
-    strong = best = others = bwd = None
+    strong = best = others = bwd = prj = None
     if not args.no_extra:
         del qh, kh, vh, host_sets, out_host
         strong = strong_scaling_config4(world, rank, local)
@@ -330,6 +330,7 @@ def run_ours(args, cfg, world, rank, local):
             best = repo_best(local)
             others = other_layers(local)
             bwd = backward_layer(local)
+            prj = projection_layer(local)
     if rank != 0:
         return
     cpu = None
@@ -360,6 +361,7 @@ def run_ours(args, cfg, world, rank, local):
         line["repo_best"] = best
         line["other_layers"] = others
         line["backward"] = bwd
+        line["projection"] = prj
     print(json.dumps(line), flush=True)
 
 
@@ -436,6 +438,30 @@ def backward_layer(local, steps=3, warmup=2):
     return {"workload": "config1", "G": G, "window": W, "R": R, "ms_per_call": ms,
             "tflops": fl / (ms * 1e-3) / 1e12, "kernel": "dc_bwd_kernel (mma.sync tensor-core products, fp32 composition)",
             "timing": f"CUDA events, {warmup} warm-up + {steps} calls"}
+
+
+def projection_layer(local, steps=5, warmup=3):
+    """The composition-weight producer (dc_proj_weights) for the headline
+    layer's tokens: M = B*T = 65536, hidden size Dm = H*D = 4096, MLP width
+    I = 128, H = 32, R = 1.  FLOPs: 2 M Dm I + 2 M Dm 4H + 2 M I 8HR."""
+    import dc_triton_opt_b200 as dc
+    device = torch.device("cuda", local)
+    M, Dm, I, H, R = 16 * 4096, 4096, 128, 32, 1
+    g = torch.Generator(device=device).manual_seed(11)
+    rn = lambda *sh, std: (std * torch.randn(*sh, generator=g, device=device)).to(torch.bfloat16)
+    x = rn(M, Dm, std=1.0)
+    w1, w2, wdd = rn(Dm, I, std=Dm ** -0.5), rn(I, 8 * H * R, std=0.01), rn(Dm, 4 * H, std=0.01)
+    hidden = torch.empty(M, I, device=device, dtype=torch.bfloat16)
+    call = lambda: dc.dc_proj_weights(x, w1, w2, wdd, H, R, hidden=hidden)
+    ms = time_calls(call, steps, warmup, torch.cuda.current_stream(device), 1)
+    fl = 2 * M * Dm * I + 2 * M * Dm * 4 * H + 2 * M * I * 8 * H * R
+    by = 2 * M * Dm * 2 + 2 * M * I * 2 + M * (8 * H * R + 4 * H) * 2
+    hbm, tc_peak, _ = peaks()
+    del x, hidden
+    torch.cuda.empty_cache()
+    return {"M": M, "Dm": Dm, "I": I, "H": H, "R": R, "ms_per_call": ms, "tflops": fl / (ms * 1e-3) / 1e12,
+            "tensor_frac": fl / (ms * 1e-3) / 1e12 / tc_peak, "hbm_gbs": by / (ms * 1e-3) / 1e9,
+            "kernel": "dc_proj_gemm (mma.sync), 3 launches", "timing": f"CUDA events, {warmup} warm-up + {steps} calls"}
 
 
 def strong_scaling_config4(world, rank, local, steps=5, warmup=3):

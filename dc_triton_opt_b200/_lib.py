@@ -25,7 +25,7 @@ DEV_ERRORS = {0: "DC_DEV_OK", 1: "DC_DEV_ERR_TIMEOUT_Q", 2: "DC_DEV_ERR_TIMEOUT_
               6: "DC_DEV_ERR_TIMEOUT_O"}
 EXPORTS = ("dc_attn_fwd", "dc_attn_fwd_residual", "dc_attn_select_kernel", "dc_attn_read_error",
            "dc_attn_last_kernel", "dc_attn_last_error", "dc_attn_abi_version", "dc_attn_params_size",
-           "dc_attn_bwd", "dc_attn_bwd_params_size", "dc_attn_fwd_varlen")
+           "dc_attn_bwd", "dc_attn_bwd_params_size", "dc_attn_fwd_varlen", "dc_proj_weights")
 
 
 class DcTerms(ctypes.Structure):
@@ -57,6 +57,13 @@ class DcAttnBwdParams(ctypes.Structure):
     _fields_ = [("fwd", DcAttnParams), ("dout", ctypes.c_void_p), ("dq", ctypes.c_void_p),
                 ("dk", ctypes.c_void_p), ("dv", ctypes.c_void_p), ("dpre", DcTermGrads),
                 ("dpost", DcTermGrads)]
+
+
+class DcProjParams(ctypes.Structure):
+    _fields_ = [("M", ctypes.c_int32), ("Dm", ctypes.c_int32), ("I", ctypes.c_int32), ("H", ctypes.c_int32),
+                ("R", ctypes.c_int32), ("dtype", ctypes.c_int32), ("x", ctypes.c_void_p), ("w1", ctypes.c_void_p),
+                ("w2", ctypes.c_void_p), ("wdd", ctypes.c_void_p), ("hidden", ctypes.c_void_p),
+                ("dw", ctypes.c_void_p * 8), ("dd", ctypes.c_void_p * 4)]
 
 
 _lib = None
@@ -93,6 +100,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.dc_attn_fwd_varlen.argtypes = [ctypes.POINTER(DcAttnParams), ctypes.c_void_p, ctypes.c_int32,
                                            ctypes.c_void_p]
         lib.dc_attn_fwd_varlen.restype = ctypes.c_int
+        lib.dc_proj_weights.argtypes = [ctypes.POINTER(DcProjParams), ctypes.c_void_p]
+        lib.dc_proj_weights.restype = ctypes.c_int
         lib.dc_attn_bwd.argtypes = [ctypes.POINTER(DcAttnBwdParams), ctypes.c_void_p]
         lib.dc_attn_bwd.restype = ctypes.c_int
         lib.dc_attn_bwd_params_size.restype = ctypes.c_int

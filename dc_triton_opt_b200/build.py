@@ -18,7 +18,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libdcattn.so")
-SOURCES = ["capi.cu", "simt_kernel.cu", "tc_kernel.cu", "tcs_kernel.cu", "tcm_kernel.cu", "bwd_kernel.cu"]
+SOURCES = ["capi.cu", "simt_kernel.cu", "tc_kernel.cu", "tcs_kernel.cu", "tcm_kernel.cu", "bwd_kernel.cu", "proj_kernel.cu"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 

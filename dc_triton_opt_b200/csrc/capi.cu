@@ -24,6 +24,7 @@ bool tcm_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tcm(const dc_attn_params &p, cudaStream_t st);
 bool bwd_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_bwd(const dc_attn_bwd_params &p, cudaStream_t st, std::string *why);
+cudaError_t launch_proj(const dc_proj_params &q, void *hidden, cudaStream_t st);
 }  // namespace dcattn
 
 // The library's own device error word, used when a caller passes no
@@ -178,6 +179,35 @@ int dc_attn_fwd(const dc_attn_params *pp, void *stream) {
 }
 
 int dc_attn_last_kernel(void) { return g_last_kernel; }
+
+static int check_proj(const dc_proj_params *q) {
+  if (!q) return fail(DC_ERR_NULL, "params is NULL");
+  if (!q->x || !q->w1 || !q->w2 || !q->wdd) return fail(DC_ERR_NULL, "x, w1, w2 and wdd must be non-NULL");
+  for (int i = 0; i < 8; ++i)
+    if (!q->dw[i]) return fail(DC_ERR_NULL, "dw[%d] is NULL", i);
+  for (int i = 0; i < 4; ++i)
+    if (!q->dd[i]) return fail(DC_ERR_NULL, "dd[%d] is NULL", i);
+  if (q->dtype != DC_DTYPE_BF16 && q->dtype != DC_DTYPE_FP16) return fail(DC_ERR_DTYPE, "dtype must be bf16 or fp16");
+  if (q->M < 1 || q->H < 2 || q->H % 2 || q->R < 1 || q->R > 8)
+    return fail(DC_ERR_SHAPE, "need M >= 1, even H >= 2, 1 <= R <= 8 (M=%d H=%d R=%d)", q->M, q->H, q->R);
+  if (q->Dm < 32 || q->Dm % 32 || q->I < 32 || q->I % 32)
+    return fail(DC_ERR_SHAPE, "Dm=%d and I=%d must be positive multiples of 32", q->Dm, q->I);
+  for (const void *ptr : {q->x, q->w1, q->w2, q->wdd})
+    if (reinterpret_cast<uintptr_t>(ptr) & 15u) return fail(DC_ERR_ALIGN, "x, w1, w2, wdd must be 16-byte aligned");
+  return DC_OK;
+}
+
+int dc_proj_weights(const dc_proj_params *q, void *stream) {
+  int rc = check_proj(q);
+  if (rc != DC_OK) return rc;
+  if (!q->hidden) return fail(DC_ERR_NULL, "hidden workspace is NULL");
+  if (reinterpret_cast<uintptr_t>(q->hidden) & 15u) return fail(DC_ERR_ALIGN, "hidden must be 16-byte aligned");
+  if ((rc = check_device()) != DC_OK) return rc;
+  cudaError_t e = dcattn::launch_proj(*q, q->hidden, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(DC_ERR_LAUNCH, "projection launch failed: %s", cudaGetErrorString(e));
+  g_last_error.clear();
+  return DC_OK;
+}
 
 int dc_attn_fwd_varlen(const dc_attn_params *pp, const int32_t *cu, int32_t nseq, void *stream) {
   int rc = validate(pp);

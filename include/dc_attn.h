@@ -160,6 +160,30 @@ DC_API int dc_attn_fwd_residual(const void *q, const void *k, const void *v,
  * (the first failing run's). */
 DC_API int dc_attn_fwd_varlen(const dc_attn_params *p, const int32_t *cu_seqlens, int32_t nseq, void *stream);
 
+/* Producer of the per-token composition weights from the hidden states x
+ * (DCFormer's dynamic weight projection; the reference has no code for this
+ * step, its weights arrive precomputed):
+ *   hidden = gelu(x W1), [M, I];   dw = hidden W2;   dd = tanh(x Wdd).
+ * All matrices row-major in `dtype`; M = tokens (B*T), Dm and I multiples of
+ * 32, H even.  Outputs (dtype, caller-owned, contiguous):
+ *   dw[0..3] = pre qw1 [M,H,R], pre qw2 [M,R,H], pre kw1 [M,H,R], pre kw2 [M,R,H],
+ *   dw[4..7] = the same for the post set    (W2 is [I, 8*H*R] in that order);
+ *   dd[0..3] = pre qdd, pre kdd, post qdd, post kdd, [M,H] each
+ *                                           (Wdd is [Dm, 4*H] in that order).
+ * `hidden` is a caller-owned workspace of M*I elements. */
+typedef struct dc_proj_params {
+  int32_t M, Dm, I, H, R, dtype;
+  const void *x;    /* [M, Dm]       */
+  const void *w1;   /* [Dm, I]       */
+  const void *w2;   /* [I, 8*H*R]    */
+  const void *wdd;  /* [Dm, 4*H]     */
+  void *hidden;     /* [M, I] workspace */
+  void *dw[8];
+  void *dd[4];
+} dc_proj_params;
+
+DC_API int dc_proj_weights(const dc_proj_params *p, void *stream);
+
 /* Gradients of one composition term set, fp32, caller-owned; a NULL pointer
  * means the gradient is not wanted.  Shapes as in dc_terms.  The per-token
  * gradients are written; w is a sum over every (b, t) and is zeroed by the

@@ -211,3 +211,31 @@ def pairs(T: int, window: Optional[int]) -> int:
     if window is None or window >= T:
         return T * (T + 1) // 2
     return T * window - window * (window - 1) // 2
+
+
+def project_weights(x, w1, w2, wdd, H: int, R: int):
+    """Composition-weight producer (TEST INFRASTRUCTURE; parity unpinned: the
+    reference project has no code for this step).  Restates the DCFormer
+    dynamic weight projection (Xiao et al., ICML 2024) as built here:
+    hidden = gelu(x W1) (erf form), dw = hidden W2, dd = tanh(x Wdd), with the
+    column order of include/dc_attn.h (dc_proj_params).  x [..., Dm]; returns
+    (pre, post) Terms with qw1/kw1 [..., H, R], qw2/kw2 [..., R, H], qdd/kdd
+    [..., H], plus the float64 hidden activations."""
+    from math import erf, sqrt
+    x = _f(x)
+    h = x @ _f(w1)
+    verf = np.vectorize(erf)
+    hidden = 0.5 * h * (1.0 + verf(h / sqrt(2.0)))
+    dw = hidden @ _f(w2)
+    dd = np.tanh(x @ _f(wdd))
+    lead = x.shape[:-1]
+    HR = H * R
+    sets = []
+    for s in range(2):
+        c = dw[..., s * 4 * HR:(s + 1) * 4 * HR]
+        t = Terms(identity=True,
+                  qw1=c[..., 0:HR].reshape(*lead, H, R), qw2=c[..., HR:2 * HR].reshape(*lead, R, H),
+                  kw1=c[..., 2 * HR:3 * HR].reshape(*lead, H, R), kw2=c[..., 3 * HR:4 * HR].reshape(*lead, R, H),
+                  qdd=dd[..., (2 * s) * H:(2 * s + 1) * H], kdd=dd[..., (2 * s + 1) * H:(2 * s + 2) * H])
+        sets.append(t)
+    return sets[0], sets[1], hidden
