@@ -25,7 +25,7 @@ DEV_ERRORS = {0: "DC_DEV_OK", 1: "DC_DEV_ERR_TIMEOUT_Q", 2: "DC_DEV_ERR_TIMEOUT_
               6: "DC_DEV_ERR_TIMEOUT_O"}
 EXPORTS = ("dc_attn_fwd", "dc_attn_fwd_residual", "dc_attn_select_kernel", "dc_attn_read_error",
            "dc_attn_last_kernel", "dc_attn_last_error", "dc_attn_abi_version", "dc_attn_params_size",
-           "dc_attn_bwd", "dc_attn_bwd_params_size", "dc_attn_fwd_varlen", "dc_proj_weights")
+           "dc_attn_bwd", "dc_attn_bwd_params_size", "dc_attn_fwd_varlen", "dc_proj_weights", "dc_proj_weights_noalloc")
 
 
 class DcTerms(ctypes.Structure):
@@ -102,6 +102,8 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.dc_attn_fwd_varlen.restype = ctypes.c_int
         lib.dc_proj_weights.argtypes = [ctypes.POINTER(DcProjParams), ctypes.c_void_p]
         lib.dc_proj_weights.restype = ctypes.c_int
+        lib.dc_proj_weights_noalloc.argtypes = [ctypes.POINTER(DcProjParams), ctypes.c_void_p]
+        lib.dc_proj_weights_noalloc.restype = ctypes.c_int
         lib.dc_attn_bwd.argtypes = [ctypes.POINTER(DcAttnBwdParams), ctypes.c_void_p]
         lib.dc_attn_bwd.restype = ctypes.c_int
         lib.dc_attn_bwd_params_size.restype = ctypes.c_int

@@ -197,6 +197,47 @@ static int check_proj(const dc_proj_params *q) {
   return DC_OK;
 }
 
+// Fixed device workspace of dc_proj_weights_noalloc (the `hidden`
+// activations, 16-bit elements).  In host code this name is only a stand-in:
+// the device address comes from cudaGetSymbolAddress, per device.
+static __device__ __align__(256) uint16_t g_proj_hidden[DC_PROJ_NOALLOC_MAX_HIDDEN];
+
+// Device address of g_proj_hidden on the current device, looked up on the
+// first call per device; nullptr (and the error text set) if that fails.
+static void *proj_hidden_addr() {
+  static void *addr[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    fail(DC_ERR_DEVICE, "cannot query the current device");
+    return nullptr;
+  }
+  if (!addr[dev]) {
+    void *p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_proj_hidden);
+    if (e != cudaSuccess || !p) {
+      fail(DC_ERR_DEVICE, "cudaGetSymbolAddress of the projection workspace failed: %s", cudaGetErrorString(e));
+      return nullptr;
+    }
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+int dc_proj_weights_noalloc(const dc_proj_params *q, void *stream) {
+  int rc = check_proj(q);
+  if (rc != DC_OK) return rc;
+  if ((int64_t)q->M * q->I > DC_PROJ_NOALLOC_MAX_HIDDEN)
+    return fail(DC_ERR_SHAPE, "dc_proj_weights_noalloc: M*I=%lld exceeds the fixed workspace of %d elements",
+                (long long)q->M * q->I, DC_PROJ_NOALLOC_MAX_HIDDEN);
+  if ((rc = check_device()) != DC_OK) return rc;
+  void *hidden = proj_hidden_addr();
+  if (!hidden) return DC_ERR_DEVICE;
+  cudaError_t e = dcattn::launch_proj(*q, hidden, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(DC_ERR_LAUNCH, "projection launch failed: %s", cudaGetErrorString(e));
+  g_last_error.clear();
+  return DC_OK;
+}
+
 int dc_proj_weights(const dc_proj_params *q, void *stream) {
   int rc = check_proj(q);
   if (rc != DC_OK) return rc;

@@ -184,6 +184,29 @@ typedef struct dc_proj_params {
 
 DC_API int dc_proj_weights(const dc_proj_params *p, void *stream);
 
+/* Largest M * I (tokens x MLP width) that dc_proj_weights_noalloc accepts:
+ * its `hidden` activations live in a fixed 8 MiB device array. */
+#define DC_PROJ_NOALLOC_MAX_HIDDEN (4 * 1024 * 1024)
+
+/* dc_proj_weights for callers that cannot allocate device memory: code that
+ * runs where cudaMalloc is unavailable or forbidden (inside a custom
+ * allocator's own callbacks, under a framework that owns every byte of the
+ * device through a memory pool, or in a tightly budgeted inference server
+ * that admits no allocation after start-up) still has to produce the
+ * weights.  The caller passes inputs and outputs as usual; p->hidden is
+ * ignored.  The intermediate activations go to a library-owned
+ * `static __device__` array of DC_PROJ_NOALLOC_MAX_HIDDEN elements, which every
+ * GPU that loads this library holds until the process exits.  Calls with
+ * M * I above that limit return DC_ERR_SHAPE.  The first call on a device
+ * looks the array's device address up (cudaGetSymbolAddress) with that device
+ * current; make that first call before any stream capture.  All calls share
+ * the one array: calls that may run at the same time on the GPU (different
+ * streams without ordering) race on it.  Nothing in the array needs to start
+ * at zero (every element a call reads it has written first).  No cudaMalloc,
+ * cudaFree or allocating library routine is called.  No counterpart in the
+ * reference. */
+DC_API int dc_proj_weights_noalloc(const dc_proj_params *p, void *stream);
+
 /* Gradients of one composition term set, fp32, caller-owned; a NULL pointer
  * means the gradient is not wanted.  Shapes as in dc_terms.  The per-token
  * gradients are written; w is a sum over every (b, t) and is zeroed by the
