@@ -461,7 +461,7 @@ def projection_layer(local, steps=5, warmup=3):
     torch.cuda.empty_cache()
     return {"M": M, "Dm": Dm, "I": I, "H": H, "R": R, "ms_per_call": ms, "tflops": fl / (ms * 1e-3) / 1e12,
             "tensor_frac": fl / (ms * 1e-3) / 1e12 / tc_peak, "hbm_gbs": by / (ms * 1e-3) / 1e9,
-            "kernel": "dc_proj_gemm (mma.sync), 3 launches", "timing": f"CUDA events, {warmup} warm-up + {steps} calls"}
+            "kernel": "dc_proj_gemm (mma.sync), 3 launches (x W1, x Wdd, hidden W2)", "timing": f"CUDA events, {warmup} warm-up + {steps} calls"}
 
 
 def strong_scaling_config4(world, rank, local, steps=5, warmup=3):
