@@ -440,13 +440,13 @@ def backward_layer(local, steps=3, warmup=2):
             "timing": f"CUDA events, {warmup} warm-up + {steps} calls"}
 
 
-def projection_layer(local, steps=5, warmup=3):
+def projection_layer(local, steps=5, warmup=3, M=16 * 4096):
     """The composition-weight producer (dc_proj_weights) for the headline
     layer's tokens: M = B*T = 65536, hidden size Dm = H*D = 4096, MLP width
     I = 128, H = 32, R = 1.  FLOPs: 2 M Dm I + 2 M Dm 4H + 2 M I 8HR."""
     import dc_triton_opt_b200 as dc
     device = torch.device("cuda", local)
-    M, Dm, I, H, R = 16 * 4096, 4096, 128, 32, 1
+    Dm, I, H, R = 4096, 128, 32, 1
     g = torch.Generator(device=device).manual_seed(11)
     rn = lambda *sh, std: (std * torch.randn(*sh, generator=g, device=device)).to(torch.bfloat16)
     x = rn(M, Dm, std=1.0)
@@ -578,7 +578,18 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the config-4 strong-scaling, repo-best and other-layer blocks")
+    ap.add_argument("--op", default=None, choices=["backward", "projection"],
+                    help="run only this op a few times at a reduced size (B=2 / 8192 tokens), "
+                         "for profiling; prints its ms per call")
     args = ap.parse_args()
+    if args.op is not None:
+        torch.cuda.set_device(0)
+        if args.op == "backward":
+            WORKLOADS["config1"] = dict(WORKLOADS["config1"], B=2)
+            print(json.dumps(backward_layer(0, steps=args.steps, warmup=args.warmup)))
+        else:
+            print(json.dumps(projection_layer(0, steps=args.steps, warmup=args.warmup, M=8192)))
+        return
     cfg = dict(WORKLOADS[args.workload])
     for k in ("G", "window", "B", "T"):
         if getattr(args, k) is not None:

@@ -62,7 +62,9 @@ __host__ __device__ inline Geo make_geo(int BM, int W, int esize) {
   g.NC = BM * HPG;
   g.span = BM + W - 1;
   g.SPR = rup(g.span, 32);
-  g.SP = g.SPR + 1;  // odd row length: column-wise (fixed key, varying row) accesses are conflict-free
+  // row length = 4 mod 32: the tensor-core fragment accesses (lanes g = 0..7
+  // along keys, t = 0..3 along rows two apart) fall on 32 distinct banks
+  g.SP = g.SPR + 4;
   int o = 0;
   g.l_off = o; o += g.NC * g.SP * 4;                     // L, then dL
   g.p_off = o; o += g.NC * g.SP * 4;                     // S, then P
