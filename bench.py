@@ -322,7 +322,7 @@ def run_ours(args, cfg, world, rank, local):
         by = 4 * B * T * H * D * 2 + 2 * B * T * H * (H // G) * 2
     achieved = by / (ms_step * 1e-3) / 1e9
     tflops_rank = fl_rank / (ms_step * 1e-3) / 1e12
-    strong = best = others = bwd = prj = None
+    strong = best = others = bwd = prj = f8 = None
     if not args.no_extra:
         del qh, kh, vh, host_sets, out_host
         strong = strong_scaling_config4(world, rank, local)
@@ -331,6 +331,7 @@ def run_ours(args, cfg, world, rank, local):
             others = other_layers(local)
             bwd = backward_layer(local)
             prj = projection_layer(local)
+            f8 = fp8_layer(local)
     if rank != 0:
         return
     cpu = None
@@ -362,6 +363,7 @@ def run_ours(args, cfg, world, rank, local):
         line["other_layers"] = others
         line["backward"] = bwd
         line["projection"] = prj
+        line["fp8"] = f8
     print(json.dumps(line), flush=True)
 
 
@@ -462,6 +464,33 @@ def projection_layer(local, steps=5, warmup=3, M=16 * 4096):
     return {"M": M, "Dm": Dm, "I": I, "H": H, "R": R, "ms_per_call": ms, "tflops": fl / (ms * 1e-3) / 1e12,
             "tensor_frac": fl / (ms * 1e-3) / 1e12 / tc_peak, "hbm_gbs": by / (ms * 1e-3) / 1e9,
             "kernel": "dc_proj_gemm (mma.sync), 3 launches (x W1, x Wdd, hidden W2)", "timing": f"CUDA events, {warmup} warm-up + {steps} calls"}
+
+
+def fp8_layer(local, steps=5, warmup=3):
+    """The headline layer (config1 G8 W128, every term) with q and k in e4m3
+    (per-tensor scales, QK^T in fp8 on the tensor cores, one-tile-per-CTA
+    kernel) beside the bf16 forward on the same inputs; error of the fp8 result
+    against the bf16 one as max|d| / max|bf16 out|."""
+    import dc_triton_opt_b200 as dc
+    device = torch.device("cuda", local)
+    cfg = dict(WORKLOADS["config1"])
+    q, k, v, pre, post = make_inputs(cfg, device, seed=21)
+    B, T, H, D, G, R, W = (cfg[x] for x in ("B", "T", "H", "D", "G", "R", "window"))
+    q8, qs = dc.quantize_e4m3(q)
+    k8, ks = dc.quantize_e4m3(k)
+    out8, out16 = torch.empty_like(v), torch.empty_like(v)
+    f8 = lambda: dc.dc_attn_fwd_fp8qk(q8, k8, v, qs, ks, pre, post, D ** -0.5, W, G, out=out8)
+    f16 = lambda: dc.dc_attn_fwd(q, k, v, pre, post, D ** -0.5, W, G, out=out16)
+    stream = torch.cuda.current_stream(device)
+    ms8 = time_calls(f8, steps, warmup, stream, 1)
+    ms16 = time_calls(f16, steps, warmup, stream, 1)
+    err = ((out8.float() - out16.float()).abs().max() / out16.float().abs().max()).item()
+    fl = flops(B, H, D, G, R, pairs(T, W))
+    del q, k, v, pre, post, q8, k8, out8, out16
+    torch.cuda.empty_cache()
+    return {"workload": "config1", "G": G, "window": W, "fp8_qk_ms": ms8, "fp8_qk_tflops": fl / (ms8 * 1e-3) / 1e12,
+            "bf16_ms": ms16, "max_rel_diff_vs_bf16": err, "quantization": "e4m3, per-tensor scales for q and k",
+            "kernel": "dc_tc_kernel (one tile per CTA), QK^T kind::f8f6f4"}
 
 
 def strong_scaling_config4(world, rank, local, steps=5, warmup=3):

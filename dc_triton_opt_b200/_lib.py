@@ -25,7 +25,7 @@ DEV_ERRORS = {0: "DC_DEV_OK", 1: "DC_DEV_ERR_TIMEOUT_Q", 2: "DC_DEV_ERR_TIMEOUT_
               6: "DC_DEV_ERR_TIMEOUT_O"}
 EXPORTS = ("dc_attn_fwd", "dc_attn_fwd_residual", "dc_attn_select_kernel", "dc_attn_read_error",
            "dc_attn_last_kernel", "dc_attn_last_error", "dc_attn_abi_version", "dc_attn_params_size",
-           "dc_attn_bwd", "dc_attn_bwd_params_size", "dc_attn_fwd_varlen", "dc_proj_weights", "dc_proj_weights_noalloc")
+           "dc_attn_bwd", "dc_attn_bwd_params_size", "dc_attn_fwd_varlen", "dc_proj_weights", "dc_proj_weights_noalloc", "dc_attn_fwd_fp8qk")
 
 
 class DcTerms(ctypes.Structure):
@@ -100,6 +100,9 @@ def load(path: str = LIB_PATH) -> ctypes.CDLL:
         lib.dc_attn_fwd_varlen.argtypes = [ctypes.POINTER(DcAttnParams), ctypes.c_void_p, ctypes.c_int32,
                                            ctypes.c_void_p]
         lib.dc_attn_fwd_varlen.restype = ctypes.c_int
+        lib.dc_attn_fwd_fp8qk.argtypes = [ctypes.POINTER(DcAttnParams), ctypes.c_float, ctypes.c_float,
+                                          ctypes.c_void_p]
+        lib.dc_attn_fwd_fp8qk.restype = ctypes.c_int
         lib.dc_proj_weights.argtypes = [ctypes.POINTER(DcProjParams), ctypes.c_void_p]
         lib.dc_proj_weights.restype = ctypes.c_int
         lib.dc_proj_weights_noalloc.argtypes = [ctypes.POINTER(DcProjParams), ctypes.c_void_p]

@@ -213,6 +213,41 @@ def dc_attn_fwd_varlen(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, cu_seq
     return o4[0]
 
 
+E4M3_MAX = 448.0
+
+
+def quantize_e4m3(x: torch.Tensor):
+    """Per-tensor e4m3 quantization for :func:`dc_attn_fwd_fp8qk`:
+    returns (x8, scale) with x ~= x8.float() * scale and |x8| <= 448."""
+    amax = x.detach().abs().amax().float().clamp_min(1e-12)
+    scale = amax / E4M3_MAX
+    return (x.float() / scale).to(torch.float8_e4m3fn), float(scale)
+
+
+def dc_attn_fwd_fp8qk(q8: torch.Tensor, k8: torch.Tensor, v: torch.Tensor, q_scale: float, k_scale: float,
+                      pre: Optional[DCTerms] = None, post: Optional[DCTerms] = None,
+                      scaling: Optional[float] = None, window: int = 128, G: int = 1,
+                      seq_lens: Optional[torch.Tensor] = None, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Forward with q and k in e4m3 (``torch.float8_e4m3fn``, [B,T,H,D]) and
+    per-tensor scales (q ~= q8 * q_scale): QK^T on the tensor cores in fp8,
+    everything else as :func:`dc_attn_fwd` in v's dtype (bf16 / fp16).  Windowed
+    layers with 1-8 heads per group (the single-pass tensor-core kernel)."""
+    _check(q8.dtype == torch.float8_e4m3fn and k8.dtype == torch.float8_e4m3fn,
+           "q8 and k8 must be torch.float8_e4m3fn")
+    _check(q8.shape == v.shape and k8.shape == v.shape, "q8, k8 and v must share one shape")
+    _check(window is not None, "the fp8 path needs a sliding window")
+    p, out, keep = _params(v, v, v, pre, post, scaling, window, G, seq_lens, out, "tc")
+    q8, k8 = q8.contiguous(), k8.contiguous()
+    keep += [q8, k8]
+    p.q, p.k = q8.data_ptr(), k8.data_ptr()
+    lib = _lib.load()
+    with torch.cuda.device(v.device):
+        stream = torch.cuda.current_stream(v.device).cuda_stream
+        _lib.check(lib.dc_attn_fwd_fp8qk(ctypes.byref(p), float(q_scale), float(k_scale), ctypes.c_void_p(stream)),
+                   "dc_attn_fwd_fp8qk")
+    return out
+
+
 _SIMT_WARNED = set()
 
 

@@ -18,6 +18,7 @@ cudaError_t launch_simt(const ParamsDev &p, int dtype, cudaStream_t st);
 size_t simt_smem_bytes(int HPG, int D, int R, int dtype);
 bool tc_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tc(const dc_attn_params &p, cudaStream_t st);
+cudaError_t launch_tc_fp8qk(const dc_attn_params &p, cudaStream_t st);
 bool tcs_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tcs(const dc_attn_params &p, cudaStream_t st);
 bool tcm_supports(const dc_attn_params &p, std::string *why);
@@ -247,6 +248,25 @@ int dc_proj_weights(const dc_proj_params *q, void *stream) {
   cudaError_t e = dcattn::launch_proj(*q, q->hidden, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DC_ERR_LAUNCH, "projection launch failed: %s", cudaGetErrorString(e));
   g_last_error.clear();
+  return DC_OK;
+}
+
+int dc_attn_fwd_fp8qk(const dc_attn_params *pp, float q_scale, float k_scale, void *stream) {
+  int rc = validate(pp);
+  if (rc != DC_OK) return rc;
+  dc_attn_params p = *pp;
+  if (!(q_scale > 0.f) || !(k_scale > 0.f)) return fail(DC_ERR_SHAPE, "fp8: q_scale and k_scale must be positive");
+  p.scale = p.scale * q_scale * k_scale;
+  std::string why;
+  if (!dcattn::tc_supports(p, &why)) return fail(DC_ERR_UNSUPPORTED, "fp8 q/k: %s", why.c_str());
+  if ((rc = check_device()) != DC_OK) return rc;
+  if (!p.err_flag && !(p.err_flag = default_err_word()))
+    return fail(DC_ERR_DEVICE, "cannot resolve the library's device error word");
+  if (p.wait_us == 0) p.wait_us = 2000000u;
+  cudaError_t e = dcattn::launch_tc_fp8qk(p, reinterpret_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return fail(DC_ERR_LAUNCH, "kernel launch failed: %s", cudaGetErrorString(e));
+  g_last_error.clear();
+  g_last_kernel = DC_KERNEL_TC;
   return DC_OK;
 }
 

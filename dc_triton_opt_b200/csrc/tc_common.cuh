@@ -430,6 +430,21 @@ static bool make_map(CUtensorMap *m, const void *base, int dtype, int B, int T, 
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// A [B, T, H, D] tensor of 8-bit floats (e4m3) as a 4-D map whose box is one
+// head's full 128-byte rows (128 d x rows), 128-byte swizzled.
+static bool make_map8(CUtensorMap *m, const void *base, int B, int T, int H, int rows, int64_t sb, int64_t st,
+                      int64_t sh) {
+  EncodeTiledFn enc = get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[4] = {(cuuint64_t)D, (cuuint64_t)H, (cuuint64_t)T, (cuuint64_t)B};
+  const cuuint64_t strides[3] = {(cuuint64_t)sh, (cuuint64_t)st, (cuuint64_t)sb};
+  const cuuint32_t box[4] = {128, 1, (cuuint32_t)rows, 1};
+  const cuuint32_t estr[4] = {1, 1, 1, 1};
+  return enc(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void *>(base), dims, strides, box, estr,
+             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // The same [B, T, H, D] tensor as a 5-D map (64 d, T, d half, H, B) whose box
 // (64 x rows x 2 x heads x 1) lands in shared memory as [head][d half][rows][64 d]:
 // one TMA operation fills both 128-byte-swizzled d halves of `heads` heads.

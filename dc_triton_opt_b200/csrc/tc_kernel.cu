@@ -33,7 +33,9 @@
 
 namespace dcattn {
 namespace tc {
-template <typename E, int HPG, int R, int CS, int MAXT>
+// F8: q and k are e4m3 (8-bit float) with their scales folded into p.scale;
+// QK^T runs as kind::f8f6f4 MMAs, everything else is unchanged.
+template <typename E, int HPG, int R, int CS, int MAXT, bool F8 = false>
 __global__ void __launch_bounds__(MAXT, 1)
     dc_tc_kernel(const __grid_constant__ CUtensorMap tm_q, const __grid_constant__ CUtensorMap tm_k,
                  const __grid_constant__ CUtensorMap tm_v, const __grid_constant__ CUtensorMap tm_kl,
@@ -93,10 +95,16 @@ __global__ void __launch_bounds__(MAXT, 1)
       ptx::tma_prefetch_desc(&tm_k);
       ptx::tma_prefetch_desc(&tm_v);
       // Q for every head of the group: two 64-column halves of [BM x 64]
-      ptx::mbar_expect_tx(bar_q, NQ * 256);
-      for (int h = 0; h < HPG; ++h)
-        for (int c = 0; c < 2; ++c)
-          ptx::tma_load_4d(smem + geo.q_off + h * BM * 256 + c * BM * 128, &tm_q, bar_q, c * 64, hbase + h, q0, b);
+      if constexpr (F8) {  // one 128-byte row per query and head: [head][BM][128 d]
+        ptx::mbar_expect_tx(bar_q, NQ * 128);
+        for (int h = 0; h < HPG; ++h)
+          ptx::tma_load_4d(smem + geo.q_off + h * BM * 128, &tm_q, bar_q, 0, hbase + h, q0, b);
+      } else {
+        ptx::mbar_expect_tx(bar_q, NQ * 256);
+        for (int h = 0; h < HPG; ++h)
+          for (int c = 0; c < 2; ++c)
+            ptx::tma_load_4d(smem + geo.q_off + h * BM * 256 + c * BM * 128, &tm_q, bar_q, c * 64, hbase + h, q0, b);
+      }
       // jobs are key-tile major: job j -> key tile j / HPG, head j % HPG; K jobs then V jobs
       for (int j = 0; j < total; ++j) {
         const int slot = j % nslot, use = j / nslot;
@@ -109,10 +117,15 @@ __global__ void __launch_bounds__(MAXT, 1)
         const bool last = kt == nkt - 1;
         const CUtensorMap *m = isv ? (last ? &tm_vl : &tm_v) : (last ? &tm_kl : &tm_k);
         const int rows = last ? rlast : KT_ROWS;
-        ptx::mbar_expect_tx(bar_full + slot, rows * 256);
         unsigned char *dst = smem + geo.ring_off + slot * TILE_BYTES;
-        ptx::tma_load_4d(dst, m, bar_full + slot, 0, hbase + h, kb + kt * KT_ROWS, b);
-        ptx::tma_load_4d(dst + TILE_BYTES / 2, m, bar_full + slot, 64, hbase + h, kb + kt * KT_ROWS, b);
+        if (F8 && !isv) {  // an e4m3 K tile: one box of 128-byte rows
+          ptx::mbar_expect_tx(bar_full + slot, rows * 128);
+          ptx::tma_load_4d(dst, m, bar_full + slot, 0, hbase + h, kb + kt * KT_ROWS, b);
+        } else {
+          ptx::mbar_expect_tx(bar_full + slot, rows * 256);
+          ptx::tma_load_4d(dst, m, bar_full + slot, 0, hbase + h, kb + kt * KT_ROWS, b);
+          ptx::tma_load_4d(dst + TILE_BYTES / 2, m, bar_full + slot, 64, hbase + h, kb + kt * KT_ROWS, b);
+        }
       }
     }
     __syncwarp();
@@ -148,13 +161,23 @@ __global__ void __launch_bounds__(MAXT, 1)
       ptx::tc_fence_after();
       const int kt = j / HPG, h = j % HPG;
       const uint64_t ad = ptx::desc_add(kd0, slot * TILE_BYTES);
-      const uint64_t bd = ptx::desc_add(qd0, h * BM * 256);
       const uint32_t dd = tbase + kt * KT_ROWS + h * BM;
+      if constexpr (F8) {
+        // 32 e4m3 elements (32 bytes) per K step: four steps along one 128-byte row
+        const uint64_t bd = ptx::desc_add(qd0, h * BM * 128);
+        const uint32_t idesc_qk8 = ptx::idesc_f16(0, 0, 0, 128, BM);  // e4m3 x e4m3 -> f32
 #pragma unroll
-      for (int ks = 0; ks < D / 16; ++ks)
-        if (ptx::elect_one())
-          ptx::mma_f16_ss(dd, ptx::desc_add(ad, (ks >> 2) * (TILE_BYTES / 2) + (ks & 3) * 32),
-                          ptx::desc_add(bd, (ks >> 2) * (BM * 128) + (ks & 3) * 32), idesc_qk, ks > 0);
+        for (int ks = 0; ks < D / 32; ++ks)
+          if (ptx::elect_one())
+            ptx::mma_f8_ss(dd, ptx::desc_add(ad, ks * 32), ptx::desc_add(bd, ks * 32), idesc_qk8, ks > 0);
+      } else {
+        const uint64_t bd = ptx::desc_add(qd0, h * BM * 256);
+#pragma unroll
+        for (int ks = 0; ks < D / 16; ++ks)
+          if (ptx::elect_one())
+            ptx::mma_f16_ss(dd, ptx::desc_add(ad, (ks >> 2) * (TILE_BYTES / 2) + (ks & 3) * 32),
+                            ptx::desc_add(bd, (ks >> 2) * (BM * 128) + (ks & 3) * 32), idesc_qk, ks > 0);
+      }
       if (ptx::elect_one()) {
         ptx::mma_commit(bar_free + slot);
         if (h == HPG - 1) ptx::mma_commit(bar_S + kt);
@@ -1294,7 +1317,7 @@ __global__ void __launch_bounds__(32 * NW, 1)
 
 // ------------------------------------------------------------------ host side
 
-template <typename E, int HPG, int R>
+template <typename E, int HPG, int R, bool F8 = false>
 static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   constexpr int BM = NQ / HPG;
   const int nkt = num_key_tiles(HPG, p.window);
@@ -1303,10 +1326,14 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   const int rlast = last_tile_rows(HPG, p.window);
   const int64_t sb = (int64_t)p.T * p.H * D, st_ = (int64_t)p.H * D, sh = D;
   CUtensorMap mq, mk, mv, mkl, mvl, mo;
-  if (!make_map(&mq, p.q, p.dtype, p.B, p.T, p.H, BM, sb, st_, sh, true) ||
-      !make_map(&mk, p.k, p.dtype, p.B, p.T, p.H, KT_ROWS, sb, st_, sh, true) ||
+  const bool qk_ok = F8 ? (make_map8(&mq, p.q, p.B, p.T, p.H, BM, sb, st_, sh) &&
+                           make_map8(&mk, p.k, p.B, p.T, p.H, KT_ROWS, sb, st_, sh) &&
+                           make_map8(&mkl, p.k, p.B, p.T, p.H, rlast, sb, st_, sh))
+                        : (make_map(&mq, p.q, p.dtype, p.B, p.T, p.H, BM, sb, st_, sh, true) &&
+                           make_map(&mk, p.k, p.dtype, p.B, p.T, p.H, KT_ROWS, sb, st_, sh, true) &&
+                           make_map(&mkl, p.k, p.dtype, p.B, p.T, p.H, rlast, sb, st_, sh, true));
+  if (!qk_ok ||
       !make_map(&mv, p.v, p.dtype, p.B, p.T, p.H, KT_ROWS, sb, st_, sh, true) ||
-      !make_map(&mkl, p.k, p.dtype, p.B, p.T, p.H, rlast, sb, st_, sh, true) ||
       !make_map(&mvl, p.v, p.dtype, p.B, p.T, p.H, rlast, sb, st_, sh, true) ||
       !make_map(&mo, p.out, p.dtype, p.B, p.T, p.H, BM, p.out_sb, p.out_st, p.out_sh, false))
     return cudaErrorInvalidValue;
@@ -1323,7 +1350,7 @@ static cudaError_t launch_t(const dc_attn_params &p, cudaStream_t st) {
   tp.post = to_ptrs(p.post);
   // short windows (<= 2 key tiles): two warps per TMEM lane quarter and key tile
   const int cs = nkt <= 2 ? 2 : 1;
-  auto kern = cs == 2 ? dc_tc_kernel<E, HPG, R, 2, 576> : dc_tc_kernel<E, HPG, R, 1, 448>;
+  auto kern = cs == 2 ? dc_tc_kernel<E, HPG, R, 2, 576, F8> : dc_tc_kernel<E, HPG, R, 1, 448, F8>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   dim3 grid((p.T + BM - 1) / BM, p.B * p.G);
@@ -1405,6 +1432,18 @@ static cudaError_t launch_e(const dc_attn_params &p, cudaStream_t st) {
   return cudaErrorInvalidValue;
 }
 
+template <typename E>
+static cudaError_t launch_e8(const dc_attn_params &p, cudaStream_t st) {
+  const bool r2 = p.R > 1;
+  switch (p.H / p.G) {
+    case 1: return r2 ? launch_t<E, 1, 2, true>(p, st) : launch_t<E, 1, 1, true>(p, st);
+    case 2: return r2 ? launch_t<E, 2, 2, true>(p, st) : launch_t<E, 2, 1, true>(p, st);
+    case 4: return r2 ? launch_t<E, 4, 2, true>(p, st) : launch_t<E, 4, 1, true>(p, st);
+    case 8: return r2 ? launch_t<E, 8, 2, true>(p, st) : launch_t<E, 8, 1, true>(p, st);
+  }
+  return cudaErrorInvalidValue;
+}
+
 }  // namespace tc
 
 bool tc_supports(const dc_attn_params &p, std::string *why) {
@@ -1420,6 +1459,12 @@ bool tc_supports(const dc_attn_params &p, std::string *why) {
   if (!al(p.q) || !al(p.k) || !al(p.v) || !al(p.out)) return no("q, k, v, out must be 16-byte aligned");
   if (p.out_sb % 8 || p.out_st % 8 || p.out_sh % 8) return no("output strides must be multiples of 8 elements");
   return true;
+}
+
+// q and k in e4m3 (their scales already folded into p.scale), the rest in p.dtype
+cudaError_t launch_tc_fp8qk(const dc_attn_params &p, cudaStream_t st) {
+  if (p.dtype == DC_DTYPE_BF16) return tc::launch_e8<__nv_bfloat16>(p, st);
+  return tc::launch_e8<__half>(p, st);
 }
 
 cudaError_t launch_tc(const dc_attn_params &p, cudaStream_t st) {

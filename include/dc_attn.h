@@ -148,6 +148,17 @@ DC_API int dc_attn_fwd_residual(const void *q, const void *k, const void *v,
                          int32_t D, int32_t G, float scaling, int32_t window,
                          int32_t chunk_size, int32_t dtype, void *stream);
 
+/* Forward with q and k in 8-bit float (e4m3, one byte per element, [B,T,H,D]
+ * contiguous) and per-tensor scales: the logits are
+ * p->scale * q_scale * k_scale * (q8 . k8), with QK^T on the tensor cores in
+ * e4m3 (tcgen05 kind::f8f6f4) and fp32 accumulation.  v, out and every weight
+ * stay in p->dtype (bf16 / fp16), and so do the probabilities fed to P'V.
+ * Runs the single-pass tensor-core kernel: heads per group 1, 2, 4 or 8,
+ * D = 128, windows of at most three key tiles; other calls return
+ * DC_ERR_UNSUPPORTED.  The reference names fp8 only as a later experiment
+ * (fa3_dc_hopper_plan.md:113-116); no counterpart kernel. */
+DC_API int dc_attn_fwd_fp8qk(const dc_attn_params *p, float q_scale, float k_scale, void *stream);
+
 /* Packed variable-length batch: p->B must be 1 and p->T the total token count;
  * q, k, v, out and every per-token weight hold the sequences back to back,
  * sequence i being tokens [cu_seqlens[i], cu_seqlens[i+1]) (host array of

@@ -457,3 +457,25 @@ def test_varlen_matches_each_sequence(lens, H, G, R, window):
                                                                 for f in ("qw1", "qw2", "kw1", "kw2", "qdd", "kdd")})
         ref = O.dc_attn_oracle(q[:, a:b], k[:, a:b], v[:, a:b], cut(pre), cut(post), 128 ** -0.5, window, G, None)
         assert_close(got[a:b], ref[0], f"varlen seq {i} len {L}")
+
+
+# ---------------------------------------------------------------- fp8 (e4m3) q and k
+
+@pytest.mark.parametrize("G,R,window,T,B", [(8, 1, 128, 300, 1), (32, 2, 96, 200, 2), (4, 2, 256, 260, 1),
+                                             (16, 1, 128, 130, 1)])
+def test_fp8_qk_matches_oracle_on_dequantized_inputs(G, R, window, T, B):
+    """QK^T in e4m3 on the tensor cores: the result equals the oracle run on the
+    dequantized q and k (q8 * q_scale), under the usual tolerance."""
+    dt = torch.bfloat16
+    q, k, v, pre, post = O.make_inputs(B, T, 32, 128, G, R, seed=G + T + R)
+    v = rnd(v, dt)
+    pre, post = round_terms(pre, dt), round_terms(post, dt)
+    q8, qs = dc.quantize_e4m3(torch.from_numpy(q).to(DEV))
+    k8, ks = dc.quantize_e4m3(torch.from_numpy(k).to(DEV))
+    qd = (q8.float() * qs).cpu().numpy()
+    kd = (k8.float() * ks).cpu().numpy()
+    ref = O.dc_attn_oracle(qd, kd, v, pre, post, 128 ** -0.5, window, G, None)
+    got = dc.dc_attn_fwd_fp8qk(q8, k8, T_(v, dt), qs, ks, to_dcterms(pre, dt), to_dcterms(post, dt), 128 ** -0.5,
+                               window, G)
+    torch.cuda.synchronize()
+    assert_close(got.float().cpu().numpy(), ref, f"fp8 G{G} R{R} W{window} T{T}")
