@@ -147,6 +147,9 @@ def main(ref_dir: str):
     terms_case("terms_g2_r2", 1, 56, 8, 128, 2, 2, 20, [56], bf, 9)
     terms_case("terms_g1_r2", 1, 40, 8, 128, 1, 2, 16, [33], bf, 10)
 
+    # the BASELINE config-0 head layout (N=32, G=1: 32 heads per group, the
+    # tensor-core-mix kernel), seq_lens, a key span over two 64-key tiles
+    residual_case("residual_h32", "residual", 1, 80, 32, 128, 1, 64, 16, [70], 0.1, bf, 11)
     blob["cases"] = np.array(cases)
     np.savez_compressed(OUT, **blob)
     print(f"wrote {OUT} ({OUT.stat().st_size / 1e6:.2f} MB, {len(cases)} cases)")

@@ -479,3 +479,13 @@ def test_fp8_qk_matches_oracle_on_dequantized_inputs(G, R, window, T, B):
                                window, G)
     torch.cuda.synchronize()
     assert_close(got.float().cpu().numpy(), ref, f"fp8 G{G} R{R} W{window} T{T}")
+
+
+def test_golden_h32_case_runs_on_the_tensor_core_mix_kernel():
+    """The 32-heads-per-group golden case (made by the reference's own function)
+    pins the tensor-core-mix kernel directly: AUTO picks it for that shape."""
+    case = next(c for c in load_cases() if c.name == "residual_h32")
+    q = T_(case.q, torch.bfloat16)
+    ws = tuple(T_(w, torch.bfloat16) for w in case.ws)
+    assert dc.select_kernel(q, q, q, dc.DCTerms.residual(*ws[:3]), dc.DCTerms.residual(*ws[3:]),
+                            case.eff_window, 1) == "tcm"
