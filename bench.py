@@ -463,7 +463,7 @@ def projection_layer(local, steps=5, warmup=3, M=16 * 4096):
     torch.cuda.empty_cache()
     return {"M": M, "Dm": Dm, "I": I, "H": H, "R": R, "ms_per_call": ms, "tflops": fl / (ms * 1e-3) / 1e12,
             "tensor_frac": fl / (ms * 1e-3) / 1e12 / tc_peak, "hbm_gbs": by / (ms * 1e-3) / 1e9,
-            "kernel": "dc_proj_gemm (mma.sync), 3 launches (x W1, x Wdd, hidden W2)", "timing": f"CUDA events, {warmup} warm-up + {steps} calls"}
+            "kernel": "dc_proj_tc_gemm (tcgen05, TMA), 2 launches (x [W1 | Wdd], hidden W2)", "timing": f"CUDA events, {warmup} warm-up + {steps} calls"}
 
 
 def fp8_layer(local, steps=5, warmup=3):

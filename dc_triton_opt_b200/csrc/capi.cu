@@ -25,7 +25,7 @@ bool tcm_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_tcm(const dc_attn_params &p, cudaStream_t st);
 bool bwd_supports(const dc_attn_params &p, std::string *why);
 cudaError_t launch_bwd(const dc_attn_bwd_params &p, cudaStream_t st, std::string *why);
-cudaError_t launch_proj(const dc_proj_params &q, void *hidden, cudaStream_t st);
+cudaError_t launch_proj(const dc_proj_params &q, void *hidden, int32_t *err, cudaStream_t st);
 }  // namespace dcattn
 
 // The library's own device error word, used when a caller passes no
@@ -233,7 +233,9 @@ int dc_proj_weights_noalloc(const dc_proj_params *q, void *stream) {
   if ((rc = check_device()) != DC_OK) return rc;
   void *hidden = proj_hidden_addr();
   if (!hidden) return DC_ERR_DEVICE;
-  cudaError_t e = dcattn::launch_proj(*q, hidden, reinterpret_cast<cudaStream_t>(stream));
+  int32_t *ew = default_err_word();
+  if (!ew) return fail(DC_ERR_DEVICE, "cannot resolve the library's device error word");
+  cudaError_t e = dcattn::launch_proj(*q, hidden, ew, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DC_ERR_LAUNCH, "projection launch failed: %s", cudaGetErrorString(e));
   g_last_error.clear();
   return DC_OK;
@@ -245,7 +247,9 @@ int dc_proj_weights(const dc_proj_params *q, void *stream) {
   if (!q->hidden) return fail(DC_ERR_NULL, "hidden workspace is NULL");
   if (reinterpret_cast<uintptr_t>(q->hidden) & 15u) return fail(DC_ERR_ALIGN, "hidden must be 16-byte aligned");
   if ((rc = check_device()) != DC_OK) return rc;
-  cudaError_t e = dcattn::launch_proj(*q, q->hidden, reinterpret_cast<cudaStream_t>(stream));
+  int32_t *ew = default_err_word();
+  if (!ew) return fail(DC_ERR_DEVICE, "cannot resolve the library's device error word");
+  cudaError_t e = dcattn::launch_proj(*q, q->hidden, ew, reinterpret_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return fail(DC_ERR_LAUNCH, "projection launch failed: %s", cudaGetErrorString(e));
   g_last_error.clear();
   return DC_OK;

@@ -7,8 +7,10 @@
 //   dd     = tanh(x Wdd)  -> pre qdd | pre kdd | post qdd | post kdd   (H each)
 //   dw     = hidden W2    -> per set (pre, post): qw1 (H R) | qw2 (R H) | kw1 (H R) | kw2 (R H)
 //
-// Two launches of one GEMM kernel (x [W1 | Wdd] with a gelu / tanh epilogue,
-// then hidden W2).  Every output column range of a token is a contiguous run
+// x [W1 | Wdd] with a gelu / tanh epilogue, then hidden W2: on the tensor
+// cores through tcgen05 (below) when the shapes fit it (both weight matrices
+// of x a multiple of 64 columns, 256 at most together), else through the
+// warp-level mma.sync kernel (one launch per weight matrix).  Every output column range of a token is a contiguous run
 // in the layout the attention kernels read ([tok][H][R], [tok][R][H],
 // [tok][H]), so the epilogue writes each range straight to its tensor: no
 // concatenated output and no layout pass.  `hidden` is the only intermediate.
@@ -24,6 +26,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "tc_common.cuh"
 
 namespace dcattn {
 namespace proj {
@@ -43,6 +46,8 @@ struct Seg {
 struct GemmParams {
   int M, N, K;
   const void *A, *B;
+  const void *B2;  // tensor-core path only: columns [nb, N) come from B2 [K, N - nb]
+  int nb;
   int nseg;
   Seg seg[MAXSEG];
 };
@@ -164,34 +169,229 @@ static cudaError_t launch(const GemmParams &p, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------- tcgen05 GEMM
+// C[M, N] = A[M, K] [B1 | B2][K, N] for N <= 256: one CTA owns 128 rows and
+// every column, so x is read once for both weight matrices.  TMA loads A as
+// 128 x 64 K-major tiles and each B as 64 x 64 MN-major tiles (both 128-byte
+// swizzled) into a 4-stage ring; one thread issues M = 128, N = N MMAs into a
+// TMEM accumulator; four warps (one per TMEM lane quarter) apply the
+// activation, stage the tile in shared memory and write every segment with
+// coalesced 16-byte stores.  Every wait is bounded; a wait that runs out writes
+// a code to `err` and the CTA skips the rest of its work.
+constexpr int TC_STAGES = 4, TC_KC = 64, TC_ABYTES = 128 * TC_KC * 2, TC_BCHUNK = TC_KC * 64 * 2;
+constexpr int TC_SROW = 256 + 8;  // staging row (elements)
+
+struct TcGemm {
+  int M, N, K, nb;  // columns [0, nb) from B1, [nb, N) from B2
+  int nseg;
+  Seg seg[MAXSEG];
+  int32_t *err;
+  uint32_t wait_us;
+};
+
+template <typename E>
+__global__ void __launch_bounds__(192, 1)
+    dc_proj_tc_gemm(const __grid_constant__ CUtensorMap ma, const __grid_constant__ CUtensorMap mb1,
+                    const __grid_constant__ CUtensorMap mb2, const TcGemm p) {
+  extern __shared__ __align__(1024) unsigned char smem_raw[];
+  unsigned char *smem = reinterpret_cast<unsigned char *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                                          ~static_cast<uintptr_t>(1023));
+  const int nbc = p.N / 64;                           // 64-column B chunks
+  const int stage_bytes = TC_ABYTES + nbc * TC_BCHUNK;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + TC_STAGES * stage_bytes);
+  uint64_t *full = bars, *freeb = bars + TC_STAGES, *done = bars + 2 * TC_STAGES;
+  uint32_t *tslot = reinterpret_cast<uint32_t *>(done + 1);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int m0 = blockIdx.x * 128, nk = p.K / TC_KC;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < TC_STAGES; ++i) {
+      ptx::mbar_init(full + i, 1);
+      ptx::mbar_init(freeb + i, 1);
+    }
+    ptx::mbar_init(done, 1);
+    ptx::fence_mbar_init();
+  }
+  if (warp == 1) ptx::tmem_alloc(tslot, 256);
+  ptx::tc_fence_before();
+  __syncthreads();
+  ptx::tc_fence_after();
+  const uint32_t tbase = *tslot;
+  auto fail = [&](int code) { atomicCAS(p.err, 0, code); };
+
+  if (warp == 0) {
+    // one thread's TMA loads are processed one after another, so the loads of
+    // a stage go out from several lanes: lane 0 the A tile, lane 1 + c B chunk c
+    for (int kt = 0; kt < nk; ++kt) {
+      const int st = kt % TC_STAGES, use = kt / TC_STAGES;
+      bool ok = true;
+      if (lane == 0 && use > 0) ok = ptx::mbar_wait(freeb + st, (use - 1) & 1, p.wait_us);
+      if (!__shfl_sync(0xffffffffu, ok, 0)) {
+        if (lane == 0) fail(tc::ERR_TIMEOUT_FREE);
+        break;
+      }
+      unsigned char *dst = smem + st * stage_bytes;
+      if (lane == 0) ptx::mbar_expect_tx(full + st, stage_bytes);
+      __syncwarp();
+      if (lane == 0) {
+        ptx::tma_load_2d(dst, &ma, full + st, kt * TC_KC, m0);
+      } else if (lane <= nbc) {
+        const int c = lane - 1;
+        const bool first = c * 64 < p.nb;
+        ptx::tma_load_2d(dst + TC_ABYTES + c * TC_BCHUNK, first ? &mb1 : &mb2, full + st,
+                         first ? c * 64 : c * 64 - p.nb, kt * TC_KC);
+      }
+      __syncwarp();
+    }
+  } else if (warp == 1) {
+    const uint32_t ab = std::is_same<E, __nv_bfloat16>::value ? 1u : 0u;
+    const uint32_t idesc = ptx::idesc_f16(ab, 0, 1, 128, p.N);
+    const uint64_t ad0 = ptx::smem_desc(ptx::smem_u32(smem), 16, 1024, 2);
+    const uint64_t bd0 = ptx::smem_desc(ptx::smem_u32(smem + TC_ABYTES), TC_BCHUNK, 1024, 2);
+    bool ok = true;
+    for (int kt = 0; kt < nk && ok; ++kt) {
+      const int st = kt % TC_STAGES;
+      ok = __all_sync(0xffffffffu, ptx::mbar_wait(full + st, (kt / TC_STAGES) & 1, p.wait_us));
+      if (!ok) {
+        if (lane == 0) fail(tc::ERR_TIMEOUT_FULL);
+        break;
+      }
+      ptx::tc_fence_after();
+      const uint64_t ad = ptx::desc_add(ad0, st * stage_bytes), bd = ptx::desc_add(bd0, st * stage_bytes);
+#pragma unroll
+      for (int ks = 0; ks < TC_KC / 16; ++ks)
+        if (ptx::elect_one())
+          ptx::mma_f16_ss(tbase, ptx::desc_add(ad, ks * 32), ptx::desc_add(bd, ks * 2048), idesc, kt > 0 || ks > 0);
+      if (ptx::elect_one()) ptx::mma_commit(freeb + st);
+      __syncwarp();
+    }
+    if (ok && ptx::elect_one()) ptx::mma_commit(done);
+    __syncwarp();
+  } else {
+    // ---- epilogue: warps 2..5, lane quarter warp % 4 holds rows 32 q .. 32 q + 31
+    const int q = warp & 3, r = 32 * q + lane;
+    E *stage = reinterpret_cast<E *>(smem);  // the ring is idle once every MMA is done
+    const bool ok = ptx::mbar_wait(done, 0, p.wait_us);
+    if (!ok && lane == 0) fail(tc::ERR_TIMEOUT_O);
+    ptx::tc_fence_after();
+    if (__all_sync(0xffffffffu, ok)) {
+      for (int c0 = 0; c0 < p.N; c0 += 32) {
+        float v[32];
+        ptx::tmem_ld<32>(tbase + (static_cast<uint32_t>(32 * q) << 16) + c0, v);
+        ptx::tmem_wait_ld();
+        int si = 0;
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const int n = c0 + j;
+          while (si + 1 < p.nseg && n >= p.seg[si + 1].start) ++si;
+          float x = v[j];
+          if (p.seg[si].act == ACT_GELU) x = 0.5f * x * (1.f + erff(x * 0.70710678118654752f));
+          else if (p.seg[si].act == ACT_TANH) x = tanhf(x);
+          stage[r * TC_SROW + n] = from_f<E>(x);
+        }
+      }
+    }
+    ptx::named_bar_sync(1, 128);
+    if (ok) {
+      const int rows = min(128, p.M - m0), tid = threadIdx.x - 64;
+      for (int si = 0; si < p.nseg; ++si) {
+        const Seg &sg = p.seg[si];
+        E *dst = reinterpret_cast<E *>(sg.dst) + (int64_t)m0 * sg.len;
+        if (sg.len % 8 == 0) {
+          const int cpr = sg.len / 8;  // 16-byte chunks per row
+          for (int idx = tid; idx < rows * cpr; idx += 128) {
+            const int rr = idx / cpr, ch = idx % cpr;
+            *reinterpret_cast<uint4 *>(dst + (int64_t)rr * sg.len + ch * 8) =
+                *reinterpret_cast<const uint4 *>(stage + rr * TC_SROW + sg.start + ch * 8);
+          }
+        } else {
+          for (int idx = tid; idx < rows * sg.len; idx += 128)
+            dst[idx] = stage[(idx / sg.len) * TC_SROW + sg.start + idx % sg.len];
+        }
+      }
+    }
+  }
+  ptx::tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    ptx::tc_fence_after();
+    ptx::tmem_dealloc(tbase, 256);
+  }
+}
+
+// 2-D map of a row-major [rows, cols] 16-bit matrix, box {64 cols, box_rows}, 128-byte swizzle
+static bool map2d(CUtensorMap *m, const void *base, int dtype, int rows, int cols, int box_rows) {
+  tc::EncodeTiledFn enc = tc::get_encode();
+  if (!enc) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUtensorMapDataType dt =
+      dtype == DC_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  return enc(m, dt, 2, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+// the tensor-core GEMM runs when both B matrices have a multiple of 64 columns,
+// N <= 256 and K is a multiple of 64
+static bool tc_fits(int K, int n1, int n2) {
+  return K % TC_KC == 0 && n1 % 64 == 0 && n2 % 64 == 0 && n1 + n2 <= 256 && n1 + n2 >= 64;
+}
+
 }  // namespace proj
 
-cudaError_t launch_proj(const dc_proj_params &q, void *hidden, cudaStream_t st) {
+// The tcgen05 path for x [W1 | Wdd] and hidden W2 when their shapes fit it,
+// the mma.sync kernel otherwise.
+template <typename E>
+static cudaError_t launch_one(const proj::GemmParams &g, int dtype, int32_t *err, cudaStream_t st) {
   using namespace proj;
-  const int H = q.H, R = q.R, HR = q.H * q.R;
-  // x [W1 | Wdd]: W1 and Wdd are two row-major [Dm, *] matrices, so the first
-  // GEMM runs twice over x (once per matrix); both reads of x come from L2 for
-  // any practical M tile order.
-  GemmParams g1{};
-  g1.M = q.M; g1.N = q.I; g1.K = q.Dm; g1.A = q.x; g1.B = q.w1;
-  g1.nseg = 1;
+  const int n1 = g.B2 ? g.nb : g.N, n2 = g.N - n1;
+  if (!tc_fits(g.K, n1, n2)) return launch<E>(g, st);
+  CUtensorMap ma, mb1, mb2;
+  if (!map2d(&ma, g.A, dtype, g.M, g.K, 128) || !map2d(&mb1, g.B, dtype, g.K, n1, TC_KC) ||
+      !map2d(&mb2, g.B2 ? g.B2 : g.B, dtype, g.K, g.B2 ? n2 : n1, TC_KC))
+    return cudaErrorInvalidValue;
+  TcGemm t{};
+  t.M = g.M; t.N = g.N; t.K = g.K; t.nb = n1; t.nseg = g.nseg;
+  for (int i = 0; i < g.nseg; ++i) t.seg[i] = g.seg[i];
+  t.err = err;
+  t.wait_us = 2000000u;
+  const int smem = TC_STAGES * (TC_ABYTES + (g.N / 64) * TC_BCHUNK) + 8 * (2 * TC_STAGES + 2) + 1024;
+  auto kern = dc_proj_tc_gemm<E>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  kern<<<(g.M + 127) / 128, 192, smem, st>>>(ma, mb1, mb2, t);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_proj(const dc_proj_params &q, void *hidden, int32_t *err, cudaStream_t st) {
+  using namespace proj;
+  const int H = q.H, HR = q.H * q.R;
+  GemmParams g1{};  // x [W1 | Wdd]: gelu -> hidden, tanh -> the four gates
+  g1.M = q.M; g1.N = q.I + 4 * H; g1.K = q.Dm; g1.A = q.x; g1.B = q.w1; g1.B2 = q.wdd; g1.nb = q.I;
+  g1.nseg = 5;
   g1.seg[0] = {0, q.I, ACT_GELU, hidden};
-  GemmParams gd{};
-  gd.M = q.M; gd.N = 4 * H; gd.K = q.Dm; gd.A = q.x; gd.B = q.wdd;
-  gd.nseg = 4;
-  for (int i = 0; i < 4; ++i) gd.seg[i] = {i * H, H, ACT_TANH, q.dd[i]};
-  GemmParams g2{};
-  g2.M = q.M; g2.N = 8 * HR; g2.K = q.I; g2.A = hidden; g2.B = q.w2;
+  for (int i = 0; i < 4; ++i) g1.seg[1 + i] = {q.I + i * H, H, ACT_TANH, q.dd[i]};
+  GemmParams g2{};  // hidden W2 -> the eight rank-R weight tensors
+  g2.M = q.M; g2.N = 8 * HR; g2.K = q.I; g2.A = hidden; g2.B = q.w2; g2.nb = g2.N;
   g2.nseg = 8;
   for (int i = 0; i < 8; ++i) g2.seg[i] = {i * HR, HR, ACT_NONE, q.dw[i]};
-  (void)R;
-  cudaError_t e;
   const bool bf = q.dtype == DC_DTYPE_BF16;
-  for (const GemmParams *g : {&g1, &gd, &g2}) {
-    e = bf ? proj::launch<__nv_bfloat16>(*g, st) : proj::launch<__half>(*g, st);
-    if (e != cudaSuccess) return e;
+  const bool fused = tc_fits(q.Dm, q.I, 4 * H);
+  cudaError_t e;
+  if (fused) {
+    e = bf ? launch_one<__nv_bfloat16>(g1, q.dtype, err, st) : launch_one<__half>(g1, q.dtype, err, st);
+  } else {  // the mma.sync kernel reads one B matrix: two launches over x
+    GemmParams ga = g1, gd = g1;
+    ga.N = q.I; ga.B2 = nullptr; ga.nb = q.I; ga.nseg = 1;
+    gd.N = 4 * H; gd.B = q.wdd; gd.B2 = nullptr; gd.nb = 4 * H; gd.nseg = 4;
+    for (int i = 0; i < 4; ++i) gd.seg[i] = {i * H, H, ACT_TANH, q.dd[i]};
+    e = bf ? launch<__nv_bfloat16>(ga, st) : launch<__half>(ga, st);
+    if (e == cudaSuccess) e = bf ? launch<__nv_bfloat16>(gd, st) : launch<__half>(gd, st);
   }
-  return cudaSuccess;
+  if (e != cudaSuccess) return e;
+  return bf ? launch_one<__nv_bfloat16>(g2, q.dtype, err, st) : launch_one<__half>(g2, q.dtype, err, st);
 }
 
 }  // namespace dcattn

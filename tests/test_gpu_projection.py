@@ -32,7 +32,9 @@ def _inputs(lead, Dm, I, H, R, seed, dt):
 
 
 @pytest.mark.parametrize("lead,Dm,I,H,R,dtype", [
-    ((2, 100), 256, 64, 8, 1, torch.bfloat16),     # ragged M (200 tokens, not a tile multiple)
+    ((2, 100), 256, 64, 8, 1, torch.bfloat16),     # ragged M (200 tokens), mma.sync path (4H = 32)
+    ((2, 100), 256, 64, 16, 1, torch.bfloat16),    # ragged M, tcgen05 path for both GEMMs (N 128, 128)
+    ((1, 384), 512, 128, 32, 1, torch.float16),    # tcgen05 path, N 256 (x [W1 | Wdd]) and 256 (hidden W2)
     ((1, 300), 512, 128, 32, 2, torch.bfloat16),
     ((3, 64), 128, 32, 4, 2, torch.float16),
 ])
