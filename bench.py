@@ -608,7 +608,8 @@ def main():
     ap.add_argument("--no-extra", action="store_true",
                     help="skip the config-4 strong-scaling, repo-best and other-layer blocks")
     ap.add_argument("--op", default=None, choices=["backward", "projection"],
-                    help="run only this op a few times at a reduced size (B=2 / 8192 tokens), "
+                    help="run only this op a few times at a reduced size (B=2: 8192 tokens for the projection, "
+                         "--B sets it), "
                          "for profiling; prints its ms per call")
     args = ap.parse_args()
     if args.op is not None:
@@ -617,7 +618,7 @@ def main():
             WORKLOADS["config1"] = dict(WORKLOADS["config1"], B=2)
             print(json.dumps(backward_layer(0, steps=args.steps, warmup=args.warmup)))
         else:
-            print(json.dumps(projection_layer(0, steps=args.steps, warmup=args.warmup, M=8192)))
+            print(json.dumps(projection_layer(0, steps=args.steps, warmup=args.warmup, M=4096 * (args.B or 2))))
         return
     cfg = dict(WORKLOADS[args.workload])
     for k in ("G", "window", "B", "T"):
