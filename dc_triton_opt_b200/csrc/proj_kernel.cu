@@ -187,6 +187,8 @@ struct TcGemm {
   Seg seg[MAXSEG];
   int32_t *err;
   uint32_t wait_us;
+  int stages;      // ring depth (<= TC_STAGES; short K loops need fewer)
+  int ring_bytes;  // max(stages * stage bytes, epilogue staging)
 };
 
 template <typename E>
@@ -198,13 +200,14 @@ __global__ void __launch_bounds__(192, 1)
                                                           ~static_cast<uintptr_t>(1023));
   const int nbc = p.N / 64;                           // 64-column B chunks
   const int stage_bytes = TC_ABYTES + nbc * TC_BCHUNK;
-  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + TC_STAGES * stage_bytes);
-  uint64_t *full = bars, *freeb = bars + TC_STAGES, *done = bars + 2 * TC_STAGES;
+  const int NS = p.stages;
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + p.ring_bytes);
+  uint64_t *full = bars, *freeb = bars + NS, *done = bars + 2 * NS;
   uint32_t *tslot = reinterpret_cast<uint32_t *>(done + 1);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int m0 = blockIdx.x * 128, nk = p.K / TC_KC;
   if (threadIdx.x == 0) {
-    for (int i = 0; i < TC_STAGES; ++i) {
+    for (int i = 0; i < NS; ++i) {
       ptx::mbar_init(full + i, 1);
       ptx::mbar_init(freeb + i, 1);
     }
@@ -222,7 +225,7 @@ __global__ void __launch_bounds__(192, 1)
     // one thread's TMA loads are processed one after another, so the loads of
     // a stage go out from several lanes: lane 0 the A tile, lane 1 + c B chunk c
     for (int kt = 0; kt < nk; ++kt) {
-      const int st = kt % TC_STAGES, use = kt / TC_STAGES;
+      const int st = kt % NS, use = kt / NS;
       bool ok = true;
       if (lane == 0 && use > 0) ok = ptx::mbar_wait(freeb + st, (use - 1) & 1, p.wait_us);
       if (!__shfl_sync(0xffffffffu, ok, 0)) {
@@ -249,8 +252,8 @@ __global__ void __launch_bounds__(192, 1)
     const uint64_t bd0 = ptx::smem_desc(ptx::smem_u32(smem + TC_ABYTES), TC_BCHUNK, 1024, 2);
     bool ok = true;
     for (int kt = 0; kt < nk && ok; ++kt) {
-      const int st = kt % TC_STAGES;
-      ok = __all_sync(0xffffffffu, ptx::mbar_wait(full + st, (kt / TC_STAGES) & 1, p.wait_us));
+      const int st = kt % NS;
+      ok = __all_sync(0xffffffffu, ptx::mbar_wait(full + st, (kt / NS) & 1, p.wait_us));
       if (!ok) {
         if (lane == 0) fail(tc::ERR_TIMEOUT_FULL);
         break;
@@ -357,7 +360,12 @@ static cudaError_t launch_one(const proj::GemmParams &g, int dtype, int32_t *err
   for (int i = 0; i < g.nseg; ++i) t.seg[i] = g.seg[i];
   t.err = err;
   t.wait_us = 2000000u;
-  const int smem = TC_STAGES * (TC_ABYTES + (g.N / 64) * TC_BCHUNK) + 8 * (2 * TC_STAGES + 2) + 1024;
+  // a ring no deeper than the K loop: a short one (hidden W2, K = 128) then
+  // fits two CTAs per SM
+  t.stages = g.K / TC_KC < TC_STAGES ? g.K / TC_KC : TC_STAGES;
+  const int sb = TC_ABYTES + (g.N / 64) * TC_BCHUNK, staging = 128 * TC_SROW * 2;
+  t.ring_bytes = t.stages * sb > staging ? t.stages * sb : (staging + 1023) / 1024 * 1024;
+  const int smem = t.ring_bytes + 8 * (2 * t.stages + 2) + 1024;
   auto kern = dc_proj_tc_gemm<E>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
