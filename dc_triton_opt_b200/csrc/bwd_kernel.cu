@@ -74,9 +74,13 @@ __host__ __device__ inline Geo make_geo(int BM, int W, int esize) {
   // (the pad rows are zeroed once and never written)
   g.q_off = o; o += (rup(g.NC, 16) + 16) * DP * esize;   // q rows
   g.do_off = o; o += (rup(g.NC, 16) + 16) * DP * esize;  // dO rows
-  g.kv_off = o; o += (rup(g.span, 16) + 16) * DP * esize;  // one head's K or V rows of the span
+  // one head's K or V rows of the span; dM (the mixing-matrix gradient of one
+  // set) shares this region: it is live only between the head loops, while
+  // no K or V rows are staged
+  const int kv_bytes = (rup(g.span, 16) + 16) * DP * esize, dm_bytes = BM * HPG * HPG * 4;
+  g.kv_off = o; o += kv_bytes > dm_bytes ? kv_bytes : dm_bytes;
   o = rup(o, 16);
-  g.m_off = o; o += 3 * BM * HPG * HPG * 4;              // Mpre, Mpost, dM
+  g.m_off = o; o += 2 * BM * HPG * HPG * 4;              // Mpre, Mpost
   g.rec_off = o; o += 2 * 2 * BM * HPG * R * 4;          // [set][qw1 | qw2][BM][HPG * R]
   g.total = o;
   return g;
@@ -166,7 +170,8 @@ __global__ void __launch_bounds__(NT, 1) dc_bwd_kernel(const BwdParams p, const 
   E *dOs = reinterpret_cast<E *>(smem + geo.do_off);
   E *KVs = reinterpret_cast<E *>(smem + geo.kv_off);
   float *Mpre = reinterpret_cast<float *>(smem + geo.m_off);
-  float *Mpost = Mpre + BM * HPG * HPG, *dM = Mpost + BM * HPG * HPG;
+  float *Mpost = Mpre + BM * HPG * HPG;
+  float *dM = reinterpret_cast<float *>(smem + geo.kv_off);
   float *rec = reinterpret_cast<float *>(smem + geo.rec_off);
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -239,11 +244,13 @@ __global__ void __launch_bounds__(NT, 1) dc_bwd_kernel(const BwdParams p, const 
   }
 
   // ---- rows x staged K/V rows of one head: out[(h, i)][j] = f * sum_d A[(h, i)][d] KV[j][d]
+  // (the pad rows after the span are rewritten with zeros every time: the
+  // region also holds dM between the head loops)
   auto stage = [&](const E *src, int h) {
-    for (int idx = tid; idx < span * (D / 8); idx += NT) {
+    for (int idx = tid; idx < (rup(span, 16) + 16) * (D / 8); idx += NT) {
       const int j = idx / (D / 8), ch = idx % (D / 8), s = k_lo + j;
       uint4 u = make_uint4(0, 0, 0, 0);
-      if (s >= 0 && s < T) u = *reinterpret_cast<const uint4 *>(src + row(s, h) + ch * 8);
+      if (j < span && s >= 0 && s < T) u = *reinterpret_cast<const uint4 *>(src + row(s, h) + ch * 8);
       *reinterpret_cast<uint4 *>(KVs + j * DP + ch * 8) = u;
     }
   };
