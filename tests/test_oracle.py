@@ -126,3 +126,55 @@ def test_backward_oracle_matches_reference_autograd(case):
     for k, ref in case.grads.items():
         scale = max(float(np.abs(ref).max()), 1e-6)
         np.testing.assert_allclose(got[k], ref, rtol=0, atol=2e-5 * max(1.0, scale), err_msg=k)
+
+
+def _tiny_grad_case(seed=0):
+    B, T, H, D, G, R = 1, 12, 4, 8, 2, 2
+    q, k, v, pre, post = O.make_inputs(B, T, H, D, G, R, seed=seed, terms=("w", "qw", "qdd"))
+    rng = np.random.default_rng(seed + 1)
+    for t in (pre, post):
+        t.qmat = (0.1 * rng.standard_normal((B, T, H, H // G))).astype(np.float64)
+    dout = rng.standard_normal(q.shape)
+    return q, k, v, pre, post, dout, G
+
+
+def test_backward_oracle_matches_finite_differences():
+    """The float64 autograd gradients of the terms the reference cannot pin
+    (static mix w, rank-2 factors, qmat) against central finite differences."""
+    from oracle.dc_oracle_torch import _forward
+    import torch
+    q, k, v, pre, post, dout, G = _tiny_grad_case()
+    scale, W = 8 ** -0.5, 5
+    g = dc_attn_torch_grads(q, k, v, pre, post, scale, W, G, None, dout)
+
+    def loss():
+        out = _forward(q, k, v, pre, post, scale, W, G, None, 256, None, torch.float64)
+        return float((out.numpy() * dout).sum())
+
+    rng = np.random.default_rng(3)
+    for name, tm in (("pre", pre), ("post", post)):
+        for n in ("w", "qw1", "qw2", "qdd", "qmat"):
+            a = getattr(tm, n).astype(np.float64)
+            setattr(tm, n, a)
+            for _ in range(3):
+                idx = tuple(rng.integers(0, s) for s in a.shape)
+                old = a[idx]
+                a[idx] = old + 1e-5
+                lp = loss()
+                a[idx] = old - 1e-5
+                lm = loss()
+                a[idx] = old
+                fd = (lp - lm) / 2e-5
+                assert abs(fd - g[f"{name}_{n}"][idx]) <= 1e-6 + 1e-5 * abs(fd), (name, n, idx, fd)
+
+
+def test_backward_oracle_static_mix_grad_is_sum_of_qmat_grads():
+    """M_t = w + qmat_t^T inside a group, so dL/dw[g, h', h] equals the sum over
+    tokens of dL/dqmat[b, t, g*HPG + h, h']."""
+    q, k, v, pre, post, dout, G = _tiny_grad_case(seed=5)
+    g = dc_attn_torch_grads(q, k, v, pre, post, 8 ** -0.5, 5, G, None, dout)
+    hpg = q.shape[2] // G
+    for name in ("pre", "post"):
+        dq = g[f"{name}_qmat"].sum(axis=(0, 1))            # [H, HPG]: (h, h')
+        want = dq.reshape(G, hpg, hpg).transpose(0, 2, 1)   # [G, h', h]
+        np.testing.assert_allclose(g[f"{name}_w"], want, atol=1e-10, rtol=1e-8)
